@@ -1,0 +1,604 @@
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+
+#include "common.h"
+#include "kernels.h"
+
+namespace defer {
+
+bool use_persistent() {
+  const char* e = getenv("DEFER_B200_PHASED");
+  return !(e && e[0] == '1');
+}
+
+static uint64_t words_per_sample(float t) { return t == 0.0f ? 0 : 1; }
+
+// ------------------------------------------------------------------ Runner
+Runner::Runner(const Model* m, int B, int max_cap) : m_(m), B_(B), max_cap_(max_cap) {
+  if (B <= 0) fail(kInvalidArgument, "batch size must be positive");
+  DEFER_CUDA(cudaSetDevice(m->device));
+  const DModel& d = m->dm;
+  max_chunks_ = (max_cap + kAttnChunk - 1) / kAttnChunk;
+  if (max_chunks_ < 1) max_chunks_ = 1;
+  DEFER_CUDA(cudaMalloc(&x_, (size_t)B * d.H * 4));
+  DEFER_CUDA(cudaMalloc(&xn_, (size_t)B * d.H * 4));
+  DEFER_CUDA(cudaMalloc(&q_, (size_t)B * d.QD * 4));
+  DEFER_CUDA(cudaMalloc(&att_, (size_t)B * d.QD * 4));
+  DEFER_CUDA(cudaMalloc(&g_, (size_t)B * d.FF * 4));
+  DEFER_CUDA(cudaMalloc(&logits_, (size_t)B * d.V * 4));
+  DEFER_CUDA(cudaMalloc(&part_, (size_t)B * d.NH * max_chunks_ * (d.HD + 2) * 4));
+  DEFER_CUDA(cudaMalloc(&d_sess_, sizeof(DSession) * B));
+  DEFER_CUDA(cudaMalloc(&d_state_, sizeof(DSlotState) * B));
+  DEFER_CUDA(cudaMalloc(&d_ctrl_, 8 * sizeof(int)));
+}
+
+Runner::~Runner() {
+  cudaFree(x_);
+  cudaFree(xn_);
+  cudaFree(q_);
+  cudaFree(att_);
+  cudaFree(g_);
+  cudaFree(logits_);
+  cudaFree(part_);
+  cudaFree(d_sess_);
+  cudaFree(d_state_);
+  cudaFree(d_ctrl_);
+  if (d_scratch_) cudaFree(d_scratch_);
+}
+
+const float* Runner::logits(int b) const { return logits_ + (size_t)b * m_->dm.V; }
+
+void Runner::download_logits(int b, float* out) const {
+  DEFER_CUDA(cudaMemcpy(out, logits(b), (size_t)m_->dm.V * 4, cudaMemcpyDeviceToHost));
+}
+
+void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& results) {
+  const int n = (int)progs.size();
+  if (n > B_) fail(kInvalidArgument, "more programs than runner slots");
+  results.assign(n, SlotResult());
+  if (n == 0) return;
+  DEFER_CUDA(cudaSetDevice(m_->device));
+  cudaStream_t st = m_->stream;
+  // Pack tokens / words / stop lists / margins into one device scratch.
+  std::vector<size_t> o_tok(n), o_words(n), o_stop(n), o_marg(n);
+  size_t total = 0;
+  int nsteps = 0;
+  for (int b = 0; b < n; b++) {
+    SlotProgram& p = progs[b];
+    if (!p.cache || p.cache->model != m_) fail(kInvalidArgument, "program without a cache of this model");
+    if (p.cache->cap > max_cap_) fail(kInvalidArgument, "cache larger than the runner supports");
+    const int ngen = (int)p.tokens.size() - p.n_prompt;
+    if (ngen < 0) fail(kInvalidArgument, "n_prompt exceeds program length");
+    if (p.temperature != 0.0f && (int)p.words.size() < ngen) fail(kInvalidArgument, "missing PRNG words");
+    o_tok[b] = total;
+    total += p.tokens.size();
+    o_words[b] = total;
+    total += p.temperature != 0.0f ? (size_t)ngen : 0;
+    o_stop[b] = total;
+    total += p.stop.size();
+    o_marg[b] = total;
+    total += p.want_margins ? (size_t)ngen : 0;
+    nsteps = std::max(nsteps, (int)p.tokens.size());
+  }
+  if (total > scratch_words_ || !d_scratch_) {
+    if (d_scratch_) cudaFree(d_scratch_);
+    scratch_words_ = std::max<size_t>(total, 4096);
+    DEFER_CUDA(cudaMalloc(&d_scratch_, scratch_words_ * 4));
+  }
+  std::vector<uint32_t> hs(std::max<size_t>(total, 1));
+  std::vector<DSession> sess(n);
+  std::vector<DSlotState> state(n);
+  for (int b = 0; b < n; b++) {
+    SlotProgram& p = progs[b];
+    const int ngen = (int)p.tokens.size() - p.n_prompt;
+    std::copy(p.tokens.begin(), p.tokens.end(), hs.begin() + o_tok[b]);
+    if (p.temperature != 0.0f) std::copy(p.words.begin(), p.words.begin() + ngen, hs.begin() + o_words[b]);
+    std::copy(p.stop.begin(), p.stop.end(), hs.begin() + o_stop[b]);
+    DSession& s = sess[b];
+    s.kc = p.cache->k;
+    s.vc = p.cache->v;
+    s.mask = p.masked ? p.cache->mask : nullptr;
+    s.tokens = d_scratch_ + o_tok[b];
+    s.words = d_scratch_ + o_words[b];
+    s.margins = p.want_margins ? reinterpret_cast<float*>(d_scratch_ + o_marg[b]) : nullptr;
+    s.stop = d_scratch_ + o_stop[b];
+    s.n_stop = (int)p.stop.size();
+    s.cap = p.cache->cap;
+    s.pos = (int)p.cache->len;
+    s.n_prompt = p.n_prompt;
+    s.n_total = (int)p.tokens.size();
+    s.temperature = p.temperature;
+    s.verify = p.verify ? 1 : 0;
+    DSlotState& z = state[b];
+    memset(&z, 0, sizeof(z));
+    z.pos = (int)p.cache->len;
+    z.done = p.tokens.empty() ? 1 : 0;
+    z.div_step = -1;
+  }
+  DEFER_CUDA(cudaMemcpyAsync(d_scratch_, hs.data(), total * 4, cudaMemcpyHostToDevice, st));
+  DEFER_CUDA(cudaMemcpyAsync(d_sess_, sess.data(), sizeof(DSession) * n, cudaMemcpyHostToDevice, st));
+  DEFER_CUDA(cudaMemcpyAsync(d_state_, state.data(), sizeof(DSlotState) * n, cudaMemcpyHostToDevice, st));
+  DEFER_CUDA(cudaMemsetAsync(d_ctrl_, 0, 8 * sizeof(int), st));
+
+  DBatch bt;
+  bt.B = n;
+  bt.sess = d_sess_;
+  bt.st = d_state_;
+  bt.x = x_;
+  bt.xn = xn_;
+  bt.q = q_;
+  bt.att = att_;
+  bt.g = g_;
+  bt.logits = logits_;
+  bt.part = part_;
+  bt.max_chunks = max_chunks_;
+  bt.status = d_ctrl_;
+  bt.any_active = d_ctrl_ + 1;
+  bt.bar = reinterpret_cast<unsigned*>(d_ctrl_ + 3);
+  last_steps_ = nsteps;
+  if (use_persistent()) launch_steps_persistent(m_->dm, bt, nsteps, m_->sms, st);
+  else launch_steps_phased(m_->dm, m_->host_layers.data(), bt, 0, nsteps, m_->sms, st);
+  DEFER_CUDA(cudaGetLastError());
+
+  int ctrl[8];
+  DEFER_CUDA(cudaMemcpyAsync(state.data(), d_state_, sizeof(DSlotState) * n, cudaMemcpyDeviceToHost, st));
+  DEFER_CUDA(cudaMemcpyAsync(ctrl, d_ctrl_, sizeof(ctrl), cudaMemcpyDeviceToHost, st));
+  DEFER_CUDA(cudaMemcpyAsync(hs.data(), d_scratch_, total * 4, cudaMemcpyDeviceToHost, st));
+  DEFER_CUDA(cudaStreamSynchronize(st));
+  for (int b = 0; b < n; b++) {
+    SlotProgram& p = progs[b];
+    const int ngen = (int)p.tokens.size() - p.n_prompt;
+    SlotResult& r = results[b];
+    r.steps = state[b].step;
+    r.div_step = state[b].div_step;
+    r.div_token = state[b].div_token;
+    r.tokens.assign(hs.begin() + o_tok[b], hs.begin() + o_tok[b] + p.tokens.size());
+    if (p.want_margins)
+      r.margins.assign(reinterpret_cast<float*>(hs.data() + o_marg[b]),
+                       reinterpret_cast<float*>(hs.data() + o_marg[b]) + ngen);
+    p.cache->len = (size_t)state[b].pos;
+  }
+  if (ctrl[0] == kStTimeout) fail(kDeviceTimeout, "a grid barrier of the token loop timed out");
+  if (ctrl[0] == kStBadToken) fail(kModel, "token id out of range");
+  if (ctrl[0] == kStContext) fail(kModel, "context length " + std::to_string(m_->cfg.max_seq_len) + " exceeded");
+}
+
+// ----------------------------------------------------------------- Session
+Session::Session(const Model* m, const uint8_t seed[32], float t, int cache_cap)
+    : model(m), temperature(t), rng_(seed) {
+  if (!(t >= 0.0f && std::isfinite(t))) fail(kModel, "temperature must be finite and >= 0");
+  memcpy(base_seed, seed, 32);
+  int cap = cache_cap > 0 ? cache_cap : (int)m->cfg.max_seq_len;
+  cache = cache_new(m, cap);
+  runner_.reset(new Runner(m, 1, cap));
+}
+
+Session::~Session() { delete cache; }
+
+// Feeds tokens in order; stops at the first token the reference would
+// reject (model.rs:417-422) and raises its error after feeding the rest.
+void Session::feed_tokens(const uint32_t* t, size_t n) {
+  size_t ok = 0;
+  std::string err;
+  for (; ok < n; ok++) {
+    if (t[ok] >= model->cfg.vocab_size) {
+      err = "token id " + std::to_string(t[ok]) + " out of range";
+      break;
+    }
+    if (cache->len + ok >= model->cfg.max_seq_len) {
+      err = "context length " + std::to_string(model->cfg.max_seq_len) + " exceeded";
+      break;
+    }
+    if (cache->len + ok >= (size_t)cache->cap) {
+      err = "cache capacity " + std::to_string(cache->cap) + " exceeded";
+      break;
+    }
+  }
+  if (ok) {
+    std::vector<SlotProgram> progs(1);
+    progs[0].cache = cache;
+    progs[0].tokens.assign(t, t + ok);
+    progs[0].n_prompt = (int)ok;
+    std::vector<SlotResult> res;
+    runner_->run(progs, res);
+    history.insert(history.end(), t, t + ok);
+    has_logits_ = true;
+  }
+  if (!err.empty()) fail(kModel, err);
+}
+
+void Session::prompt(const uint32_t* tokens, size_t n) {
+  if (history.size() != prompt_len) fail(kModel, "cannot add prompt tokens after generation started");
+  feed_tokens(tokens, n);
+  prompt_len = history.size();
+}
+
+void Session::refeed_last() {
+  uint32_t last = history.back();
+  history.pop_back();
+  cache->len -= 1;
+  feed_tokens(&last, 1);
+}
+
+std::vector<uint32_t> Session::generate(size_t max_tokens, const std::vector<uint32_t>& stop,
+                                        const std::function<int(uint32_t, uint64_t)>& on_token) {
+  std::vector<uint32_t> out;
+  if (max_tokens == 0) return out;
+  if (!has_logits_) fail(kModel, "no context: provide a non-empty prompt");
+  const size_t limit = std::min<size_t>(model->cfg.max_seq_len, cache->cap);
+  const size_t room = cache->len < limit ? limit - cache->len : 0;
+  const size_t n = std::min(max_tokens, room);
+  const uint64_t wps = words_per_sample(temperature);
+  const size_t len0 = history.size();
+  const uint64_t rng0 = rng_.word_pos();
+  if (n) {
+    std::vector<SlotProgram> progs(1);
+    SlotProgram& p = progs[0];
+    p.cache = cache;
+    p.tokens.assign(n, 0);
+    p.n_prompt = 0;
+    p.temperature = temperature;
+    if (wps) {
+      p.words.resize(n);
+      rng_.words(rng0, n, p.words.data());
+    }
+    p.stop = stop;
+    p.want_margins = true;
+    std::vector<SlotResult> res;
+    runner_->run(progs, res);
+    last_margins = res[0].margins;
+    const int k = res[0].steps;
+    for (int i = 0; i < k; i++) {
+      const uint32_t t = res[0].tokens[i];
+      history.push_back(t);
+      rng_.set_word_pos(rng0 + (uint64_t)(i + 1) * wps);
+      out.push_back(t);
+      int rc = on_token ? on_token(t, rng_.word_pos()) : 0;
+      if (rc != 0) {
+        // The device ran ahead: roll the cache back to this token and
+        // recompute its logits (same arithmetic, same bits).
+        if (i + 1 < k) {
+          cache->len = len0 + i + 1;
+          refeed_last();
+        }
+        fail((Status)rc, "token callback failed");
+      }
+    }
+    const bool stopped = !out.empty() && std::find(stop.begin(), stop.end(), out.back()) != stop.end();
+    if (stopped || (size_t)k < n) return out;
+  }
+  if (n < max_tokens) {
+    // The next step samples (one word) and then fails to feed (model.rs:420-422).
+    rng_.set_word_pos(rng_.word_pos() + wps);
+    fail(kModel, "context length " + std::to_string(model->cfg.max_seq_len) + " exceeded");
+  }
+  return out;
+}
+
+uint32_t Session::step() {
+  std::vector<uint32_t> none;
+  std::vector<uint32_t> r = generate(1, none, nullptr);
+  return r.at(0);
+}
+
+Checkpoint Session::checkpoint() const {
+  Checkpoint c;
+  memcpy(c.model_signature, model->signature, 32);
+  memcpy(c.base_seed, base_seed, 32);
+  c.temperature = temperature;
+  c.history_tokens = history;
+  c.prompt_len = (uint32_t)prompt_len;
+  c.rng_word_pos = U128{rng_.word_pos(), 0};
+  return c;
+}
+
+void Session::last_logits(float* out) const {
+  if (!has_logits_) fail(kModel, "no logits yet");
+  runner_->download_logits(0, out);
+}
+
+static void validate_checkpoint(const Model* m, const Checkpoint& ck) {
+  if (memcmp(ck.model_signature, m->signature, 32) != 0)
+    fail(kCheckpoint, "model signature mismatch: checkpoint " + to_hex(ck.model_signature, 32) + " vs loaded " +
+                          to_hex(m->signature, 32));
+  const size_t plen = ck.prompt_len;
+  if (plen > ck.history_tokens.size()) fail(kCheckpoint, "prompt_len exceeds history");
+  const uint64_t expected = (uint64_t)(ck.history_tokens.size() - plen) * words_per_sample(ck.temperature);
+  if (ck.rng_word_pos.hi != 0 || ck.rng_word_pos.lo != expected)
+    fail(kCheckpoint, "rng_word_pos " + std::to_string(ck.rng_word_pos.lo) + " inconsistent with " +
+                          std::to_string(ck.history_tokens.size() - plen) + " sampled tokens (expected " +
+                          std::to_string(expected) + ")");
+}
+
+static SlotProgram replay_program(const Checkpoint& ck, KvCache* cache) {
+  SlotProgram p;
+  p.cache = cache;
+  p.tokens = ck.history_tokens;
+  p.n_prompt = (int)ck.prompt_len;
+  p.temperature = ck.temperature;
+  p.verify = true;
+  const size_t ngen = ck.history_tokens.size() - ck.prompt_len;
+  if (words_per_sample(ck.temperature) && ngen) {
+    ChaCha8 r(ck.base_seed);
+    p.words.resize(ngen);
+    r.words(0, ngen, p.words.data());
+  }
+  return p;
+}
+
+Session* Session::checkout(const Model* m, const Checkpoint& ck, int cache_cap) {
+  validate_checkpoint(m, ck);
+  std::unique_ptr<Session> s(new Session(m, ck.base_seed, ck.temperature, cache_cap));
+  const size_t n = ck.history_tokens.size();
+  for (size_t i = 0; i < n; i++)
+    if (ck.history_tokens[i] >= m->cfg.vocab_size) s->feed_tokens(ck.history_tokens.data(), i + 1);  // raises
+  if (n > std::min<size_t>(m->cfg.max_seq_len, s->cache->cap)) s->feed_tokens(ck.history_tokens.data(), n);  // raises
+  if (n) {
+    std::vector<SlotProgram> progs(1, replay_program(ck, s->cache));
+    progs[0].want_margins = true;
+    std::vector<SlotResult> res;
+    s->runner_->run(progs, res);
+    s->last_margins = res[0].margins;
+    const SlotResult& r = res[0];
+    if (r.div_step >= 0)
+      fail(kDivergence, "replay sampled token " + std::to_string(r.div_token) + " at position " +
+                            std::to_string(r.div_step) + ", checkpoint recorded " +
+                            std::to_string(ck.history_tokens[r.div_step]));
+    s->history = ck.history_tokens;
+    s->has_logits_ = true;
+  }
+  s->prompt_len = ck.prompt_len;
+  s->rng_.set_word_pos((uint64_t)(n - ck.prompt_len) * words_per_sample(ck.temperature));
+  return s.release();
+}
+
+// ----------------------------------------------------------- model forward
+static void free_forward_runner(void* p) { delete static_cast<Runner*>(p); }
+
+void model_forward(Model* m, KvCache* c, uint32_t token, const size_t* masked, size_t n_masked, float* logits_out) {
+  if (c->model != m) fail(kInvalidArgument, "cache belongs to another model");
+  if (token >= m->cfg.vocab_size) fail(kModel, "token id " + std::to_string(token) + " out of range");
+  if (c->len >= m->cfg.max_seq_len) fail(kModel, "context length " + std::to_string(m->cfg.max_seq_len) + " exceeded");
+  if (c->len >= (size_t)c->cap) fail(kModel, "cache capacity " + std::to_string(c->cap) + " exceeded");
+  // The model owns one single-slot runner for this entry point.
+  const int want = std::max<int>(c->cap, (int)m->cfg.max_seq_len);
+  if (!m->fwd_runner || m->fwd_runner_cap < want) {
+    if (m->fwd_runner) m->fwd_runner_free(m->fwd_runner);
+    m->fwd_runner = nullptr;
+    m->fwd_runner = new Runner(m, 1, want);
+    m->fwd_runner_free = free_forward_runner;
+    m->fwd_runner_cap = want;
+  }
+  Runner* fr = static_cast<Runner*>(m->fwd_runner);
+  std::vector<uint32_t> bits;
+  bool any = false;
+  if (n_masked) {
+    bits.assign((size_t)c->cap / 32 + 1, 0);
+    for (size_t i = 0; i < n_masked; i++)
+      if (masked[i] < c->len) {
+        bits[masked[i] >> 5] |= 1u << (masked[i] & 31);
+        any = true;
+      }
+  }
+  std::vector<SlotProgram> progs(1);
+  progs[0].cache = c;
+  progs[0].tokens = {token};
+  progs[0].n_prompt = 1;
+  progs[0].masked = any;
+  if (any) DEFER_CUDA(cudaMemcpy(c->mask, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice));
+  std::vector<SlotResult> res;
+  fr->run(progs, res);
+  if (any) DEFER_CUDA(cudaMemset(c->mask, 0, bits.size() * 4));
+  if (logits_out) fr->download_logits(0, logits_out);
+}
+
+// ----------------------------------------------------------- batch drivers
+double log_softmax_at(const float* logits, size_t n, size_t idx) {
+  double mx = -INFINITY;
+  for (size_t i = 0; i < n; i++)
+    if ((double)logits[i] > mx) mx = (double)logits[i];
+  double sum = 0.0;
+  for (size_t i = 0; i < n; i++)
+    if (!std::isnan(logits[i])) sum += exp((double)logits[i] - mx);
+  return ((double)logits[idx] - mx) - log(sum);
+}
+
+namespace {
+struct EventPair {
+  cudaEvent_t a = nullptr, b = nullptr;
+  EventPair() {
+    DEFER_CUDA(cudaEventCreate(&a));
+    DEFER_CUDA(cudaEventCreate(&b));
+  }
+  ~EventPair() {
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+  }
+};
+}  // namespace
+
+void replay_batch(Model* m, const std::vector<Checkpoint>& cks, int batch, bool fingerprints,
+                  std::vector<ReplayOutcome>& out, double* device_ms) {
+  out.assign(cks.size(), ReplayOutcome());
+  if (device_ms) *device_ms = 0.0;
+  std::vector<size_t> todo;
+  int cap = 1;
+  for (size_t i = 0; i < cks.size(); i++) {
+    try {
+      validate_checkpoint(m, cks[i]);
+      for (uint32_t t : cks[i].history_tokens)
+        if (t >= m->cfg.vocab_size) fail(kModel, "token id " + std::to_string(t) + " out of range");
+      if (cks[i].history_tokens.size() > m->cfg.max_seq_len)
+        fail(kModel, "context length " + std::to_string(m->cfg.max_seq_len) + " exceeded");
+      todo.push_back(i);
+      cap = std::max<int>(cap, (int)cks[i].history_tokens.size());
+    } catch (const Error& e) {
+      out[i].status = e.status;
+      out[i].message = e.what();
+    }
+  }
+  if (todo.empty()) return;
+  if (batch <= 0) batch = 1;
+  batch = std::min<int>(batch, (int)todo.size());
+  Runner runner(m, batch, cap);
+  std::vector<std::unique_ptr<KvCache>> caches;
+  for (int b = 0; b < batch; b++) caches.emplace_back(cache_new(m, cap));
+  EventPair ev;
+  float total_ms = 0.0f;
+  for (size_t w = 0; w < todo.size(); w += batch) {
+    const size_t nw = std::min<size_t>(batch, todo.size() - w);
+    std::vector<SlotProgram> progs;
+    for (size_t b = 0; b < nw; b++) {
+      caches[b]->len = 0;
+      progs.push_back(replay_program(cks[todo[w + b]], caches[b].get()));
+    }
+    std::vector<SlotResult> res;
+    DEFER_CUDA(cudaEventRecord(ev.a, m->stream));
+    runner.run(progs, res);
+    DEFER_CUDA(cudaEventRecord(ev.b, m->stream));
+    DEFER_CUDA(cudaEventSynchronize(ev.b));
+    float ms = 0.0f;
+    DEFER_CUDA(cudaEventElapsedTime(&ms, ev.a, ev.b));
+    total_ms += ms;
+    for (size_t b = 0; b < nw; b++) {
+      ReplayOutcome& o = out[todo[w + b]];
+      const Checkpoint& ck = cks[todo[w + b]];
+      if (res[b].div_step >= 0) {
+        o.status = kDivergence;
+        o.div_step = res[b].div_step;
+        o.div_token = res[b].div_token;
+        o.message = "replay sampled token " + std::to_string(res[b].div_token) + " at position " +
+                    std::to_string(res[b].div_step) + ", checkpoint recorded " +
+                    std::to_string(ck.history_tokens[res[b].div_step]);
+      } else if (fingerprints) {
+        cache_fingerprint(caches[b].get(), o.fingerprint);
+      }
+    }
+  }
+  if (device_ms) *device_ms = total_ms;
+}
+
+void generate_batch(Model* m, const std::vector<GenRequest>& reqs, int batch, std::vector<std::vector<uint32_t>>& out,
+                    double* device_ms) {
+  out.assign(reqs.size(), {});
+  if (device_ms) *device_ms = 0.0;
+  int cap = 1;
+  for (auto& r : reqs) {
+    if (r.prompt.empty()) fail(kModel, "no context: provide a non-empty prompt");
+    for (uint32_t t : r.prompt)
+      if (t >= m->cfg.vocab_size) fail(kModel, "token id " + std::to_string(t) + " out of range");
+    if (r.prompt.size() + r.max_tokens > m->cfg.max_seq_len)
+      fail(kModel, "context length " + std::to_string(m->cfg.max_seq_len) + " exceeded");
+    if (!(r.temperature >= 0.0f && std::isfinite(r.temperature))) fail(kModel, "temperature must be finite and >= 0");
+    cap = std::max<int>(cap, (int)(r.prompt.size() + r.max_tokens));
+  }
+  if (reqs.empty()) return;
+  if (batch <= 0) batch = 1;
+  batch = std::min<int>(batch, (int)reqs.size());
+  Runner runner(m, batch, cap);
+  std::vector<std::unique_ptr<KvCache>> caches;
+  for (int b = 0; b < batch; b++) caches.emplace_back(cache_new(m, cap));
+  EventPair ev;
+  float total_ms = 0.0f;
+  for (size_t w = 0; w < reqs.size(); w += batch) {
+    const size_t nw = std::min<size_t>(batch, reqs.size() - w);
+    std::vector<SlotProgram> progs;
+    for (size_t b = 0; b < nw; b++) {
+      const GenRequest& r = reqs[w + b];
+      caches[b]->len = 0;
+      SlotProgram p;
+      p.cache = caches[b].get();
+      p.tokens = r.prompt;
+      p.tokens.resize(r.prompt.size() + r.max_tokens, 0);
+      p.n_prompt = (int)r.prompt.size();
+      p.temperature = r.temperature;
+      if (r.temperature != 0.0f && r.max_tokens) {
+        ChaCha8 c(r.seed);
+        p.words.resize(r.max_tokens);
+        c.words(0, r.max_tokens, p.words.data());
+      }
+      progs.push_back(std::move(p));
+    }
+    std::vector<SlotResult> res;
+    DEFER_CUDA(cudaEventRecord(ev.a, m->stream));
+    runner.run(progs, res);
+    DEFER_CUDA(cudaEventRecord(ev.b, m->stream));
+    DEFER_CUDA(cudaEventSynchronize(ev.b));
+    float ms = 0.0f;
+    DEFER_CUDA(cudaEventElapsedTime(&ms, ev.a, ev.b));
+    total_ms += ms;
+    for (size_t b = 0; b < nw; b++) {
+      const size_t np = reqs[w + b].prompt.size();
+      const size_t end = std::max<size_t>(np, (size_t)res[b].steps);
+      out[w + b].assign(res[b].tokens.begin() + np, res[b].tokens.begin() + end);
+    }
+  }
+  if (device_ms) *device_ms = total_ms;
+}
+
+void ablation_batch(Model* m, const uint32_t* context, size_t n, uint32_t target, const size_t* positions,
+                    size_t n_pos, int batch, double* base_logprob, double* ablated) {
+  if (n == 0) fail(kModel, "cannot ablate an empty context");
+  if (target >= m->cfg.vocab_size) fail(kModel, "target token " + std::to_string(target) + " out of range");
+  for (size_t i = 0; i < n_pos; i++)
+    if (positions[i] + 1 >= n)
+      fail(kModel, "position " + std::to_string(positions[i]) + " can not be ablated (must be < " +
+                       std::to_string(n - 1) + "; the query token itself is excluded)");
+  for (size_t i = 0; i < n; i++)
+    if (context[i] >= m->cfg.vocab_size) fail(kModel, "token id " + std::to_string(context[i]) + " out of range");
+  if (n > m->cfg.max_seq_len) fail(kModel, "context length " + std::to_string(m->cfg.max_seq_len) + " exceeded");
+  const int cap = (int)n;
+  std::unique_ptr<KvCache> full(cache_new(m, cap));
+  std::vector<float> logits(m->cfg.vocab_size);
+  {
+    Runner r1(m, 1, cap);
+    std::vector<SlotProgram> progs(1);
+    progs[0].cache = full.get();
+    progs[0].tokens.assign(context, context + n);
+    progs[0].n_prompt = (int)n;
+    std::vector<SlotResult> res;
+    r1.run(progs, res);
+    r1.download_logits(0, logits.data());
+    *base_logprob = log_softmax_at(logits.data(), logits.size(), target);
+  }
+  if (n_pos == 0) return;
+  if (batch <= 0) batch = 1;
+  batch = std::min<int>(batch, (int)n_pos);
+  Runner runner(m, batch, cap);
+  std::vector<std::unique_ptr<KvCache>> caches;
+  for (int b = 0; b < batch; b++) caches.emplace_back(cache_new(m, cap));
+  const size_t words = (size_t)cap / 32 + 1;
+  for (size_t w = 0; w < n_pos; w += batch) {
+    const size_t nw = std::min<size_t>(batch, n_pos - w);
+    std::vector<SlotProgram> progs;
+    std::vector<std::vector<uint32_t>> bits(nw);
+    for (size_t b = 0; b < nw; b++) {
+      const size_t p = positions[w + b];
+      KvCache* c = caches[b].get();
+      cache_copy_prefix(c, full.get(), p + 1, m->stream);
+      c->len = p + 1;
+      bits[b].assign(words, 0);
+      bits[b][p >> 5] |= 1u << (p & 31);
+      DEFER_CUDA(cudaMemcpyAsync(c->mask, bits[b].data(), words * 4, cudaMemcpyHostToDevice, m->stream));
+      SlotProgram prog;
+      prog.cache = c;
+      prog.tokens.assign(context + p + 1, context + n);
+      prog.n_prompt = (int)prog.tokens.size();
+      prog.masked = true;
+      progs.push_back(std::move(prog));
+    }
+    std::vector<SlotResult> res;
+    runner.run(progs, res);
+    for (size_t b = 0; b < nw; b++) {
+      runner.download_logits((int)b, logits.data());
+      ablated[w + b] = log_softmax_at(logits.data(), logits.size(), target);
+      DEFER_CUDA(cudaMemset(caches[b]->mask, 0, words * 4));
+    }
+  }
+}
+
+}  // namespace defer

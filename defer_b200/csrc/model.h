@@ -37,6 +37,10 @@ struct Model {
   DLayer* d_layers = nullptr;
   std::vector<float> inv_freq;
   cudaStream_t stream = nullptr;
+  // Single-slot runner of the Model::forward entry point (owned).
+  void* fwd_runner = nullptr;
+  void (*fwd_runner_free)(void*) = nullptr;
+  int fwd_runner_cap = 0;
   ~Model();
 };
 
