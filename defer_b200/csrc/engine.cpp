@@ -312,6 +312,9 @@ static void validate_checkpoint(const Model* m, const Checkpoint& ck) {
     fail(kCheckpoint, "rng_word_pos " + std::to_string(ck.rng_word_pos.lo) + " inconsistent with " +
                           std::to_string(ck.history_tokens.size() - plen) + " sampled tokens (expected " +
                           std::to_string(expected) + ")");
+  // Replay samples the first generated token from the prompt's logits
+  // (engine.rs:104-110 fails without them).
+  if (plen == 0 && !ck.history_tokens.empty()) fail(kModel, "no context: provide a non-empty prompt");
 }
 
 static SlotProgram replay_program(const Checkpoint& ck, KvCache* cache) {
