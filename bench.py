@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 token loop on the reference's headline workload.
+
+Workload: SmolLM2-135M-shape Llama, random-init
+fp32 weights N(0, 0.02) from seed 0; one session per GPU at temperature
+0.7 with ChaCha8 seed 42 (+ rank); a 32-token uniform-random prompt; decode
+to a 2048-token context while appending every token to a WAL on the host;
+then a verified checkout (replay with Divergence checks) of that WAL.
+
+One step = that whole session loop: 32 prompt + 2016 generated + 2048
+replayed = 4096 single-token forward passes (each with its sampler step).
+
+  value : tokens per second of the step on the device (CUDA events recorded
+          on the engine's stream around every token-loop launch; weights and
+          caches resident in HBM), summed over ranks, time = max over ranks.
+  e2e   : the same tokens per wall-clock second through the public API with
+          host buffers (prompt / WAL / checkpoint bytes in, tokens out),
+          including every host<->device copy and the WAL file writes.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MODEL = "smollm2-135m"
+PROMPT_LEN = 32
+CONTEXT = 2048
+TEMPERATURE = 0.7
+SEED = 42
+FALLBACK_HBM_GBS = 6650.0
+WORKLOAD = ("config2: SmolLM2-135M-shape fp32 Llama (synthetic N(0,0.02) seed 0), T=0.7, ChaCha8 seed 42+rank, "
+            "32-token prompt -> 2048-token context with a host WAL, then verified WAL replay; "
+            "1 session per GPU")
+
+
+def model_dir() -> str:
+    return os.environ.get("DEFER_BENCH_DIR", os.path.join(tempfile.gettempdir(), "defer_bench"))
+
+
+def prompt_tokens(vocab: int):
+    import numpy as np
+    return [int(t) for t in np.random.default_rng(2).integers(0, vocab, PROMPT_LEN)]
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_per_token():
+    """DRAM bytes per token of the token-loop kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    try:
+        d = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        return d.get(MODEL)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+class Clocks:
+    """Samples nvidia-smi every 200 ms while the timed region runs."""
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = os.path.join(tempfile.gettempdir(), f"defer_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.device), "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().splitlines()]
+        except OSError:
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 8:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[4:8]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------- CPU baseline
+def _cpu_session_worker(args):
+    """Oracle session (the reference's CPU path restated in C) on one core:
+    32-token prompt, then `gen` sampled tokens; returns (forwards, seconds)."""
+    path, gen, seed, core = args
+    if core is not None:
+        try:
+            os.sched_setaffinity(0, {core})
+        except OSError:
+            pass
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    m = O.Model.load(path)
+    prompt = prompt_tokens(m.config.vocab_size)
+    t0 = time.perf_counter()
+    s = O.Session(m, O.seed_from_u64(seed), TEMPERATURE, cache_cap=PROMPT_LEN + gen + 1)
+    s.prompt(prompt)
+    s.generate(gen)
+    return PROMPT_LEN + gen, time.perf_counter() - t0
+
+
+def cpu_model_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_baseline(path: str, gen: int, workers: int):
+    ctx = mp.get_context("spawn")
+    cores = sorted(os.sched_getaffinity(0))[:workers]
+    with ctx.Pool(len(cores)) as pool:
+        res = pool.map(_cpu_session_worker, [(path, gen, SEED + i, c) for i, c in enumerate(cores)])
+    toks = sum(r[0] for r in res)
+    secs = max(r[1] for r in res)
+    return toks / secs, len(cores), toks, secs
+
+
+# ------------------------------------------------------------------- arms
+def run_reference(args):
+    """The reference's CPU implementation of the path (the oracle port; the
+    Rust crate cannot be built here) timed on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from defer_b200 import synthetic
+    path = synthetic.model_path(MODEL, model_dir(), 0)
+    workers = min(8, len(os.sched_getaffinity(0)))
+    gen = args.ref_gen
+    for _ in range(args.warmup):
+        cpu_baseline(path, 4, workers)
+    vals, toks, secs = [], 0, 0.0
+    for _ in range(args.steps):
+        v, cores, t, s = cpu_baseline(path, gen, workers)
+        vals.append(v)
+        toks += t
+        secs += s
+    value = toks / secs
+    sample = (f"per step: {cores} independent oracle sessions (one per core, single-threaded like the reference), "
+              f"each the first {PROMPT_LEN}+{gen} forwards of the workload (prompt + sampled decode); "
+              f"CPU: {cpu_model_name()}")
+    line = {"impl": "reference", "metric": "decode tok/s (single-session token loop)", "value": value,
+            "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * secs / max(args.steps, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / 17.0, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "cpu_sample": sample},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def session_step(D, m, prompt, seed_bytes, wal_path):
+    """One step through the public API: prompt, generate to CONTEXT with a
+    host WAL, then checkout from the WAL bytes. Returns (tokens, h2d, d2h)."""
+    s = D.Session(m, seed_bytes, TEMPERATURE)
+    s.prompt(prompt)
+    hdr = D.WalHeader(m.signature, seed_bytes, TEMPERATURE, len(prompt), 0, prompt)
+    w = D.WalWriter.create(wal_path, hdr)
+    gen = CONTEXT - len(prompt)
+    out = s.generate(gen, on_token=lambda sess, t: w.append(t, sess.rng_word_pos()))
+    w.close()
+    ck = D.WalLog.read(wal_path).to_checkpoint()
+    r = D.Session.checkout(m, ck)
+    assert r.history() == s.history() and len(out) == gen
+    tokens = len(prompt) + gen + CONTEXT
+    # host->device: program tokens + PRNG words of each run; device->host:
+    # tokens, margins and slot state read back after each run
+    h2d = 4 * (len(prompt) + 2 * gen + CONTEXT + gen)
+    d2h = 4 * (len(prompt) + 2 * gen + CONTEXT + 2 * gen)
+    return tokens, h2d, d2h
+
+
+def run_b200(args):
+    import numpy as np  # noqa: F401
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist = tdist
+
+    import defer_b200 as D
+    from defer_b200 import synthetic
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    if rank == 0:
+        path = synthetic.model_path(MODEL, model_dir(), 0)
+    barrier()
+    path = synthetic.model_path(MODEL, model_dir(), 0)
+
+    # CPU baseline first (spawned pool, before this process touches the GPU)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, toks, secs = cpu_baseline(path, args.cpu_gen, 1)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"{toks} forwards of the workload's first steps ({PROMPT_LEN}-token prompt + "
+                         f"{args.cpu_gen} sampled tokens) by the single-threaded oracle port pinned to one core, "
+                         f"{secs:.1f} s; CPU: {cpu_model_name()}"}
+
+    m = D.Model.load(path, device=local)
+    prompt = prompt_tokens(m.config.vocab_size)
+    seed_bytes = D.seed_from_u64(SEED + rank)
+    wal = os.path.join(tempfile.gettempdir(), f"defer_bench_{os.getpid()}.wal")
+    for _ in range(args.warmup):
+        session_step(D, m, prompt, seed_bytes, wal)
+
+    barrier()
+    m.timing(reset=True)
+    with Clocks(local) as clk:
+        barrier()
+        t0 = time.perf_counter()
+        tokens = h2d = d2h = 0
+        for _ in range(args.steps):
+            t, a, b = session_step(D, m, prompt, seed_bytes, wal)
+            tokens += t
+            h2d += a
+            d2h += b
+        wall = time.perf_counter() - t0
+        barrier()
+    tm = m.timing(reset=True)
+    clocks = clk.summary()
+    try:
+        os.unlink(wal)
+    except OSError:
+        pass
+
+    dev_s = max_over_ranks(tm["device_ms"] / 1e3)
+    wall_s = max_over_ranks(wall)
+    all_tokens = sum_over_ranks(tokens)
+    value = all_tokens / dev_s
+    e2e = all_tokens / wall_s
+    peak, peak_kind = peaks()
+    runs = max(tm["runs"], 1)
+    achieved = tm["hbm_bytes"] / (tm["device_ms"] / 1e3) / 1e9
+    tpt = traffic_per_token()
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_kind": peak_kind, "kernel": "k_persistent (token loop)",
+                "bytes_per_launch": tm["hbm_bytes"] / runs,
+                "traffic": (tpt * tokens / runs) if tpt else None,
+                "launch_ms": tm["device_ms"] / runs}
+    if rank == 0:
+        line = {"metric": "decode tok/s (single-session token loop)", "value": value, "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1000.0 * dev_s / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": value / world / 17.0, "dtype": "fp32", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "tokens_per_step_per_gpu": tokens // max(args.steps, 1),
+                           "l2": "weights 538 MB per token > 126 MB L2: inputs larger than L2, no flush",
+                           "parallelism": f"{world} independent sessions (one per GPU), no collective"},
+                "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d // max(args.steps, 1),
+                        "d2h_bytes_per_step": d2h // max(args.steps, 1)},
+                "gpu_launches": tm["launches"], "clocks": clocks,
+                "device": {"tokens": tokens, "device_ms": tm["device_ms"], "runs": tm["runs"]}}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-gen", type=int, default=150, help="sampled tokens of the CPU baseline sample")
+    ap.add_argument("--ref-gen", type=int, default=48, help="sampled tokens per reference-arm step")
+    ap.add_argument("--no-cpu", action="store_true")
+    a = ap.parse_args(argv)
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_b200(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -192,6 +192,18 @@ class Model:
     def forward(self, token: int, cache: "KvCache"):
         return self.forward_ext(token, cache, ())
 
+    def timing(self, reset: bool = False) -> dict:
+        """Totals of the token-loop runs since the last reset: device_ms
+        (CUDA events on the model's stream), runs, launches, tokens and
+        algorithmic hbm_bytes."""
+        ms = ctypes.c_double(0)
+        b = ctypes.c_double(0)
+        r, l, t = ctypes.c_uint64(0), ctypes.c_uint64(0), ctypes.c_uint64(0)
+        _check(_L().defer_model_timing(self._h, ctypes.byref(ms), ctypes.byref(r), ctypes.byref(l), ctypes.byref(t),
+                                       ctypes.byref(b), 1 if reset else 0))
+        return {"device_ms": ms.value, "runs": r.value, "launches": l.value, "tokens": t.value,
+                "hbm_bytes": b.value}
+
 
 class KvCache:
     """KvCache (src/model.rs:184-243) in HBM."""

@@ -98,6 +98,9 @@ SIGNATURES = [
     ("defer_generate_batch", ctypes.c_int, [vp, ctypes.POINTER(c_u32p), c_szp, c_u8p, c_f32p, c_szp, sz,
                                             ctypes.c_int, ctypes.POINTER(c_u32p), c_szp, c_f64p]),
     ("defer_ablation", ctypes.c_int, [vp, c_u32p, sz, ctypes.c_uint32, c_szp, sz, ctypes.c_int, c_f64p, c_f64p]),
+    ("defer_model_timing", ctypes.c_int, [vp, c_f64p, ctypes.POINTER(ctypes.c_uint64),
+                                          ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), c_f64p,
+                                          ctypes.c_int]),
     ("defer_log_softmax_at", ctypes.c_double, [c_f32p, sz, sz]),
 ]
 

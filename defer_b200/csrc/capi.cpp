@@ -546,6 +546,24 @@ int defer_ablation(defer_model* m, const uint32_t* context, size_t n, uint32_t t
   });
 }
 
+int defer_model_timing(defer_model* m, double* device_ms, uint64_t* runs, uint64_t* launches, uint64_t* tokens,
+                       double* hbm_bytes, int reset) {
+  return guard([&] {
+    need(m, "model");
+    const defer::Model& M = *m->m;
+    if (device_ms) *device_ms = M.t_device_ms;
+    if (runs) *runs = M.t_runs;
+    if (launches) *launches = M.t_launches;
+    if (tokens) *tokens = M.t_tokens;
+    if (hbm_bytes) *hbm_bytes = M.t_bytes;
+    if (reset) {
+      M.t_device_ms = 0.0;
+      M.t_runs = M.t_launches = M.t_tokens = 0;
+      M.t_bytes = 0.0;
+    }
+  });
+}
+
 double defer_log_softmax_at(const float* logits, size_t n, size_t idx) {
   return defer::log_softmax_at(logits, n, idx);
 }

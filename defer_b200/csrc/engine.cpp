@@ -34,6 +34,8 @@ Runner::Runner(const Model* m, int B, int max_cap) : m_(m), B_(B), max_cap_(max_
   DEFER_CUDA(cudaMalloc(&d_sess_, sizeof(DSession) * B));
   DEFER_CUDA(cudaMalloc(&d_state_, sizeof(DSlotState) * B));
   DEFER_CUDA(cudaMalloc(&d_ctrl_, 8 * sizeof(int)));
+  DEFER_CUDA(cudaEventCreate(&ev_start_));
+  DEFER_CUDA(cudaEventCreate(&ev_stop_));
 }
 
 Runner::~Runner() {
@@ -48,6 +50,8 @@ Runner::~Runner() {
   cudaFree(d_state_);
   cudaFree(d_ctrl_);
   if (d_scratch_) cudaFree(d_scratch_);
+  if (ev_start_) cudaEventDestroy(ev_start_);
+  if (ev_stop_) cudaEventDestroy(ev_stop_);
 }
 
 const float* Runner::logits(int b) const { return logits_ + (size_t)b * m_->dm.V; }
@@ -140,9 +144,12 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   bt.any_active = d_ctrl_ + 1;
   bt.bar = reinterpret_cast<unsigned*>(d_ctrl_ + 3);
   last_steps_ = nsteps;
-  if (use_persistent()) launch_steps_persistent(m_->dm, bt, nsteps, m_->sms, st);
+  const bool persistent = use_persistent();
+  DEFER_CUDA(cudaEventRecord(ev_start_, st));
+  if (persistent) launch_steps_persistent(m_->dm, bt, nsteps, m_->sms, st);
   else launch_steps_phased(m_->dm, m_->host_layers.data(), bt, 0, nsteps, m_->sms, st);
   DEFER_CUDA(cudaGetLastError());
+  DEFER_CUDA(cudaEventRecord(ev_stop_, st));
 
   int ctrl[8];
   DEFER_CUDA(cudaMemcpyAsync(state.data(), d_state_, sizeof(DSlotState) * n, cudaMemcpyDeviceToHost, st));
@@ -162,6 +169,28 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
                        reinterpret_cast<float*>(hs.data() + o_marg[b]) + ngen);
     p.cache->len = (size_t)state[b].pos;
   }
+  // Timing and algorithmic traffic of this run.
+  float ms = 0.0f;
+  DEFER_CUDA(cudaEventElapsedTime(&ms, ev_start_, ev_stop_));
+  const DModel& d = m_->dm;
+  const double kv_row = 2.0 * d.L * d.KVD * 4.0;  // K and V of one position, all layers
+  int steps_run = 0;
+  double bytes = 0.0;
+  uint64_t tokens = 0;
+  for (int b = 0; b < n; b++) {
+    const int k = results[b].steps;
+    const double p0 = (double)sess[b].pos;
+    steps_run = std::max(steps_run, k);
+    tokens += (uint64_t)k;
+    // step i reads positions 0..p0+i and writes position p0+i
+    bytes += kv_row * ((double)k * (p0 + 1.0) + (double)k * (k - 1) / 2.0 + (double)k);
+  }
+  bytes += (double)steps_run * (double)m_->weight_bytes;
+  m_->t_device_ms += ms;
+  m_->t_runs += 1;
+  m_->t_launches += persistent ? 1 : (uint64_t)nsteps * (4 + 8 * (uint64_t)d.L) + 1;
+  m_->t_tokens += tokens;
+  m_->t_bytes += bytes;
   if (ctrl[0] == kStTimeout) fail(kDeviceTimeout, "a grid barrier of the token loop timed out");
   if (ctrl[0] == kStBadToken) fail(kModel, "token id out of range");
   if (ctrl[0] == kStContext) fail(kModel, "context length " + std::to_string(m_->cfg.max_seq_len) + " exceeded");

@@ -59,6 +59,7 @@ class Runner {
   uint32_t* d_scratch_ = nullptr;
   size_t scratch_words_ = 0;
   int last_steps_ = 0;
+  cudaEvent_t ev_start_ = nullptr, ev_stop_ = nullptr;
 };
 
 // Whether runs use the persistent kernel (default) or one launch per phase

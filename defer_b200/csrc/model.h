@@ -41,6 +41,13 @@ struct Model {
   void* fwd_runner = nullptr;
   void (*fwd_runner_free)(void*) = nullptr;
   int fwd_runner_cap = 0;
+  // Accumulated by every token-loop run on this model (see defer_model_timing):
+  // device time between events recorded on `stream` around the launch, runs,
+  // kernel launches, tokens fed, and algorithmic HBM bytes (weights once per
+  // step + KV entries read and written).
+  mutable double t_device_ms = 0.0;
+  mutable uint64_t t_runs = 0, t_launches = 0, t_tokens = 0;
+  mutable double t_bytes = 0.0;
   ~Model();
 };
 

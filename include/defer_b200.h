@@ -186,6 +186,15 @@ DEFER_API int defer_generate_batch(defer_model* m, const uint32_t* const* prompt
 DEFER_API int defer_ablation(defer_model* m, const uint32_t* context, size_t n, uint32_t target,
                              const size_t* positions, size_t n_pos, int batch, double* base_logprob,
                              double* ablated_logprobs);
+/* Instrumentation (no counterpart in the reference, which only prints tok/s
+ * at src/main.rs:303-313): totals over every token-loop run of this model
+ * since the last reset — device milliseconds between CUDA events recorded
+ * on the model's stream around each launch, runs, kernel launches, tokens
+ * fed, and algorithmic HBM bytes (weights once per step plus KV read and
+ * written). Any pointer may be NULL; reset != 0 zeroes the totals after
+ * reading them. */
+DEFER_API int defer_model_timing(defer_model* m, double* device_ms, uint64_t* runs, uint64_t* launches,
+                                 uint64_t* tokens, double* hbm_bytes, int reset);
 /* attribution::log_softmax_at (src/attribution.rs:71-85). */
 DEFER_API double defer_log_softmax_at(const float* logits, size_t n, size_t idx);
 
