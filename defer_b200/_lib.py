@@ -56,6 +56,8 @@ SIGNATURES = [
     ("defer_model_signature", ctypes.c_int, [vp, c_u8p]),
     ("defer_model_eos_tokens", ctypes.c_int, [vp, c_u32p, sz, c_szp]),
     ("defer_forward", ctypes.c_int, [vp, vp, ctypes.c_uint32, c_szp, sz, c_f32p]),
+    ("defer_forward_noalloc", ctypes.c_int, [vp, vp, vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, vp,
+                                             vp]),
     ("defer_cache_new", ctypes.c_int, [vp, ctypes.c_uint32, ctypes.POINTER(vp)]),
     ("defer_cache_free", None, [vp]),
     ("defer_cache_len", sz, [vp]),

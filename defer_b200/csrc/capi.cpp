@@ -141,6 +141,15 @@ int defer_forward(defer_model* m, defer_cache* c, uint32_t token, const size_t* 
   });
 }
 
+int defer_forward_noalloc(defer_model* m, float* k_cache, float* v_cache, uint32_t cap, uint32_t pos,
+                          uint32_t token, float* logits_out, void* stream) {
+  return guard([&] {
+    need(m, "model");
+    defer::forward_noalloc(m->m.get(), k_cache, v_cache, cap, pos, token, logits_out,
+                           static_cast<cudaStream_t>(stream));
+  });
+}
+
 int defer_cache_new(defer_model* m, uint32_t cap, defer_cache** out) {
   return guard([&] {
     need(m, "model");

@@ -130,4 +130,10 @@ void ablation_batch(Model* m, const uint32_t* context, size_t n, uint32_t target
 
 double log_softmax_at(const float* logits, size_t n, size_t idx);  // attribution.rs:71-85
 
+// One forward step whose scratch lives in a fixed device array instead of
+// allocated buffers (csrc/noalloc.cu); the caller owns the KV cache and the
+// logits buffer.
+void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uint32_t pos, uint32_t token,
+                     float* logits_out, cudaStream_t st);
+
 }  // namespace defer

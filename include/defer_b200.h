@@ -65,6 +65,28 @@ DEFER_API int defer_model_eos_tokens(const defer_model* m, uint32_t* out, size_t
 DEFER_API int defer_forward(defer_model* m, defer_cache* c, uint32_t token, const size_t* masked, size_t n_masked,
                             float* logits_out);
 
+/* Allocation-free forward step. No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory while they run — e.g. a
+ * server whose memory pool already holds all free HBM, or a latency-bound
+ * loop that must not enter the driver's allocator — and therefore cannot
+ * use defer_forward, whose first call on a model allocates its scratch.
+ * Same arithmetic and result as defer_forward on a cache of `cap`
+ * positions, with the caller's buffers: k_cache and v_cache each hold
+ * num_layers * num_kv_heads * cap * head_dim floats laid out
+ * [layer][kv_head][position][dim], positions < pos filled by earlier calls;
+ * position `pos` is written; logits_out receives vocab_size floats. All
+ * three are device pointers. `stream` is a cudaStream_t (NULL = legacy
+ * default stream); the call returns after the step has finished.
+ * Limits: the step's scratch lives in one 4 MiB array inside this library
+ * (held by every GPU that loads it until the process exits); a model/cap
+ * whose scratch would exceed it is rejected with InvalidArgument. The first
+ * call on a device looks up that array's device address, so make that first
+ * call before any stream capture. All calls share the array and each call
+ * reinitialises it, so calls must not overlap on the GPU (different
+ * streams or threads racing each other corrupt each other's scratch). */
+DEFER_API int defer_forward_noalloc(defer_model* m, float* k_cache, float* v_cache, uint32_t cap, uint32_t pos,
+                                    uint32_t token, float* logits_out, void* stream);
+
 /* ------------------------------------------------------------- cache ---- */
 /* Model::new_cache / KvCache (src/model.rs:184-243, 370-372). `cap` = 0
  * means max_position_embeddings positions. */
