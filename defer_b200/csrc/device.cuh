@@ -1,4 +1,4 @@
-// Device-side model/batch views and the phase functions of one token step.
+// Device-side model/batch views of the token step.
 //
 // Every phase is written against a work partition (cta, ncta) so the same
 // code runs either as one launch per phase or inside the persistent
@@ -23,10 +23,14 @@
 //    w_c = expf(m_c - M), L = fmaf(w_c, l_c, L), O = fmaf(w_c, acc_c, O),
 //    out = O / L.
 //  * SiLU/GeLU, residual add: no contraction, ops.rs:120-156 order.
-//  * sampler: argmax exact (NaN skipped, lowest index on ties); softmax
-//    with s = l / T, e = expf(s - max) and a fixed hierarchical sum
-//    (8 elements per lane, 32 lanes per 256-block, 32 blocks per superblock,
-//    sequential at every level); the CDF uses the same hierarchy.
+//  * sampler (sampler.rs:24-109): argmax exact (NaN skipped, lowest index on
+//    ties); s = l / T, M = max s, e = expf(s - M), Z = sum of e, p = e * (1/Z).
+//    Every sum is hierarchical and sequential at each level: 32 elements per
+//    block, 32 blocks per group, 32 groups per supergroup, then supergroups.
+//    The CDF at element i is Q3 + (Q2 + (Q1 + t)) with Q3/Q2/Q1 the
+//    sequential prefixes of the supergroup / group / block sums before i and
+//    t the sequential prefix inside i's block, so it is monotone and its
+//    value at every block / group / supergroup end equals the running total.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -36,6 +40,8 @@ namespace defer {
 constexpr int kThreads = 256;       // threads per CTA for every phase
 constexpr int kWarps = kThreads / 32;
 constexpr int kAttnChunk = 64;      // key positions per attention chunk
+constexpr int kSBlk = 32;           // sampler block: elements per block (one per lane)
+constexpr int kMaxGroup = 8;        // sessions per GEMV register tile
 
 enum StatusCode : int {
   kStOk = 0,
@@ -101,18 +107,29 @@ struct DSlotState {
   uint32_t div_token;
 };
 
+// Sampler block statistics of one slot (nblk = ceil(V / kSBlk) entries each).
+struct DSampleStats {
+  float* lmax;   // [B][nblk] largest raw logit of the block (NaN skipped)
+  int* larg;     // [B][nblk] its index (lowest on ties), INT_MAX if none
+  float* smax;   // [B][nblk] largest s = l / T of the block
+  float* esum;   // [B][nblk] block sums of e
+  float* psum;   // [B][nblk] block sums of p
+};
+
 struct DBatch {
   int B;
   const DSession* sess;   // [B]
   DSlotState* st;         // [B]
   float* x;               // [B, H] residual stream
-  float* xn;              // [B, H] normed input of the next GEMV
   float* q;               // [B, QD]
   float* att;             // [B, QD]
   float* g;               // [B, FF]
   float* logits;          // [B, V]
   float* part;            // [B, NH, max_chunks, HD + 2] attention partials
+  int* tickets;           // [B, NKV] attention chunks finished (last one combines)
   int max_chunks;
+  int nblk;               // sampler blocks per slot
+  DSampleStats ss;
   int* status;            // global status word
   int* any_active;        // [2] set by the select phase (indexed by step parity)
   unsigned* bar;          // grid barrier counter

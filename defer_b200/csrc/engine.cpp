@@ -24,8 +24,10 @@ Runner::Runner(const Model* m, int B, int max_cap) : m_(m), B_(B), max_cap_(max_
   const DModel& d = m->dm;
   max_chunks_ = (max_cap + kAttnChunk - 1) / kAttnChunk;
   if (max_chunks_ < 1) max_chunks_ = 1;
+  nblk_ = (d.V + kSBlk - 1) / kSBlk;
   DEFER_CUDA(cudaMalloc(&x_, (size_t)B * d.H * 4));
-  DEFER_CUDA(cudaMalloc(&xn_, (size_t)B * d.H * 4));
+  DEFER_CUDA(cudaMalloc(&tickets_, (size_t)B * d.NKV * sizeof(int)));
+  DEFER_CUDA(cudaMalloc(&stats_, (size_t)5 * B * nblk_ * 4));
   DEFER_CUDA(cudaMalloc(&q_, (size_t)B * d.QD * 4));
   DEFER_CUDA(cudaMalloc(&att_, (size_t)B * d.QD * 4));
   DEFER_CUDA(cudaMalloc(&g_, (size_t)B * d.FF * 4));
@@ -40,7 +42,8 @@ Runner::Runner(const Model* m, int B, int max_cap) : m_(m), B_(B), max_cap_(max_
 
 Runner::~Runner() {
   cudaFree(x_);
-  cudaFree(xn_);
+  cudaFree(tickets_);
+  cudaFree(stats_);
   cudaFree(q_);
   cudaFree(att_);
   cudaFree(g_);
@@ -127,13 +130,23 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   DEFER_CUDA(cudaMemcpyAsync(d_sess_, sess.data(), sizeof(DSession) * n, cudaMemcpyHostToDevice, st));
   DEFER_CUDA(cudaMemcpyAsync(d_state_, state.data(), sizeof(DSlotState) * n, cudaMemcpyHostToDevice, st));
   DEFER_CUDA(cudaMemsetAsync(d_ctrl_, 0, 8 * sizeof(int), st));
+  DEFER_CUDA(cudaMemsetAsync(tickets_, 0, (size_t)n * m_->dm.NKV * sizeof(int), st));
 
   DBatch bt;
   bt.B = n;
   bt.sess = d_sess_;
   bt.st = d_state_;
   bt.x = x_;
-  bt.xn = xn_;
+  bt.tickets = tickets_;
+  bt.nblk = nblk_;
+  {
+    const size_t per = (size_t)n * nblk_;
+    bt.ss.lmax = stats_;
+    bt.ss.larg = reinterpret_cast<int*>(stats_ + per);
+    bt.ss.smax = stats_ + 2 * per;
+    bt.ss.esum = stats_ + 3 * per;
+    bt.ss.psum = stats_ + 4 * per;
+  }
   bt.q = q_;
   bt.att = att_;
   bt.g = g_;
@@ -188,7 +201,7 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   bytes += (double)steps_run * (double)m_->weight_bytes;
   m_->t_device_ms += ms;
   m_->t_runs += 1;
-  m_->t_launches += persistent ? 1 : (uint64_t)nsteps * (4 + 8 * (uint64_t)d.L) + 1;
+  m_->t_launches += persistent ? 1 : (uint64_t)nsteps * (uint64_t)launches_per_step_phased(d) + 1;
   m_->t_tokens += tokens;
   m_->t_bytes += bytes;
   if (ctrl[0] == kStTimeout) fail(kDeviceTimeout, "a grid barrier of the token loop timed out");

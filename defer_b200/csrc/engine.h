@@ -50,9 +50,10 @@ class Runner {
 
  private:
   const Model* m_;
-  int B_, max_cap_, max_chunks_;
-  float *x_ = nullptr, *xn_ = nullptr, *q_ = nullptr, *att_ = nullptr, *g_ = nullptr, *logits_ = nullptr,
-        *part_ = nullptr;
+  int B_, max_cap_, max_chunks_, nblk_;
+  float *x_ = nullptr, *q_ = nullptr, *att_ = nullptr, *g_ = nullptr, *logits_ = nullptr, *part_ = nullptr;
+  int* tickets_ = nullptr;
+  float* stats_ = nullptr;  // sampler block statistics, 5 arrays of [B][nblk]
   DSession* d_sess_ = nullptr;
   DSlotState* d_state_ = nullptr;
   int* d_ctrl_ = nullptr;  // status, any_active[2], barrier counter

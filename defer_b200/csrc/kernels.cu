@@ -18,6 +18,10 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   return v;
 }
 
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -33,8 +37,7 @@ __device__ __forceinline__ void grid_barrier(unsigned* bar, unsigned& target, in
   __syncthreads();
   if (threadIdx.x == 0) {
     target += gridDim.x;
-    __threadfence();
-    atomicAdd(bar, 1u);
+    red_release_add(bar, 1u);
     const unsigned long long t0 = globaltimer_ns();
     unsigned spins = 0;
     while ((int)(ld_acquire_u32(bar) - target) < 0) {
@@ -43,6 +46,7 @@ __device__ __forceinline__ void grid_barrier(unsigned* bar, unsigned& target, in
         break;
       }
     }
+    __threadfence();
   }
   __syncthreads();
 }
@@ -50,45 +54,47 @@ __device__ __forceinline__ void grid_barrier(unsigned* bar, unsigned& target, in
 __device__ __forceinline__ int ld_status(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
 // ------------------------------------------------------ per-phase kernels
-extern __shared__ float dyn_smem[];
+extern __shared__ __align__(16) float dyn_smem[];
 
+template <bool BF16>
 __global__ void __launch_bounds__(kThreads) k_select(DModel m, DBatch bt, int run_step) {
-  ph_select(m, bt, run_step, blockIdx.x, gridDim.x, dyn_smem);
+  ph_select<BF16>(m, bt, run_step, blockIdx.x, gridDim.x, dyn_smem);
 }
 __global__ void __launch_bounds__(kThreads) k_finalize(DBatch bt) { ph_finalize(bt, blockIdx.x, gridDim.x); }
-template <bool BF16>
-__global__ void __launch_bounds__(kThreads) k_embed(DModel m, DBatch bt) {
-  ph_embed<BF16>(m, bt, blockIdx.x, gridDim.x);
-}
-__global__ void __launch_bounds__(kThreads) k_norm(DModel m, DBatch bt, const float* w) {
-  ph_norm(m, bt, w, blockIdx.x, gridDim.x);
-}
 template <bool BF16, int G>
 __global__ void __launch_bounds__(kThreads) k_qkv(DModel m, DBatch bt, int l) {
-  ph_qkv<BF16, G>(m, bt, l, blockIdx.x, gridDim.x);
+  ph_qkv<BF16, G>(m, bt, l, blockIdx.x, gridDim.x, dyn_smem);
 }
 __global__ void __launch_bounds__(kThreads) k_attn(DModel m, DBatch bt, int l) {
   ph_attn(m, bt, l, blockIdx.x, gridDim.x, dyn_smem);
 }
-__global__ void __launch_bounds__(kThreads) k_combine(DModel m, DBatch bt) {
-  ph_combine(m, bt, blockIdx.x, gridDim.x);
-}
 template <bool BF16, int G>
-__global__ void __launch_bounds__(kThreads) k_oproj(DModel m, DBatch bt, int l) {
-  ph_residual_gemv<BF16, G>(m, bt, m.layers[l].wo, m.QD, bt.att, m.QD, blockIdx.x, gridDim.x);
+__global__ void __launch_bounds__(kThreads) k_oproj(DModel m, DBatch bt, int l, unsigned smem_floats) {
+  ph_residual_gemv<BF16, G>(m, bt, m.layers[l].wo, m.QD, bt.att, blockIdx.x, gridDim.x, dyn_smem, smem_floats);
 }
 template <bool BF16, int G>
 __global__ void __launch_bounds__(kThreads) k_gateup(DModel m, DBatch bt, int l) {
-  ph_gateup<BF16, G>(m, bt, l, blockIdx.x, gridDim.x);
+  ph_gateup<BF16, G>(m, bt, l, blockIdx.x, gridDim.x, dyn_smem);
 }
 template <bool BF16, int G>
-__global__ void __launch_bounds__(kThreads) k_down(DModel m, DBatch bt, int l) {
-  ph_residual_gemv<BF16, G>(m, bt, m.layers[l].wdown, m.FF, bt.g, m.FF, blockIdx.x, gridDim.x);
+__global__ void __launch_bounds__(kThreads) k_down(DModel m, DBatch bt, int l, unsigned smem_floats) {
+  if (l + 1 < m.L)
+    prefetch_rows(m.layers[l + 1].wqkv, m.QKVR, m.H, BF16, m.QKVR / 2, 2, blockIdx.x, gridDim.x);
+  ph_residual_gemv<BF16, G>(m, bt, m.layers[l].wdown, m.FF, bt.g, blockIdx.x, gridDim.x, dyn_smem, smem_floats);
 }
 template <bool BF16, int G>
 __global__ void __launch_bounds__(kThreads) k_head(DModel m, DBatch bt) {
-  ph_head<BF16, G>(m, bt, blockIdx.x, gridDim.x);
+  ph_head<BF16, G>(m, bt, blockIdx.x, gridDim.x, dyn_smem);
 }
+template <bool FIRST>
+__global__ void __launch_bounds__(kThreads) k_sample1(DModel m, DBatch bt) {
+  ph_sample1<FIRST>(m, bt, blockIdx.x, gridDim.x);
+}
+template <bool FIRST>
+__global__ void __launch_bounds__(kThreads) k_sample2(DModel m, DBatch bt) {
+  ph_sample2<FIRST>(m, bt, blockIdx.x, gridDim.x, dyn_smem);
+}
+__global__ void __launch_bounds__(kThreads) k_restat(DModel m, DBatch bt) { ph_restat(m, bt, blockIdx.x, gridDim.x); }
 
 // The device sampler on an arbitrary logits vector (one CTA).
 __global__ void __launch_bounds__(kThreads) k_sample_one(const float* logits, int V, float T, uint32_t word,
@@ -101,10 +107,17 @@ __global__ void __launch_bounds__(kThreads) k_sample_one(const float* logits, in
   }
 }
 
+size_t sample_one_smem_bytes(int V) {
+  const int nblk = (V + kSBlk - 1) / kSBlk;
+  const int ng2 = (nblk + 31) / 32;
+  return (size_t)(5 * nblk + ng2 + (ng2 + 31) / 32 + 8) * sizeof(float);
+}
+
 void launch_sample_one(const float* logits, int V, float T, uint32_t word, uint32_t* out_tok, float* out_margin,
                        cudaStream_t st) {
-  size_t smem = (size_t)(2 * kWarps + (V + 255) / 256 + 8) * sizeof(float);
-  if (smem > 48 * 1024) fail(kInvalidArgument, "vocabulary too large for the sampler");
+  const size_t smem = sample_one_smem_bytes(V);
+  if (smem > 200 * 1024) fail(kInvalidArgument, "vocabulary too large for the one-CTA sampler");
+  DEFER_CUDA(cudaFuncSetAttribute(k_sample_one, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   k_sample_one<<<1, kThreads, smem, st>>>(logits, V, T, word, out_tok, out_margin);
   DEFER_CUDA(cudaGetLastError());
 }
@@ -114,40 +127,51 @@ void launch_sample_one(const float* logits, int V, float T, uint32_t word, uint3
 // pointers are read from the device array, so the kernel argument block
 // stays small.
 template <bool BF16, int G>
-__global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt, int nsteps) {
+__global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt, int nsteps, unsigned smem_floats) {
   const int cta = blockIdx.x, ncta = gridDim.x;
   unsigned target = 0;
+  if (any_first(bt, false)) {  // the first step samples from the previous run's logits
+    ph_restat(m, bt, cta, ncta);
+    grid_barrier(bt.bar, target, bt.status);
+    if (any_first(bt, true)) {
+      ph_sample1<true>(m, bt, cta, ncta);
+      grid_barrier(bt.bar, target, bt.status);
+      ph_sample2<true>(m, bt, cta, ncta, dyn_smem);
+      grid_barrier(bt.bar, target, bt.status);
+    }
+  }
   for (int s = 0; s < nsteps; s++) {
-    ph_select(m, bt, s, cta, ncta, dyn_smem);
+    ph_select<BF16>(m, bt, s, cta, ncta, dyn_smem);
     grid_barrier(bt.bar, target, bt.status);
     if (ld_status(bt.status) != kStOk) return;
     if (!ld_status(bt.any_active + (s & 1))) break;
-    ph_embed<BF16>(m, bt, cta, ncta);
-    grid_barrier(bt.bar, target, bt.status);
     for (int l = 0; l < m.L; l++) {
       const DLayer& Ly = m.layers[l];
-      ph_norm(m, bt, Ly.attn_norm, cta, ncta);
-      grid_barrier(bt.bar, target, bt.status);
-      ph_qkv<BF16, G>(m, bt, l, cta, ncta);
+      ph_qkv<BF16, G>(m, bt, l, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
       ph_attn(m, bt, l, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
-      ph_combine(m, bt, cta, ncta);
+      ph_residual_gemv<BF16, G>(m, bt, Ly.wo, m.QD, bt.att, cta, ncta, dyn_smem, smem_floats);
       grid_barrier(bt.bar, target, bt.status);
-      ph_residual_gemv<BF16, G>(m, bt, Ly.wo, m.QD, bt.att, m.QD, cta, ncta);
+      ph_gateup<BF16, G>(m, bt, l, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
-      ph_norm(m, bt, Ly.ffn_norm, cta, ncta);
-      grid_barrier(bt.bar, target, bt.status);
-      ph_gateup<BF16, G>(m, bt, l, cta, ncta);
-      grid_barrier(bt.bar, target, bt.status);
-      ph_residual_gemv<BF16, G>(m, bt, Ly.wdown, m.FF, bt.g, m.FF, cta, ncta);
+      if (l + 1 < m.L) prefetch_rows(m.layers[l + 1].wqkv, m.QKVR, m.H, BF16, m.QKVR / 2, 2, cta, ncta);
+      ph_residual_gemv<BF16, G>(m, bt, Ly.wdown, m.FF, bt.g, cta, ncta, dyn_smem, smem_floats);
       grid_barrier(bt.bar, target, bt.status);
       if (ld_status(bt.status) != kStOk) return;
     }
-    ph_norm(m, bt, m.norm, cta, ncta);
+    ph_head<BF16, G>(m, bt, cta, ncta, dyn_smem);
+    // Decided before the barrier: once a CTA has passed it, the next
+    // step's SELECT may already be changing the slot state this reads, and
+    // every CTA must take the same number of barriers.
+    const bool sampling = any_sampling(bt);
     grid_barrier(bt.bar, target, bt.status);
-    ph_head<BF16, G>(m, bt, cta, ncta);
-    grid_barrier(bt.bar, target, bt.status);
+    if (sampling) {
+      ph_sample1<false>(m, bt, cta, ncta);
+      grid_barrier(bt.bar, target, bt.status);
+      ph_sample2<false>(m, bt, cta, ncta, dyn_smem);
+      grid_barrier(bt.bar, target, bt.status);
+    }
     if (ld_status(bt.status) != kStOk) return;
   }
   ph_finalize(bt, cta, ncta);
@@ -156,43 +180,75 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
 // ------------------------------------------------------------ launchers
 static int div_up(long a, long b) { return (int)((a + b - 1) / b); }
 
-size_t step_smem_bytes(const DModel& m) {
-  const int G = m.NH / m.NKV;
-  size_t attn = (size_t)(G * m.HD + G * kAttnChunk) * sizeof(float);
-  size_t samp = (size_t)(2 * kWarps + (m.V + 255) / 256 + 8) * sizeof(float);
-  size_t s = attn > samp ? attn : samp;
-  return s < 1024 ? 1024 : s;
+static int group_for(int B) { return B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8; }
+
+// Dynamic shared memory (floats) of the step phases for a batch of B: the
+// staged activations of one slot group (normed inputs, O-projection input,
+// the down-projection input when it fits), the attention chunk, and the
+// sampler's group sums.
+static size_t step_smem_floats(const DModel& m, int B) {
+  const int G = group_for(B);
+  const int Gh = m.NH / m.NKV;
+  size_t f = (size_t)G * std::max(m.H, m.QD);
+  const size_t ffs = (size_t)G * m.FF;
+  if (ffs * 4 <= 96 * 1024) f = std::max(f, ffs);
+  f = std::max(f, (size_t)(Gh * m.HD + Gh * kAttnChunk));
+  const int nblk = (m.V + kSBlk - 1) / kSBlk;
+  const int ng2 = (nblk + 31) / 32;
+  f = std::max(f, (size_t)(ng2 + (ng2 + 31) / 32 + 8));
+  return (f + 3) & ~(size_t)3;
+}
+
+size_t step_smem_bytes(const DModel& m, int B) { return step_smem_floats(m, B) * sizeof(float); }
+
+template <class K>
+static void allow_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024)
+    DEFER_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
 }
 
 template <bool BF16, int G>
 static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt, int first_step, int nsteps, int sms,
                         cudaStream_t st) {
-  const size_t smem = step_smem_bytes(m);
+  const size_t sf = step_smem_floats(m, bt.B);
+  const size_t smem = sf * sizeof(float);
+  allow_smem(k_select<BF16>, smem);
+  allow_smem(k_qkv<BF16, G>, smem);
+  allow_smem(k_attn, smem);
+  allow_smem(k_oproj<BF16, G>, smem);
+  allow_smem(k_gateup<BF16, G>, smem);
+  allow_smem(k_down<BF16, G>, smem);
+  allow_smem(k_head<BF16, G>, smem);
+  allow_smem(k_sample2<false>, smem);
+  allow_smem(k_sample2<true>, smem);
   const int B = bt.B;
-  const int cap = sms * 8;
-  auto wg = [&](long units) { return std::max(1, std::min(div_up(units, kWarps), cap)); };
+  const int grid = sms;
   const int attn_units = B * m.NKV * bt.max_chunks;
+  (void)hl;
+  // statistics of the resident logits for slots whose first step samples
+  // (each kernel skips the slots that do not)
+  k_restat<<<grid, kThreads, 0, st>>>(m, bt);
+  k_sample1<true><<<grid, kThreads, 0, st>>>(m, bt);
+  k_sample2<true><<<grid, kThreads, smem, st>>>(m, bt);
   for (int s = 0; s < nsteps; s++) {
-    k_select<<<B, kThreads, smem, st>>>(m, bt, first_step + s);
-    k_embed<BF16><<<B, kThreads, 0, st>>>(m, bt);
+    k_select<BF16><<<B, kThreads, smem, st>>>(m, bt, first_step + s);
     for (int l = 0; l < m.L; l++) {
-      k_norm<<<B, kThreads, 0, st>>>(m, bt, hl[l].attn_norm);
-      k_qkv<BF16, G><<<wg(m.QKVR / 2), kThreads, 0, st>>>(m, bt, l);
-      k_attn<<<std::min(attn_units, cap), kThreads, smem, st>>>(m, bt, l);
-      k_combine<<<std::min(B * m.NH, cap), kThreads, 0, st>>>(m, bt);
-      k_oproj<BF16, G><<<wg(m.H), kThreads, 0, st>>>(m, bt, l);
-      k_norm<<<B, kThreads, 0, st>>>(m, bt, hl[l].ffn_norm);
-      k_gateup<BF16, G><<<wg(m.FF), kThreads, 0, st>>>(m, bt, l);
-      k_down<BF16, G><<<wg(m.H), kThreads, 0, st>>>(m, bt, l);
+      k_qkv<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l);
+      k_attn<<<std::min(attn_units, sms * 8), kThreads, smem, st>>>(m, bt, l);
+      k_oproj<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l, (unsigned)sf);
+      k_gateup<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l);
+      k_down<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l, (unsigned)sf);
     }
-    k_norm<<<B, kThreads, 0, st>>>(m, bt, m.norm);
-    k_head<BF16, G><<<wg(m.V), kThreads, 0, st>>>(m, bt);
+    k_head<BF16, G><<<grid, kThreads, smem, st>>>(m, bt);
+    // The sample phases skip every slot that does not sample next.
+    k_sample1<false><<<grid, kThreads, 0, st>>>(m, bt);
+    k_sample2<false><<<grid, kThreads, smem, st>>>(m, bt);
   }
   k_finalize<<<B, kThreads, 0, st>>>(bt);
   DEFER_CUDA(cudaGetLastError());
 }
 
-static int group_for(int B) { return B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8; }
+int launches_per_step_phased(const DModel& m) { return 4 + 5 * m.L; }
 
 void launch_steps_phased(const DModel& m, const DLayer* host_layers, const DBatch& bt, int first_step, int nsteps,
                          int sms, cudaStream_t st) {
@@ -216,8 +272,10 @@ void launch_steps_phased(const DModel& m, const DLayer* host_layers, const DBatc
 
 template <bool BF16, int G>
 static void persistent_impl(const DModel& m, const DBatch& bt, int nsteps, int sms, cudaStream_t st) {
-  const size_t smem = step_smem_bytes(m);
+  const size_t sf = step_smem_floats(m, bt.B);
+  const size_t smem = sf * sizeof(float);
   auto kern = k_persistent<BF16, G>;
+  allow_smem(kern, smem);
   int per_sm = 0;
   DEFER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
   if (per_sm < 1) fail(kCuda, "persistent kernel cannot be resident");
@@ -227,7 +285,8 @@ static void persistent_impl(const DModel& m, const DBatch& bt, int nsteps, int s
   DModel mm = m;
   DBatch bb = bt;
   int ns = nsteps;
-  void* args[] = {&mm, &bb, &ns};
+  unsigned sfl = (unsigned)sf;
+  void* args[] = {&mm, &bb, &ns, &sfl};
   DEFER_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(kThreads), args, smem, st));
 }
 

@@ -28,8 +28,10 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 // into the scratch (every call starts from these values, whatever the
 // previous call left there).
 __global__ void k_noalloc_init(DSession s, uint32_t token, DSession* d_sess, DSlotState* d_state, uint32_t* d_tok,
-                               int* ctrl) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+                               int* ctrl, int* tickets, int n_tickets) {
+  if (blockIdx.x != 0) return;
+  for (int i = threadIdx.x; i < n_tickets; i += blockDim.x) tickets[i] = 0;
+  if (threadIdx.x != 0) return;
   *d_tok = token;
   s.tokens = d_tok;
   *d_sess = s;
@@ -89,8 +91,10 @@ void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uin
   const size_t o_state = take(sizeof(DSlotState));
   const size_t o_sess = take(sizeof(DSession));
   const size_t o_tok = take(sizeof(uint32_t));
+  const int nblk = (d.V + kSBlk - 1) / kSBlk;
   const size_t o_x = take((size_t)d.H * 4);
-  const size_t o_xn = take((size_t)d.H * 4);
+  const size_t o_tickets = take((size_t)d.NKV * sizeof(int));
+  const size_t o_stats = take((size_t)5 * nblk * 4);
   const size_t o_q = take((size_t)d.QD * 4);
   const size_t o_att = take((size_t)d.QD * 4);
   const size_t o_g = take((size_t)d.FF * 4);
@@ -122,7 +126,8 @@ void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uin
   s.n_total = 1;
   s.temperature = 0.0f;
   s.verify = 0;
-  k_noalloc_init<<<1, 32, 0, st>>>(s, token, sess, state, tok, ctrl);
+  int* tickets = reinterpret_cast<int*>(base + o_tickets);
+  k_noalloc_init<<<1, 32, 0, st>>>(s, token, sess, state, tok, ctrl, tickets, d.NKV);
   DEFER_CUDA(cudaGetLastError());
 
   DBatch bt;
@@ -130,7 +135,14 @@ void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uin
   bt.sess = sess;
   bt.st = state;
   bt.x = reinterpret_cast<float*>(base + o_x);
-  bt.xn = reinterpret_cast<float*>(base + o_xn);
+  bt.tickets = tickets;
+  bt.nblk = nblk;
+  float* stats = reinterpret_cast<float*>(base + o_stats);
+  bt.ss.lmax = stats;
+  bt.ss.larg = reinterpret_cast<int*>(stats + nblk);
+  bt.ss.smax = stats + 2 * nblk;
+  bt.ss.esum = stats + 3 * nblk;
+  bt.ss.psum = stats + 4 * nblk;
   bt.q = reinterpret_cast<float*>(base + o_q);
   bt.att = reinterpret_cast<float*>(base + o_att);
   bt.g = reinterpret_cast<float*>(base + o_g);

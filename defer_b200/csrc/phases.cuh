@@ -1,5 +1,13 @@
 // Phase functions of one token step (see device.cuh for the arithmetic
 // contract). Included by kernels.cu only.
+//
+// A step is: SELECT (choose this step's token per slot, write the embedding
+// row) | per layer: QKV (RMSNorm + projection + RoPE + KV append) | ATTN
+// (chunk partials; the last chunk of each KV head combines) | O (+residual)
+// | GATEUP (RMSNorm + gate/up + SiLU*up) | DOWN (+residual) | HEAD (final
+// RMSNorm + lm_head + sampler block statistics) | for slots that sample at
+// T > 0 next: SAMPLE1 (block e-sums) | SAMPLE2 (block p-sums). Each "|" is a
+// grid-wide dependency (one barrier in the persistent kernel).
 #pragma once
 #include <cuda_runtime.h>
 
@@ -37,6 +45,18 @@ __device__ __forceinline__ float ld_f(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ int ld_i(const int* p) { return __ldcg(p); }
 __device__ __forceinline__ uint32_t ld_u(const uint32_t* p) { return __ldcg(p); }
 
+// Starts moving [p, p + bytes) from HBM into L2 without waiting (16-byte
+// granules; p 16-byte aligned). Used to stream the next phase's weights
+// while the current phase and its barrier run.
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
+  const char* c = static_cast<const char*>(p);
+  const size_t piece = 64 * 1024;
+  for (size_t off = (size_t)(threadIdx.x & 31) * piece; off < bytes; off += 32 * piece) {
+    const size_t n = (bytes - off < piece ? bytes - off : piece) & ~(size_t)15;
+    if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c + off), "r"((unsigned)n) : "memory");
+  }
+}
+
 __device__ __forceinline__ float warp_sum_butterfly(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -47,6 +67,14 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
   return v;
+}
+
+// Sequential sum of the 32 lane values in lane order (all lanes get it).
+__device__ __forceinline__ float warp_seq_sum(float v) {
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, v, j));
+  return s;
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
@@ -82,10 +110,17 @@ struct WChunk<true> {
   }
 };
 
+// Activation chunk of slot g: from shared memory (staged) or global (L2).
+template <bool SMEM>
+__device__ __forceinline__ float4 ld_x(const float* p) {
+  if (SMEM) return *reinterpret_cast<const float4*>(p);
+  return ld_act(p);
+}
+
 // Canonical warp dot product of NR weight rows against G activation
-// vectors (all lanes return the same sums).
-template <bool BF16, int NR, int G>
-__device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, const float* const (&xs)[G],
+// vectors x_g = xs + g * xstride (all lanes return the same sums).
+template <bool BF16, bool SMEM, int NR, int G>
+__device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, const float* xs, int xstride,
                                          float (&acc)[NR][G]) {
   constexpr int E = WChunk<BF16>::E;
   const int lane = threadIdx.x & 31;
@@ -94,7 +129,7 @@ __device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, c
   for (int r = 0; r < NR; r++)
 #pragma unroll
     for (int g = 0; g < G; g++) acc[r][g] = 0.0f;
-#pragma unroll 2
+#pragma unroll 4
   for (int j = lane; j < nch; j += 32) {
     float w[NR][E];
 #pragma unroll
@@ -104,7 +139,7 @@ __device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, c
       float xv[E];
 #pragma unroll
       for (int q = 0; q < E / 4; q++) {
-        float4 t = ld_act(xs[g] + j * E + 4 * q);
+        float4 t = ld_x<SMEM>(xs + (size_t)g * xstride + j * E + 4 * q);
         xv[4 * q] = t.x;
         xv[4 * q + 1] = t.y;
         xv[4 * q + 2] = t.z;
@@ -124,19 +159,394 @@ __device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, c
 
 __device__ __forceinline__ size_t row_bytes(int K, bool bf16) { return (size_t)K * (bf16 ? 2 : 4); }
 
-// ----------------------------------------------------------- select / embed
-__device__ uint32_t sample_cta(const float* logits, int V, float T, uint32_t word, float* margin, float* smem);
+// Contiguous share [u0, u1) of `units` for CTA `cta` of `ncta`.
+__device__ __forceinline__ void cta_range(int units, int cta, int ncta, int& u0, int& u1) {
+  u0 = (int)((long long)units * cta / ncta);
+  u1 = (int)((long long)units * (cta + 1) / ncta);
+}
 
-// Advances the slots that fed a token in the previous step, then picks the
-// token of this step for every slot (prompt token, sample, or verified
-// replay of a recorded token). CTA unit = slot.
+// Prefetch of this CTA's rows [u0*rows_per_unit, u1*rows_per_unit) of a
+// matrix with K columns, when the whole matrix is small enough to sit in
+// L2 next to the phase in flight.
+constexpr size_t kPrefetchMaxBytes = 48u << 20;
+__device__ __forceinline__ void prefetch_rows(const void* W, int rows_total, int K, bool bf16, int units, int per_unit,
+                                              int cta, int ncta) {
+  const size_t rb = row_bytes(K, bf16);
+  if ((size_t)rows_total * rb > kPrefetchMaxBytes) return;
+  if (threadIdx.x >= 32) return;
+  int u0, u1;
+  cta_range(units, cta, ncta, u0, u1);
+  if (u1 > u0)
+    prefetch_l2(static_cast<const char*>(W) + (size_t)u0 * per_unit * rb, (size_t)(u1 - u0) * per_unit * rb);
+}
+
+// ------------------------------------------------------------ RMSNorm
+// dst[g][i] = rmsnorm(x of slot b0+g)[i] for the G slots of a group
+// (inactive or missing slots get zeros). Warp g computes slot g's sum of
+// squares with the canonical dot; all threads then write the products.
+template <int G>
+__device__ void stage_norm(const DModel& m, const DBatch& bt, int b0, const float* w_of_layer, const float* x,
+                           float* dst) {
+  __shared__ float s_inv[kMaxGroup];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < G) {
+    const int b = b0 + warp;
+    float acc = 0.0f;
+    if (b < bt.B && ld_i(&bt.st[b].active)) {
+      const float* xb = x + (size_t)b * m.H;
+      for (int j = lane; j < m.H / 4; j += 32) {
+        float4 t = ld_act(xb + 4 * j);
+        acc = fmaf(t.x, t.x, acc);
+        acc = fmaf(t.y, t.y, acc);
+        acc = fmaf(t.z, t.z, acc);
+        acc = fmaf(t.w, t.w, acc);
+      }
+    }
+    acc = warp_sum_butterfly(acc);
+    if (lane == 0) s_inv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)m.H), m.eps)));
+  }
+  __syncthreads();
+  for (int g = 0; g < G; g++) {
+    const int b = b0 + g;
+    const bool live = b < bt.B && ld_i(&bt.st[b].active);
+    const float inv = s_inv[g];
+    const float* xb = x + (size_t)(live ? b : 0) * m.H;
+    for (int i = threadIdx.x; i < m.H; i += kThreads)
+      dst[(size_t)g * m.H + i] = live ? __fmul_rn(__fmul_rn(ld_f(xb + i), inv), w_of_layer[i]) : 0.0f;
+  }
+  __syncthreads();
+}
+
+// Copies slot activations [b0, b0+G) (stride K) into shared memory.
+template <int G>
+__device__ void stage_copy(const DBatch& bt, int b0, const float* src, int K, float* dst) {
+  for (int g = 0; g < G; g++) {
+    const int b = b0 + g;
+    const bool live = b < bt.B;
+    const float* s = src + (size_t)(live ? b : 0) * K;
+    for (int i = threadIdx.x * 4; i < K; i += kThreads * 4) {
+      float4 v = live ? ld_act(s + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(dst + (size_t)g * K + i) = v;
+    }
+  }
+  __syncthreads();
+}
+
+// --------------------------------------------------------------- sampler
+struct ValIdx {
+  float v;
+  int i;
+};
+
+// b better than a: valid (non-NaN), larger, or equal with a lower index.
+__device__ __forceinline__ bool vi_better(ValIdx b, ValIdx a) {
+  if (b.i == INT_MAX) return false;
+  if (a.i == INT_MAX) return true;
+  return b.v > a.v || (b.v == a.v && b.i < a.i);
+}
+
+__device__ __forceinline__ ValIdx vi_warp_best(ValIdx x) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    ValIdx o{__shfl_xor_sync(0xffffffffu, x.v, off), __shfl_xor_sync(0xffffffffu, x.i, off)};
+    if (vi_better(o, x)) x = o;
+  }
+  return x;
+}
+
+// e of logit l (NaN s counts as 0, sampler.rs:56).
+__device__ __forceinline__ float e_of(float l, float T, float M) {
+  const float s = __fdiv_rn(l, T);
+  return isnan(s) ? 0.0f : expf(__fsub_rn(s, M));
+}
+
+// Warp statistics of one 32-element block held one value per lane
+// (`valid` false past the vocabulary): raw argmax and max of s = l / T.
+__device__ __forceinline__ void block_stats(float l, int idx, bool valid, float T, float* lmax, int* larg,
+                                            float* smax) {
+  ValIdx me{l, (valid && !isnan(l)) ? idx : INT_MAX};
+  ValIdx best = vi_warp_best(me);
+  float s = -INFINITY;
+  if (valid && T != 0.0f) s = __fdiv_rn(l, T);
+  s = warp_max(s);  // fmaxf skips NaN
+  if ((threadIdx.x & 31) == 0) {
+    *lmax = best.v;
+    *larg = best.i;
+    *smax = s;
+  }
+}
+
+// Sequential sum of a[k0 .. min(k0 + 32, n)) (terms past n add exactly 0).
+__device__ __forceinline__ float seq_sum32(const float* a, int k0, int n, bool global_src) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) v[j] = (k0 + j < n) ? (global_src ? ld_f(a + k0 + j) : a[k0 + j]) : 0.0f;
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j++) s = __fadd_rn(s, v[j]);
+  return s;
+}
+
+// Hierarchical totals of block sums `bs[0..nblk)` into smem:
+// g2[nblk/32 groups], g3[groups/32 supergroups]; returns the total (all
+// threads). Sequential at every level.
+__device__ float hier_total(const float* bs, int nblk, float* g2, float* g3, bool global_src) {
+  const int ng2 = (nblk + 31) / 32, ng3 = (ng2 + 31) / 32;
+  __shared__ float s_tot;
+  for (int t = threadIdx.x; t < ng2; t += kThreads) g2[t] = seq_sum32(bs, t * 32, nblk, global_src);
+  __syncthreads();
+  for (int t = threadIdx.x; t < ng3; t += kThreads) g3[t] = seq_sum32(g2, t * 32, ng2, false);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int k = 0; k < ng3; k++) s = __fadd_rn(s, g3[k]);
+    s_tot = s;
+  }
+  __syncthreads();
+  const float r = s_tot;
+  __syncthreads();
+  return r;
+}
+
+// Finds the sampled token from the block p-sums (CDF search, sampler.rs:94-108).
+// `lg` holds the slot's logits (global). Returns the token; *margin = distance
+// of r to the nearest edge of the chosen token's CDF interval. smem needs
+// ng2 + ng3 floats. Whole CTA.
+__device__ uint32_t cdf_find(const float* lg, int V, const float* psum, bool global_src, int nblk, float T, float M,
+                             float inv, float r, float* margin, float* smem) {
+  const int ng2 = (nblk + 31) / 32, ng3 = (ng2 + 31) / 32;
+  float* g2 = smem;
+  float* g3 = smem + ng2;
+  hier_total(psum, nblk, g2, g3, global_src);
+  __shared__ int s_blk, s_found, s_tok, s_last, s_grp;
+  __shared__ float s_base, s_Q3, s_Q2, s_Q1, s_margin;
+  if (threadIdx.x == 0) {
+    // supergroup and group searches; cum = Q3 + (Q2 + (Q1 + t))
+    float Q3 = 0.0f;
+    int found = 0, grp = 0;
+    float Q2f = 0.0f;
+    for (int t3 = 0; t3 < ng3 && !found; t3++) {
+      const float Q3n = __fadd_rn(Q3, g3[t3]);
+      if (r < Q3n) {
+        float Q2 = 0.0f;
+        const int e2 = min(ng2, t3 * 32 + 32);
+        for (int t2 = t3 * 32; t2 < e2; t2++) {
+          const float Q2n = __fadd_rn(Q2, g2[t2]);
+          if (r < __fadd_rn(Q3, Q2n) || t2 == e2 - 1) {  // the end of the supergroup is Q3n
+            found = 1;
+            grp = t2;
+            Q2f = Q2;
+            break;
+          }
+          Q2 = Q2n;
+        }
+        s_Q3 = Q3;
+        break;
+      }
+      Q3 = Q3n;
+    }
+    s_found = found;
+    s_grp = grp;
+    s_Q2 = Q2f;
+    s_base = Q3;  // when not found: the CDF total
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // block search inside the group (warp 0), and the last block with p > 0
+    const int lane = threadIdx.x;
+    if (s_found) {
+      const int k = s_grp * 32 + lane;
+      const float bsum = k < nblk ? (global_src ? ld_f(psum + k) : psum[k]) : 0.0f;
+      float Q1 = 0.0f;  // sequential prefix of the block sums before this lane
+      for (int j = 0; j < 32; j++) {
+        const float o = __shfl_sync(0xffffffffu, bsum, j);
+        if (j < lane) Q1 = __fadd_rn(Q1, o);
+      }
+      const float Q3 = s_Q3, Q2 = s_Q2;
+      const bool in = k < nblk && r < __fadd_rn(Q3, __fadd_rn(Q2, __fadd_rn(Q1, bsum)));
+      const unsigned hit = __ballot_sync(0xffffffffu, in);
+      const unsigned valid = __ballot_sync(0xffffffffu, k < nblk);
+      const int j = hit ? __ffs(hit) - 1 : 31 - __clz(valid);  // the group's end is Q3 + Q2n
+      if (lane == j) {
+        s_blk = k;
+        s_Q1 = Q1;
+      }
+    }
+    int lastb = -1;  // highest block with p > 0
+    for (int k0 = ((nblk - 1) / 32) * 32; k0 >= 0 && lastb < 0; k0 -= 32) {
+      const int k = k0 + lane;
+      const bool nz = k < nblk && (global_src ? ld_f(psum + k) : psum[k]) > 0.0f;
+      const unsigned m = __ballot_sync(0xffffffffu, nz);
+      if (m) lastb = k0 + 31 - __clz(m);
+    }
+    if (lane == 0) s_last = lastb;
+  }
+  __syncthreads();
+  uint32_t tok;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    if (s_found) {
+      const int i = s_blk * kSBlk + lane;
+      const float p = i < V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
+      float t = 0.0f, prevt = 0.0f;
+      for (int j = 0; j < 32; j++) {
+        const float o = __shfl_sync(0xffffffffu, p, j);
+        if (j <= lane) {
+          prevt = t;
+          t = __fadd_rn(t, o);
+        }
+      }
+      const float Q3 = s_Q3, Q2 = s_Q2, Q1 = s_Q1;
+      const float cum = __fadd_rn(Q3, __fadd_rn(Q2, __fadd_rn(Q1, t)));
+      const float prev = lane == 0 ? __fadd_rn(Q3, __fadd_rn(Q2, Q1)) : __fadd_rn(Q3, __fadd_rn(Q2, __fadd_rn(Q1, prevt)));
+      const unsigned hit = __ballot_sync(0xffffffffu, i < V && r < cum);
+      if (hit) {
+        const int j = __ffs(hit) - 1;
+        if (lane == j) {
+          s_tok = i;
+          s_margin = fminf(__fsub_rn(cum, r), __fsub_rn(r, prev));
+        }
+      } else {
+        // only reachable when the block was chosen as the last of its
+        // group without r falling inside: the last non-zero token
+        const unsigned nz = __ballot_sync(0xffffffffu, i < V && p > 0.0f);
+        if (lane == 0) {
+          s_tok = nz ? s_blk * kSBlk + 31 - __clz(nz) : max(0, s_blk * kSBlk);
+          s_margin = 0.0f;
+        }
+      }
+    } else {
+      const int lb = s_last;
+      const int i = (lb < 0 ? 0 : lb) * kSBlk + lane;
+      const float p = (lb >= 0 && i < V) ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
+      const unsigned nz = __ballot_sync(0xffffffffu, p > 0.0f);
+      if (lane == 0) {
+        s_tok = nz ? lb * kSBlk + 31 - __clz(nz) : 0;
+        s_margin = __fsub_rn(r, s_base);
+      }
+    }
+  }
+  __syncthreads();
+  tok = (uint32_t)s_tok;
+  *margin = s_margin;
+  __syncthreads();
+  return tok;
+}
+
+// Greedy choice from the block statistics (exact).
+__device__ uint32_t argmax_from_blocks(const float* lmax, const int* larg, int nblk, bool global_src) {
+  ValIdx best{NAN, INT_MAX};
+  for (int k = threadIdx.x; k < nblk; k += kThreads) {
+    ValIdx c{global_src ? ld_f(lmax + k) : lmax[k], global_src ? ld_i(larg + k) : larg[k]};
+    if (vi_better(c, best)) best = c;
+  }
+  best = vi_warp_best(best);
+  __shared__ float s_v[kWarps];
+  __shared__ int s_i[kWarps];
+  __shared__ int s_res;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    s_v[warp] = best.v;
+    s_i[warp] = best.i;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    ValIdx c = lane < kWarps ? ValIdx{s_v[lane], s_i[lane]} : ValIdx{NAN, INT_MAX};
+    c = vi_warp_best(c);
+    if (lane == 0) s_res = c.i == INT_MAX ? 0 : c.i;
+  }
+  __syncthreads();
+  const uint32_t r = (uint32_t)s_res;
+  __syncthreads();
+  return r;
+}
+
+__device__ float max_of(const float* a, int n, bool global_src) {
+  float v = -INFINITY;
+  for (int k = threadIdx.x; k < n; k += kThreads) v = fmaxf(v, global_src ? ld_f(a + k) : a[k]);
+  v = warp_max(v);
+  __shared__ float s_m[kWarps];
+  if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = -INFINITY;
+  for (int w = 0; w < kWarps; w++) r = fmaxf(r, s_m[w]);
+  __syncthreads();
+  return r;
+}
+
+// Whole sampler on one logits vector by one CTA (same arithmetic as the
+// distributed path: the block statistics and sums are computed here).
+// smem: 5 * nblk + ng2 + ng3 floats.
+__device__ uint32_t sample_cta(const float* lg, int V, float T, uint32_t word, float* margin, float* smem) {
+  const int nblk = (V + kSBlk - 1) / kSBlk;
+  float* lmax = smem;
+  int* larg = reinterpret_cast<int*>(smem + nblk);
+  float* smax = smem + 2 * nblk;
+  float* esum = smem + 3 * nblk;
+  float* psum = smem + 4 * nblk;
+  float* tail = smem + 5 * nblk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int k = warp; k < nblk; k += kWarps) {
+    const int i = k * kSBlk + lane;
+    const bool valid = i < V;
+    const float l = valid ? ld_f(lg + i) : NAN;
+    block_stats(l, i, valid, T, lmax + k, larg + k, smax + k);
+  }
+  __syncthreads();
+  if (T == 0.0f) {
+    *margin = 0.0f;
+    return argmax_from_blocks(lmax, larg, nblk, false);
+  }
+  const float M = max_of(smax, nblk, false);
+  for (int k = warp; k < nblk; k += kWarps) {
+    const int i = k * kSBlk + lane;
+    const float e = i < V ? e_of(ld_f(lg + i), T, M) : 0.0f;
+    const float s = warp_seq_sum(e);
+    if (lane == 0) esum[k] = s;
+  }
+  __syncthreads();
+  const float Z = hier_total(esum, nblk, tail, tail + (nblk + 31) / 32, false);
+  if (!(Z > 0.0f) || !isfinite(Z)) {
+    *margin = NAN;
+    return argmax_from_blocks(lmax, larg, nblk, false);
+  }
+  const float inv = __fdiv_rn(1.0f, Z);
+  for (int k = warp; k < nblk; k += kWarps) {
+    const int i = k * kSBlk + lane;
+    const float p = i < V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
+    const float s = warp_seq_sum(p);
+    if (lane == 0) psum[k] = s;
+  }
+  __syncthreads();
+  const float r = (float)(word >> 8) * (1.0f / 16777216.0f);
+  return cdf_find(lg, V, psum, false, nblk, T, M, inv, r, margin, tail);
+}
+
+// ----------------------------------------------------------- select / embed
+// Whether slot b samples at T > 0 in the step after the current one.
+__device__ __forceinline__ bool samples_next(const DBatch& bt, int b) {
+  const DSession& S = bt.sess[b];
+  if (S.temperature == 0.0f) return false;
+  if (!ld_i(&bt.st[b].active) || ld_i(&bt.st[b].done)) return false;
+  const int nxt = ld_i(&bt.st[b].step) + 1;
+  return nxt >= S.n_prompt && nxt < S.n_total;
+}
+
+// Advances the slots that fed a token in the previous step, picks the
+// token of this step for every slot (prompt token, sample from the
+// previous step's statistics, or verified replay of a recorded token) and
+// writes its embedding row. CTA unit = slot.
+template <bool BF16>
 __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int cta, int ncta, float* smem) {
   const int tid = threadIdx.x;
   if (cta == 0 && tid == 0) bt.any_active[(run_step + 1) & 1] = 0;
-  __shared__ int s_go;
+  __shared__ int s_go, s_step;
+  __shared__ uint32_t s_tok;
   for (int b = cta; b < bt.B; b += ncta) {
     DSlotState* st = bt.st + b;
     const DSession& S = bt.sess[b];
+    // Thread 0 owns the slot state; the decisions every thread branches on
+    // travel through shared memory (never re-read from global memory).
     if (tid == 0) {
       if (st->was_active) {
         st->pos += 1;
@@ -146,21 +556,40 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
       st->active = 0;
       if (st->step >= S.n_total) st->done = 1;
       s_go = !st->done;
+      s_step = st->step;
     }
     __syncthreads();
     if (!s_go) {
       __syncthreads();
       continue;
     }
-    const int s = ld_i(&st->step);
+    const int s = s_step;
     uint32_t tok;
     if (s < S.n_prompt) {
       tok = S.tokens[s];
     } else {
       const int k = s - S.n_prompt;
       const float T = S.temperature;
+      const int nb = bt.nblk;
+      const float* lmax = bt.ss.lmax + (size_t)b * nb;
+      const int* larg = bt.ss.larg + (size_t)b * nb;
       float margin = 0.0f;
-      uint32_t smp = sample_cta(bt.logits + (size_t)b * m.V, m.V, T, T == 0.0f ? 0u : S.words[k], &margin, smem);
+      uint32_t smp;
+      if (T == 0.0f) {
+        smp = argmax_from_blocks(lmax, larg, nb, true);
+      } else {
+        const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
+        const int ng2 = (nb + 31) / 32;
+        const float Z = hier_total(bt.ss.esum + (size_t)b * nb, nb, smem, smem + ng2, true);
+        if (!(Z > 0.0f) || !isfinite(Z)) {
+          smp = argmax_from_blocks(lmax, larg, nb, true);
+          margin = NAN;
+        } else {
+          const float r = (float)(S.words[k] >> 8) * (1.0f / 16777216.0f);
+          smp = cdf_find(bt.logits + (size_t)b * m.V, m.V, bt.ss.psum + (size_t)b * nb, true, nb, T, M,
+                         __fdiv_rn(1.0f, Z), r, &margin, smem);
+        }
+      }
       if (S.verify) {
         tok = S.tokens[s];
         if (tid == 0 && smp != tok) {
@@ -174,22 +603,38 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
       }
       if (tid == 0 && S.margins) S.margins[k] = margin;
     }
-    if (tid == 0 && !st->done) {
-      if (tok >= (uint32_t)m.V) {
-        atomicExch(bt.status, kStBadToken);
-        st->done = 1;
-      } else if (st->pos >= m.max_seq || st->pos >= S.cap) {
-        atomicExch(bt.status, kStContext);
-        st->done = 1;
-      } else {
-        st->cur = tok;
-        st->active = 1;
-        st->was_active = 1;
-        bt.any_active[run_step & 1] = 1;
-        if (!S.verify && s >= S.n_prompt) {
-          for (int i = 0; i < S.n_stop; i++)
-            if (S.stop[i] == tok) st->done = 1;  // fed now, nothing after it
+    if (tid == 0) {
+      s_tok = 0xFFFFFFFFu;
+      if (!st->done) {
+        if (tok >= (uint32_t)m.V) {
+          atomicExch(bt.status, kStBadToken);
+          st->done = 1;
+        } else if (st->pos >= m.max_seq || st->pos >= S.cap) {
+          atomicExch(bt.status, kStContext);
+          st->done = 1;
+        } else {
+          st->cur = tok;
+          st->active = 1;
+          st->was_active = 1;
+          bt.any_active[run_step & 1] = 1;
+          s_tok = tok;
+          if (!S.verify && s >= S.n_prompt) {
+            for (int i = 0; i < S.n_stop; i++)
+              if (S.stop[i] == tok) st->done = 1;  // fed now, nothing after it
+          }
         }
+      }
+    }
+    __syncthreads();
+    const uint32_t t = s_tok;
+    if (t != 0xFFFFFFFFu) {
+      float* x = bt.x + (size_t)b * m.H;
+      if (BF16) {
+        const uint16_t* e = reinterpret_cast<const uint16_t*>(m.embed) + (size_t)t * m.H;
+        for (int i = tid; i < m.H; i += kThreads) x[i] = __uint_as_float((uint32_t)e[i] << 16);
+      } else {
+        const float* e = reinterpret_cast<const float*>(m.embed) + (size_t)t * m.H;
+        for (int i = tid; i < m.H; i += kThreads) x[i] = e[i];
       }
     }
     __syncthreads();
@@ -211,68 +656,27 @@ __device__ void ph_finalize(const DBatch& bt, int cta, int ncta) {
   }
 }
 
-template <bool BF16>
-__device__ void ph_embed(const DModel& m, const DBatch& bt, int cta, int ncta) {
-  for (int b = cta; b < bt.B; b += ncta) {
-    if (!ld_i(&bt.st[b].active)) continue;
-    const uint32_t tok = ld_u(&bt.st[b].cur);
-    float* x = bt.x + (size_t)b * m.H;
-    if (BF16) {
-      const uint16_t* e = reinterpret_cast<const uint16_t*>(m.embed) + (size_t)tok * m.H;
-      for (int i = threadIdx.x; i < m.H; i += kThreads) x[i] = __uint_as_float((uint32_t)e[i] << 16);
-    } else {
-      const float* e = reinterpret_cast<const float*>(m.embed) + (size_t)tok * m.H;
-      for (int i = threadIdx.x; i < m.H; i += kThreads) x[i] = e[i];
-    }
-  }
-}
-
-// xn = rmsnorm(x, w) per active slot. CTA unit = slot.
-__device__ void ph_norm(const DModel& m, const DBatch& bt, const float* w, int cta, int ncta) {
-  __shared__ float s_inv;
-  for (int b = cta; b < bt.B; b += ncta) {
-    if (!ld_i(&bt.st[b].active)) continue;
-    const float* x = bt.x + (size_t)b * m.H;
-    if (threadIdx.x < 32) {
-      const int lane = threadIdx.x;
-      float acc = 0.0f;
-      for (int j = lane; j < m.H / 4; j += 32) {
-        float4 t = ld_act(x + 4 * j);
-        acc = fmaf(t.x, t.x, acc);
-        acc = fmaf(t.y, t.y, acc);
-        acc = fmaf(t.z, t.z, acc);
-        acc = fmaf(t.w, t.w, acc);
-      }
-      acc = warp_sum_butterfly(acc);
-      if (lane == 0) s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)m.H), m.eps)));
-    }
-    __syncthreads();
-    const float inv = s_inv;
-    float* xn = bt.xn + (size_t)b * m.H;
-    for (int i = threadIdx.x; i < m.H; i += kThreads) xn[i] = __fmul_rn(__fmul_rn(ld_f(x + i), inv), w[i]);
-    __syncthreads();
-  }
-}
-
 // ----------------------------------------------------------------- GEMVs
-// QKV projection + bias + RoPE + KV append. Warp unit = row pair
-// (rows 2u, 2u+1 of the pair-interleaved wqkv).
+// QKV projection (RMSNorm staged in smem) + bias + RoPE + KV append.
+// Unit = row pair (rows 2u, 2u+1 of the pair-interleaved wqkv).
 template <bool BF16, int G>
-__device__ void ph_qkv(const DModel& m, const DBatch& bt, int l, int cta, int ncta) {
+__device__ void ph_qkv(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   const DLayer& Ly = m.layers[l];
+  prefetch_rows(Ly.wo, m.H, m.QD, BF16, m.H, 1, cta, ncta);  // the O projection comes next
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = m.QKVR / 2;
+  int u0, u1;
+  cta_range(units, cta, ncta, u0, u1);
+  if (u0 >= u1) return;
   const size_t rb = row_bytes(m.H, BF16);
   const int qh = m.QD / 2, kh = m.KVD / 2;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
-    const float* xs[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) xs[g] = bt.xn + (size_t)(b0 + g < bt.B ? b0 + g : b0) * m.H;
-    for (int u = cta * kWarps + warp; u < units; u += ncta * kWarps) {
+    stage_norm<G>(m, bt, b0, Ly.attn_norm, bt.x, smem);
+    for (int u = u0 + warp; u < u1; u += kWarps) {
       const char* base = reinterpret_cast<const char*>(Ly.wqkv);
       const void* rows[2] = {base + (size_t)(2 * u) * rb, base + (size_t)(2 * u + 1) * rb};
       float acc[2][G];
-      warp_dot<BF16, 2, G>(rows, m.H, xs, acc);
+      warp_dot<BF16, true, 2, G>(rows, m.H, smem, m.H, acc);
       int sect, h, i;
       if (u < qh) {
         sect = 0;
@@ -317,23 +721,27 @@ __device__ void ph_qkv(const DModel& m, const DBatch& bt, int l, int cta, int nc
         }
       }
     }
+    __syncthreads();
   }
 }
 
-// x[b] += W x_in[b] (O projection and down projection). Warp unit = row.
+// x[b] += W x_in[b] (O projection, down projection). Unit = row.
 template <bool BF16, int G>
 __device__ void ph_residual_gemv(const DModel& m, const DBatch& bt, const void* W, int K, const float* xin,
-                                 int xin_stride, int cta, int ncta) {
+                                 int cta, int ncta, float* smem, size_t smem_floats) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int u0, u1;
+  cta_range(m.H, cta, ncta, u0, u1);
+  if (u0 >= u1) return;
   const size_t rb = row_bytes(K, BF16);
+  const bool staged = (size_t)G * K <= smem_floats;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
-    const float* xs[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) xs[g] = xin + (size_t)(b0 + g < bt.B ? b0 + g : b0) * xin_stride;
-    for (int r = cta * kWarps + warp; r < m.H; r += ncta * kWarps) {
+    if (staged) stage_copy<G>(bt, b0, xin, K, smem);
+    for (int r = u0 + warp; r < u1; r += kWarps) {
       const void* rows[1] = {reinterpret_cast<const char*>(W) + (size_t)r * rb};
       float acc[1][G];
-      warp_dot<BF16, 1, G>(rows, K, xs, acc);
+      if (staged) warp_dot<BF16, true, 1, G>(rows, K, smem, K, acc);
+      else warp_dot<BF16, false, 1, G>(rows, K, xin + (size_t)b0 * K, K, acc);
 #pragma unroll
       for (int g = 0; g < G; g++) {
         const int b = b0 + g;
@@ -342,24 +750,27 @@ __device__ void ph_residual_gemv(const DModel& m, const DBatch& bt, const void* 
         *x = __fadd_rn(ld_f(x), acc[0][g]);
       }
     }
+    if (staged) __syncthreads();
   }
 }
 
-// gate/up projection + activation * up. Warp unit = j (rows 2j, 2j+1).
+// gate/up projection (RMSNorm staged) + activation * up. Unit = j.
 template <bool BF16, int G>
-__device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int ncta) {
+__device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   const DLayer& Ly = m.layers[l];
+  prefetch_rows(Ly.wdown, m.H, m.FF, BF16, m.H, 1, cta, ncta);  // the down projection comes next
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int u0, u1;
+  cta_range(m.FF, cta, ncta, u0, u1);
+  if (u0 >= u1) return;
   const size_t rb = row_bytes(m.H, BF16);
   for (int b0 = 0; b0 < bt.B; b0 += G) {
-    const float* xs[G];
-#pragma unroll
-    for (int g = 0; g < G; g++) xs[g] = bt.xn + (size_t)(b0 + g < bt.B ? b0 + g : b0) * m.H;
-    for (int j = cta * kWarps + warp; j < m.FF; j += ncta * kWarps) {
+    stage_norm<G>(m, bt, b0, Ly.ffn_norm, bt.x, smem);
+    for (int j = u0 + warp; j < u1; j += kWarps) {
       const char* base = reinterpret_cast<const char*>(Ly.wgu);
       const void* rows[2] = {base + (size_t)(2 * j) * rb, base + (size_t)(2 * j + 1) * rb};
       float acc[2][G];
-      warp_dot<BF16, 2, G>(rows, m.H, xs, acc);
+      warp_dot<BF16, true, 2, G>(rows, m.H, smem, m.H, acc);
 #pragma unroll
       for (int g = 0; g < G; g++) {
         const int b = b0 + g;
@@ -376,49 +787,172 @@ __device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int
         bt.g[(size_t)b * m.FF + j] = __fmul_rn(act, up);
       }
     }
+    __syncthreads();
   }
 }
 
-// logits[b] = head · xn[b]. Warp unit = vocabulary row.
+// Final RMSNorm + lm_head + sampler block statistics. Unit = block of
+// kSBlk vocabulary rows; lane r of the unit's warp ends holding row r.
 template <bool BF16, int G>
-__device__ void ph_head(const DModel& m, const DBatch& bt, int cta, int ncta) {
+__device__ void ph_head(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
+  prefetch_rows(m.layers[0].wqkv, m.QKVR, m.H, BF16, m.QKVR / 2, 2, cta, ncta);  // next step's first phase
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = bt.nblk;
+  int u0, u1;
+  cta_range(nb, cta, ncta, u0, u1);
+  if (u0 >= u1) return;
   const size_t rb = row_bytes(m.H, BF16);
   for (int b0 = 0; b0 < bt.B; b0 += G) {
-    const float* xs[G];
+    stage_norm<G>(m, bt, b0, m.norm, bt.x, smem);
+    for (int k = u0 + warp; k < u1; k += kWarps) {
+      float mine[G];
 #pragma unroll
-    for (int g = 0; g < G; g++) xs[g] = bt.xn + (size_t)(b0 + g < bt.B ? b0 + g : b0) * m.H;
-    for (int r = cta * kWarps + warp; r < m.V; r += ncta * kWarps) {
-      const void* rows[1] = {reinterpret_cast<const char*>(m.head) + (size_t)r * rb};
-      float acc[1][G];
-      warp_dot<BF16, 1, G>(rows, m.H, xs, acc);
+      for (int g = 0; g < G; g++) mine[g] = NAN;
+      for (int r = 0; r < kSBlk; r += 2) {
+        const int row0 = min(k * kSBlk + r, m.V - 1), row1 = min(k * kSBlk + r + 1, m.V - 1);
+        const void* rows[2] = {reinterpret_cast<const char*>(m.head) + (size_t)row0 * rb,
+                               reinterpret_cast<const char*>(m.head) + (size_t)row1 * rb};
+        float acc[2][G];
+        warp_dot<BF16, true, 2, G>(rows, m.H, smem, m.H, acc);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          if (lane == r) mine[g] = acc[0][g];
+          if (lane == r + 1) mine[g] = acc[1][g];
+        }
+      }
+      const int i = k * kSBlk + lane;
+      const bool valid = i < m.V;
 #pragma unroll
       for (int g = 0; g < G; g++) {
         const int b = b0 + g;
-        if (lane != g || b >= bt.B || !ld_i(&bt.st[b].active)) continue;
-        bt.logits[(size_t)b * m.V + r] = acc[0][g];
+        if (b >= bt.B || !ld_i(&bt.st[b].active)) continue;
+        if (valid) bt.logits[(size_t)b * m.V + i] = mine[g];
+        const size_t o = (size_t)b * nb + k;
+        block_stats(mine[g], i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
       }
+    }
+    __syncthreads();
+  }
+}
+
+// A run whose first step samples takes its logits from the previous run;
+// their block statistics are recomputed here before the first SELECT.
+__device__ __forceinline__ bool samples_first(const DBatch& bt, int b) {
+  const DSession& S = bt.sess[b];
+  return S.n_prompt == 0 && S.n_total > 0;
+}
+
+__device__ __forceinline__ bool any_first(const DBatch& bt, bool need_temperature) {
+  for (int b = 0; b < bt.B; b++)
+    if (samples_first(bt, b) && (!need_temperature || bt.sess[b].temperature != 0.0f)) return true;
+  return false;
+}
+
+// Block statistics of the resident logits of every slot whose run starts
+// with a sampling step. Unit = block of kSBlk logits.
+__device__ void ph_restat(const DModel& m, const DBatch& bt, int cta, int ncta) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = bt.nblk;
+  int u0, u1;
+  cta_range(nb, cta, ncta, u0, u1);
+  for (int b = 0; b < bt.B; b++) {
+    if (!samples_first(bt, b)) continue;
+    const float T = bt.sess[b].temperature;
+    const float* lg = bt.logits + (size_t)b * m.V;
+    for (int k = u0 + warp; k < u1; k += kWarps) {
+      const int i = k * kSBlk + lane;
+      const bool valid = i < m.V;
+      const size_t o = (size_t)b * nb + k;
+      block_stats(valid ? ld_f(lg + i) : NAN, i, valid, T, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
     }
   }
 }
 
+// Whether slot b's sampler sums are needed: for the next step (FIRST =
+// false) or for the first step of the run (FIRST = true).
+template <bool FIRST>
+__device__ __forceinline__ bool needs_sums(const DBatch& bt, int b) {
+  if (FIRST) return samples_first(bt, b) && bt.sess[b].temperature != 0.0f;
+  return samples_next(bt, b);
+}
+
+// Block sums of e for slots sampling next (needs the max over all blocks).
+template <bool FIRST>
+__device__ void ph_sample1(const DModel& m, const DBatch& bt, int cta, int ncta) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = bt.nblk;
+  int u0, u1;
+  cta_range(nb, cta, ncta, u0, u1);
+  for (int b = 0; b < bt.B; b++) {
+    if (!needs_sums<FIRST>(bt, b)) continue;
+    const float T = bt.sess[b].temperature;
+    const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
+    const float* lg = bt.logits + (size_t)b * m.V;
+    for (int k = u0 + warp; k < u1; k += kWarps) {
+      const int i = k * kSBlk + lane;
+      const float e = i < m.V ? e_of(ld_f(lg + i), T, M) : 0.0f;
+      const float s = warp_seq_sum(e);
+      if (lane == 0) bt.ss.esum[(size_t)b * nb + k] = s;
+    }
+  }
+}
+
+// Block sums of p = e * (1/Z) for slots sampling next.
+template <bool FIRST>
+__device__ void ph_sample2(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = bt.nblk;
+  const int ng2 = (nb + 31) / 32;
+  int u0, u1;
+  cta_range(nb, cta, ncta, u0, u1);
+  for (int b = 0; b < bt.B; b++) {
+    if (!needs_sums<FIRST>(bt, b)) continue;
+    const float T = bt.sess[b].temperature;
+    const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
+    const float Z = hier_total(bt.ss.esum + (size_t)b * nb, nb, smem, smem + ng2, true);
+    if (!(Z > 0.0f) || !isfinite(Z)) continue;  // SELECT falls back to argmax
+    const float inv = __fdiv_rn(1.0f, Z);
+    const float* lg = bt.logits + (size_t)b * m.V;
+    for (int k = u0 + warp; k < u1; k += kWarps) {
+      const int i = k * kSBlk + lane;
+      const float p = i < m.V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
+      const float s = warp_seq_sum(p);
+      if (lane == 0) bt.ss.psum[(size_t)b * nb + k] = s;
+    }
+  }
+}
+
+// Whether any slot samples at T > 0 next (identical in every CTA).
+__device__ __forceinline__ bool any_sampling(const DBatch& bt) {
+  for (int b = 0; b < bt.B; b++)
+    if (samples_next(bt, b)) return true;
+  return false;
+}
+
 // ------------------------------------------------------------- attention
-// Partial attention of one key chunk for the query heads of one KV head.
-// CTA unit = (slot, kv head, chunk). smem: G*HD + G*kAttnChunk floats.
+// Partial attention of one key chunk for the query heads of one KV head;
+// the CTA finishing the last chunk of a (slot, KV head) combines all its
+// chunks in chunk order. CTA unit = (slot, kv head, chunk).
 __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
+  {  // the gate/up projection comes after the O projection
+    const DLayer& Ly = m.layers[l];
+    prefetch_rows(Ly.wgu, 2 * m.FF, m.H, m.bf16 != 0, m.FF, 2, cta, ncta);
+  }
   const int G = m.NH / m.NKV;
   const int maxc = bt.max_chunks;
   const int units = bt.B * m.NKV * maxc;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* qs = smem;             // [G][HD]
   float* sc = smem + G * m.HD;  // [G][kAttnChunk]
+  __shared__ int s_last;
   for (int u = cta; u < units; u += ncta) {
     const int b = u / (m.NKV * maxc);
     const int rem = u % (m.NKV * maxc);
     const int kvh = rem / maxc, c = rem % maxc;
     if (!ld_i(&bt.st[b].active)) continue;
     const int pos = ld_i(&bt.st[b].pos);
-    if (c > pos / kAttnChunk) continue;
+    const int nch = pos / kAttnChunk + 1;
+    if (c >= nch) continue;
     const DSession& S = bt.sess[b];
     const int t0 = c * kAttnChunk;
     const int tn = min(kAttnChunk, pos + 1 - t0);
@@ -473,263 +1007,40 @@ __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int n
       for (int tt = 0; tt < tn; tt++) acc = fmaf(e[tt], ld_f(vb + (size_t)tt * m.HD + d), acc);
       part_b[((size_t)(kvh * G + h) * maxc + c) * (m.HD + 2) + 2 + d] = acc;
     }
+    // The last chunk of this (slot, KV head) to finish combines; every
+    // writer makes its partials visible GPU-wide before the ticket.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      int* tk = bt.tickets + (size_t)b * m.NKV + kvh;
+      const int done = atomicAdd(tk, 1) + 1;
+      s_last = (done == nch);
+      if (s_last) {
+        __threadfence();
+        *tk = 0;  // ready for the next layer (a barrier separates them)
+      }
+    }
+    __syncthreads();
+    if (s_last) {
+      for (int idx = tid; idx < G * m.HD; idx += kThreads) {
+        const int h = idx / m.HD, d = idx % m.HD;
+        const float* p = part_b + (size_t)(kvh * G + h) * maxc * (m.HD + 2);
+        float M = -INFINITY;
+        for (int cc = 0; cc < nch; cc++) M = fmaxf(M, ld_f(p + (size_t)cc * (m.HD + 2)));
+        float L = 0.0f, O = 0.0f;
+        for (int cc = 0; cc < nch; cc++) {
+          const float* pc = p + (size_t)cc * (m.HD + 2);
+          const float mc = ld_f(pc), lc = ld_f(pc + 1), ac = ld_f(pc + 2 + d);
+          const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
+          L = fmaf(w, lc, L);
+          O = fmaf(w, ac, O);
+        }
+        bt.att[(size_t)b * m.QD + (size_t)(kvh * G + h) * m.HD + d] = __fdiv_rn(O, L);
+      }
+    }
     __syncthreads();
   }
-}
-
-// Combines the chunk partials of one query head in chunk order.
-// CTA unit = (slot, head).
-__device__ void ph_combine(const DModel& m, const DBatch& bt, int cta, int ncta) {
-  const int maxc = bt.max_chunks;
-  for (int u = cta; u < bt.B * m.NH; u += ncta) {
-    const int b = u / m.NH, h = u % m.NH;
-    if (!ld_i(&bt.st[b].active)) continue;
-    const int nch = ld_i(&bt.st[b].pos) / kAttnChunk + 1;
-    const float* p = bt.part + ((size_t)b * m.NH + h) * maxc * (m.HD + 2);
-    const int d = threadIdx.x;
-    if (d >= m.HD) continue;
-    float M = -INFINITY;
-    for (int c = 0; c < nch; c++) M = fmaxf(M, ld_f(p + (size_t)c * (m.HD + 2)));
-    float L = 0.0f, O = 0.0f;
-    for (int c = 0; c < nch; c++) {
-      const float* pc = p + (size_t)c * (m.HD + 2);
-      const float mc = ld_f(pc), lc = ld_f(pc + 1), ac = ld_f(pc + 2 + d);
-      const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
-      L = fmaf(w, lc, L);
-      O = fmaf(w, ac, O);
-    }
-    bt.att[(size_t)b * m.QD + h * m.HD + d] = __fdiv_rn(O, L);
-  }
-}
-
-// --------------------------------------------------------------- sampler
-struct ValIdx {
-  float v;
-  int i;
-};
-
-// b better than a: valid (non-NaN), larger, or equal with a lower index.
-__device__ __forceinline__ bool vi_better(ValIdx b, ValIdx a) {
-  if (b.i == INT_MAX) return false;
-  if (a.i == INT_MAX) return true;
-  return b.v > a.v || (b.v == a.v && b.i < a.i);
-}
-
-__device__ __forceinline__ ValIdx vi_warp_best(ValIdx x) {
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    ValIdx o{__shfl_xor_sync(0xffffffffu, x.v, off), __shfl_xor_sync(0xffffffffu, x.i, off)};
-    if (vi_better(o, x)) x = o;
-  }
-  return x;
-}
-
-// argmax with the reference's rules (sampler.rs:24-40): NaN skipped,
-// strict > so the lowest index wins ties, 0 when every value is NaN.
-__device__ uint32_t argmax_cta(const float* l, int V, float* smem) {
-  ValIdx best{NAN, INT_MAX};
-  for (int i = threadIdx.x; i < V; i += kThreads) {
-    const float v = ld_f(l + i);
-    if (isnan(v)) continue;
-    ValIdx c{v, i};
-    if (vi_better(c, best)) best = c;
-  }
-  best = vi_warp_best(best);
-  float* sv = smem;
-  int* si = reinterpret_cast<int*>(smem + kWarps);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) {
-    sv[warp] = best.v;
-    si[warp] = best.i;
-  }
-  __syncthreads();
-  ValIdx r{NAN, INT_MAX};
-  if (warp == 0) {
-    ValIdx c = lane < kWarps ? ValIdx{sv[lane], si[lane]} : ValIdx{NAN, INT_MAX};
-    r = vi_warp_best(c);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) si[0] = r.i == INT_MAX ? 0 : r.i;
-  __syncthreads();
-  const uint32_t out = (uint32_t)si[0];
-  __syncthreads();
-  return out;
-}
-
-__device__ __forceinline__ float block_max(float v, float* red) {
-  v = warp_max(v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float r = -INFINITY;
-  for (int w = 0; w < kWarps; w++) r = fmaxf(r, red[w]);
-  __syncthreads();
-  return r;
-}
-
-__device__ __forceinline__ int block_max_int(int v, int* red) {
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, off));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  int r = INT_MIN;
-  for (int w = 0; w < kWarps; w++) r = max(r, red[w]);
-  __syncthreads();
-  return r;
-}
-
-// Unnormalised (e) or normalised (p = e * inv) probability of element i.
-__device__ __forceinline__ float prob_at(const float* l, int V, int i, float T, float M, float inv, bool norm) {
-  if (i >= V) return 0.0f;
-  const float s = __fdiv_rn(ld_f(l + i), T);
-  const float e = isnan(s) ? 0.0f : expf(__fsub_rn(s, M));
-  return norm ? __fmul_rn(e, inv) : e;
-}
-
-// Sums of the 256-element blocks (8 per lane, sequential at each level).
-__device__ void block_sums(const float* l, int V, float T, float M, float inv, bool norm, float* bsum, int nblk) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int k = warp; k < nblk; k += kWarps) {
-    const int i0 = k * 256 + lane * 8;
-    float ls = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; e++) ls = __fadd_rn(ls, prob_at(l, V, i0 + e, T, M, inv, norm));
-    float bs = 0.0f;
-    for (int j = 0; j < 32; j++) bs = __fadd_rn(bs, __shfl_sync(0xffffffffu, ls, j));
-    if (lane == 0) bsum[k] = bs;
-  }
-}
-
-// Temperature sampling (sampler.rs:43-109) with the canonical hierarchical
-// sums. Returns the token; *margin = distance of r to the nearest CDF edge
-// of the chosen token (NaN on the degenerate one-hot path, 0 when greedy).
-__device__ uint32_t sample_cta(const float* l, int V, float T, uint32_t word, float* margin, float* smem) {
-  if (T == 0.0f) {
-    *margin = 0.0f;
-    return argmax_cta(l, V, smem);
-  }
-  const int nblk = (V + 255) / 256;
-  const int nsb = (nblk + 31) / 32;
-  float* red = smem;                // [kWarps]
-  float* bsum = smem + 2 * kWarps;  // [nblk]
-  __shared__ float s_total, s_Q, s_R, s_margin;
-  __shared__ int s_k, s_found, s_tok;
-  // max of s = l / T (NaN ignored)
-  float mx = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += kThreads) mx = fmaxf(mx, __fdiv_rn(ld_f(l + i), T));
-  const float M = block_max(mx, red);
-  // total of e
-  block_sums(l, V, T, M, 0.0f, false, bsum, nblk);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float tot = 0.0f;
-    for (int s = 0; s < nsb; s++) {
-      float sb = 0.0f;
-      for (int k = s * 32; k < min(nblk, s * 32 + 32); k++) sb = __fadd_rn(sb, bsum[k]);
-      tot = __fadd_rn(tot, sb);
-    }
-    s_total = tot;
-  }
-  __syncthreads();
-  const float total = s_total;
-  if (!(total > 0.0f) || !isfinite(total)) {
-    *margin = NAN;
-    return argmax_cta(l, V, smem);
-  }
-  const float inv = __fdiv_rn(1.0f, total);
-  // block sums of p and the last index with p > 0
-  block_sums(l, V, T, M, inv, true, bsum, nblk);
-  int last = -1;
-  for (int i = threadIdx.x; i < V; i += kThreads)
-    if (prob_at(l, V, i, T, M, inv, true) > 0.0f) last = i;
-  __syncthreads();
-  last = block_max_int(last, reinterpret_cast<int*>(red));
-  const float r = (float)(word >> 8) * (1.0f / 16777216.0f);
-  if (threadIdx.x == 0) {
-    float Q = 0.0f, R = 0.0f;
-    int found = 0, fk = 0;
-    for (int s = 0; s < nsb && !found; s++) {
-      float sb = 0.0f;
-      for (int k = s * 32; k < min(nblk, s * 32 + 32); k++) sb = __fadd_rn(sb, bsum[k]);
-      const float Qn = __fadd_rn(Q, sb);
-      if (r < Qn) {
-        float Rk = 0.0f;
-        fk = min(nblk, s * 32 + 32) - 1;
-        for (int k = s * 32; k < min(nblk, s * 32 + 32); k++) {
-          const float Rn = __fadd_rn(Rk, bsum[k]);
-          if (r < __fadd_rn(Q, Rn)) {
-            fk = k;
-            break;
-          }
-          Rk = Rn;
-        }
-        R = Rk;
-        found = 1;
-        break;
-      }
-      Q = Qn;
-    }
-    s_found = found;
-    s_k = fk;
-    s_Q = Q;
-    s_R = R;
-  }
-  __syncthreads();
-  if (!s_found) {
-    // r at or beyond the rounded CDF total: the last non-zero token
-    // (sampler.rs:106-108).
-    *margin = __fsub_rn(r, s_Q);
-    const uint32_t result = (uint32_t)(last < 0 ? 0 : last);
-    __syncthreads();
-    return result;
-  }
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    const int i0 = s_k * 256 + lane * 8;
-    float pv[8];
-    float ls = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-      pv[e] = prob_at(l, V, i0 + e, T, M, inv, true);
-      ls = __fadd_rn(ls, pv[e]);
-    }
-    float S = 0.0f;  // sequential prefix of the lane sums before this lane
-    for (int j = 0; j < 32; j++) {
-      const float o = __shfl_sync(0xffffffffu, ls, j);
-      if (j < lane) S = __fadd_rn(S, o);
-    }
-    const float Q = s_Q, R = s_R;
-    const float lane_end = __fadd_rn(Q, __fadd_rn(R, __fadd_rn(S, ls)));
-    const unsigned hit = __ballot_sync(0xffffffffu, r < lane_end);
-    const int j = hit ? __ffs(hit) - 1 : 31;
-    if (lane == j) {
-      float t = 0.0f;
-      float prev = __fadd_rn(Q, __fadd_rn(R, S));
-      int tok = min(i0 + 7, V - 1);
-      float mg = 0.0f;
-      for (int e = 0; e < 8; e++) {
-        t = __fadd_rn(t, pv[e]);
-        const float cum = __fadd_rn(Q, __fadd_rn(R, __fadd_rn(S, t)));
-        if (r < cum) {
-          tok = i0 + e;
-          mg = fminf(__fsub_rn(cum, r), __fsub_rn(r, prev));
-          break;
-        }
-        prev = cum;
-      }
-      s_tok = tok;
-      s_margin = mg;
-    }
-  }
-  __syncthreads();
-  const uint32_t result = (uint32_t)s_tok;
-  *margin = s_margin;
-  __syncthreads();
-  return result;
 }
 
 }  // namespace defer
