@@ -6,6 +6,7 @@
 #include <cstring>
 
 #include "common.h"
+#include "flow.h"
 #include "kernels.h"
 
 namespace defer {
@@ -13,6 +14,13 @@ namespace defer {
 bool use_persistent() {
   const char* e = getenv("DEFER_B200_PHASED");
   return !(e && e[0] == '1');
+}
+
+int loop_mode() {
+  const char* e = getenv("DEFER_B200_LOOP");
+  if (e && strcmp(e, "barrier") == 0) return 0;
+  if (e && strcmp(e, "flow") == 0) return 2;
+  return 1;
 }
 
 static uint64_t words_per_sample(float t) { return t == 0.0f ? 0 : 1; }
@@ -36,6 +44,11 @@ Runner::Runner(const Model* m, int B, int max_cap) : m_(m), B_(B), max_cap_(max_
   DEFER_CUDA(cudaMalloc(&d_sess_, sizeof(DSession) * B));
   DEFER_CUDA(cudaMalloc(&d_state_, sizeof(DSlotState) * B));
   DEFER_CUDA(cudaMalloc(&d_ctrl_, 8 * sizeof(int)));
+  if (B <= kMaxGroup) {
+    flow_n_ = flow_tagged_words(d, B, max_chunks_, m->sms);
+    DEFER_CUDA(cudaMalloc(&flow_words_, flow_n_ * sizeof(uint64_t)));
+    DEFER_CUDA(cudaMemset(flow_words_, 0, flow_n_ * sizeof(uint64_t)));
+  }
   DEFER_CUDA(cudaEventCreate(&ev_start_));
   DEFER_CUDA(cudaEventCreate(&ev_stop_));
 }
@@ -52,6 +65,7 @@ Runner::~Runner() {
   cudaFree(d_sess_);
   cudaFree(d_state_);
   cudaFree(d_ctrl_);
+  if (flow_words_) cudaFree(flow_words_);
   if (d_scratch_) cudaFree(d_scratch_);
   if (ev_start_) cudaEventDestroy(ev_start_);
   if (ev_stop_) cudaEventDestroy(ev_stop_);
@@ -158,8 +172,27 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   bt.bar = reinterpret_cast<unsigned*>(d_ctrl_ + 3);
   last_steps_ = nsteps;
   const bool persistent = use_persistent();
+  FlowPlan plan;
+  const int mode = persistent ? loop_mode() : 0;
+  if (mode && flow_words_) plan = flow_plan(m_->dm, n, max_chunks_, m_->sms);
+  if (mode == 2 && !plan.ok)
+    fail(kInvalidArgument, std::string("the dataflow token loop does not apply: ") +
+                               (flow_words_ ? plan.why : "batch wider than its slot group"));
+  FlowBufs fb{};
+  if (plan.ok) {
+    const uint64_t need = flow_tags_per_run(m_->dm, nsteps);
+    if (flow_epoch_ + need >= 0xFFFFFF00ull) {
+      // tags would wrap: clear every tagged word and start again
+      DEFER_CUDA(cudaMemsetAsync(flow_words_, 0, flow_n_ * sizeof(uint64_t), st));
+      flow_epoch_ = 1;
+    }
+    fb = flow_bufs(m_->dm, B_, max_chunks_, m_->sms, flow_words_);
+    fb.epoch = (uint32_t)flow_epoch_;
+    flow_epoch_ += need;
+  }
   DEFER_CUDA(cudaEventRecord(ev_start_, st));
-  if (persistent) launch_steps_persistent(m_->dm, bt, nsteps, m_->sms, st);
+  if (plan.ok) launch_steps_flow(m_->dm, bt, fb, plan, nsteps, st);
+  else if (persistent) launch_steps_persistent(m_->dm, bt, nsteps, m_->sms, st);
   else launch_steps_phased(m_->dm, m_->host_layers.data(), bt, 0, nsteps, m_->sms, st);
   DEFER_CUDA(cudaGetLastError());
   DEFER_CUDA(cudaEventRecord(ev_stop_, st));
@@ -204,7 +237,7 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   m_->t_launches += persistent ? 1 : (uint64_t)nsteps * (uint64_t)launches_per_step_phased(d) + 1;
   m_->t_tokens += tokens;
   m_->t_bytes += bytes;
-  if (ctrl[0] == kStTimeout) fail(kDeviceTimeout, "a grid barrier of the token loop timed out");
+  if (ctrl[0] == kStTimeout) fail(kDeviceTimeout, "a bounded wait of the token loop timed out");
   if (ctrl[0] == kStBadToken) fail(kModel, "token id out of range");
   if (ctrl[0] == kStContext) fail(kModel, "context length " + std::to_string(m_->cfg.max_seq_len) + " exceeded");
 }

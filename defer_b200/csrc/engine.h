@@ -59,13 +59,21 @@ class Runner {
   int* d_ctrl_ = nullptr;  // status, any_active[2], barrier counter
   uint32_t* d_scratch_ = nullptr;
   size_t scratch_words_ = 0;
+  uint64_t* flow_words_ = nullptr;  // tagged buffers of the dataflow kernel (B <= 8)
+  size_t flow_n_ = 0;
+  uint64_t flow_epoch_ = 1;         // first tag of the next run
   int last_steps_ = 0;
   cudaEvent_t ev_start_ = nullptr, ev_stop_ = nullptr;
 };
 
-// Whether runs use the persistent kernel (default) or one launch per phase
+// Whether runs use a persistent kernel (default) or one launch per phase
 // (DEFER_B200_PHASED=1).
 bool use_persistent();
+// Among the persistent kernels: 1 = the dataflow kernel where it applies,
+// else the grid-barrier kernel (default); 0 = always the grid-barrier
+// kernel (DEFER_B200_LOOP=barrier); 2 = the dataflow kernel or an error
+// (DEFER_B200_LOOP=flow).
+int loop_mode();
 
 class Session {
  public:

@@ -1,5 +1,6 @@
 // Phase functions of one token step (see device.cuh for the arithmetic
-// contract). Included by kernels.cu only.
+// contract). Included by kernels.cu (phase and grid-barrier kernels) and by
+// flow.cu (dataflow kernel), each its own device module.
 //
 // A step is: SELECT (choose this step's token per slot, write the embedding
 // row) | per layer: QKV (RMSNorm + projection + RoPE + KV append) | ATTN
@@ -16,7 +17,21 @@
 
 #include "device.cuh"
 
+// CTA-wide barrier of the phase code. A kernel whose CTAs hold threads that
+// do not run the phases (a weight-producer warp) defines it, before
+// including this header, as a named barrier over the kThreads phase threads.
+#ifndef DEFER_CTA_SYNC
+#define DEFER_CTA_SYNC() __syncthreads()
+#endif
+// Threads that run the phase code in each CTA (a multiple of 32).
+#ifndef DEFER_PHASE_THREADS
+#define DEFER_PHASE_THREADS 256
+#endif
+
 namespace defer {
+
+constexpr int kPT = DEFER_PHASE_THREADS;  // phase threads per CTA
+constexpr int kPW = kPT / 32;             // phase warps per CTA
 
 // ----------------------------------------------------------- primitives
 // Weights never change while a kernel runs: streamed through the
@@ -205,31 +220,31 @@ __device__ void stage_norm(const DModel& m, const DBatch& bt, int b0, const floa
     acc = warp_sum_butterfly(acc);
     if (lane == 0) s_inv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)m.H), m.eps)));
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   for (int g = 0; g < G; g++) {
     const int b = b0 + g;
     const bool live = b < bt.B && ld_i(&bt.st[b].active);
     const float inv = s_inv[g];
     const float* xb = x + (size_t)(live ? b : 0) * m.H;
-    for (int i = threadIdx.x; i < m.H; i += kThreads)
+    for (int i = threadIdx.x; i < m.H; i += kPT)
       dst[(size_t)g * m.H + i] = live ? __fmul_rn(__fmul_rn(ld_f(xb + i), inv), w_of_layer[i]) : 0.0f;
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
 }
 
 // Copies slot activations [b0, b0+G) (stride K) into shared memory.
 template <int G>
-__device__ void stage_copy(const DBatch& bt, int b0, const float* src, int K, float* dst) {
+static __device__ void stage_copy(const DBatch& bt, int b0, const float* src, int K, float* dst) {
   for (int g = 0; g < G; g++) {
     const int b = b0 + g;
     const bool live = b < bt.B;
     const float* s = src + (size_t)(live ? b : 0) * K;
-    for (int i = threadIdx.x * 4; i < K; i += kThreads * 4) {
+    for (int i = threadIdx.x * 4; i < K; i += kPT * 4) {
       float4 v = live ? ld_act(s + i) : make_float4(0.f, 0.f, 0.f, 0.f);
       *reinterpret_cast<float4*>(dst + (size_t)g * K + i) = v;
     }
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
 }
 
 // --------------------------------------------------------------- sampler
@@ -290,21 +305,21 @@ __device__ __forceinline__ float seq_sum32(const float* a, int k0, int n, bool g
 // Hierarchical totals of block sums `bs[0..nblk)` into smem:
 // g2[nblk/32 groups], g3[groups/32 supergroups]; returns the total (all
 // threads). Sequential at every level.
-__device__ float hier_total(const float* bs, int nblk, float* g2, float* g3, bool global_src) {
+static __device__ float hier_total(const float* bs, int nblk, float* g2, float* g3, bool global_src) {
   const int ng2 = (nblk + 31) / 32, ng3 = (ng2 + 31) / 32;
   __shared__ float s_tot;
-  for (int t = threadIdx.x; t < ng2; t += kThreads) g2[t] = seq_sum32(bs, t * 32, nblk, global_src);
-  __syncthreads();
-  for (int t = threadIdx.x; t < ng3; t += kThreads) g3[t] = seq_sum32(g2, t * 32, ng2, false);
-  __syncthreads();
+  for (int t = threadIdx.x; t < ng2; t += kPT) g2[t] = seq_sum32(bs, t * 32, nblk, global_src);
+  DEFER_CTA_SYNC();
+  for (int t = threadIdx.x; t < ng3; t += kPT) g3[t] = seq_sum32(g2, t * 32, ng2, false);
+  DEFER_CTA_SYNC();
   if (threadIdx.x == 0) {
     float s = 0.0f;
     for (int k = 0; k < ng3; k++) s = __fadd_rn(s, g3[k]);
     s_tot = s;
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   const float r = s_tot;
-  __syncthreads();
+  DEFER_CTA_SYNC();
   return r;
 }
 
@@ -312,7 +327,7 @@ __device__ float hier_total(const float* bs, int nblk, float* g2, float* g3, boo
 // `lg` holds the slot's logits (global). Returns the token; *margin = distance
 // of r to the nearest edge of the chosen token's CDF interval. smem needs
 // ng2 + ng3 floats. Whole CTA.
-__device__ uint32_t cdf_find(const float* lg, int V, const float* psum, bool global_src, int nblk, float T, float M,
+static __device__ uint32_t cdf_find(const float* lg, int V, const float* psum, bool global_src, int nblk, float T, float M,
                              float inv, float r, float* margin, float* smem) {
   const int ng2 = (nblk + 31) / 32, ng3 = (ng2 + 31) / 32;
   float* g2 = smem;
@@ -350,7 +365,7 @@ __device__ uint32_t cdf_find(const float* lg, int V, const float* psum, bool glo
     s_Q2 = Q2f;
     s_base = Q3;  // when not found: the CDF total
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   if (threadIdx.x < 32) {
     // block search inside the group (warp 0), and the last block with p > 0
     const int lane = threadIdx.x;
@@ -381,7 +396,7 @@ __device__ uint32_t cdf_find(const float* lg, int V, const float* psum, bool glo
     }
     if (lane == 0) s_last = lastb;
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   uint32_t tok;
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
@@ -426,58 +441,58 @@ __device__ uint32_t cdf_find(const float* lg, int V, const float* psum, bool glo
       }
     }
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   tok = (uint32_t)s_tok;
   *margin = s_margin;
-  __syncthreads();
+  DEFER_CTA_SYNC();
   return tok;
 }
 
 // Greedy choice from the block statistics (exact).
-__device__ uint32_t argmax_from_blocks(const float* lmax, const int* larg, int nblk, bool global_src) {
+static __device__ uint32_t argmax_from_blocks(const float* lmax, const int* larg, int nblk, bool global_src) {
   ValIdx best{NAN, INT_MAX};
-  for (int k = threadIdx.x; k < nblk; k += kThreads) {
+  for (int k = threadIdx.x; k < nblk; k += kPT) {
     ValIdx c{global_src ? ld_f(lmax + k) : lmax[k], global_src ? ld_i(larg + k) : larg[k]};
     if (vi_better(c, best)) best = c;
   }
   best = vi_warp_best(best);
-  __shared__ float s_v[kWarps];
-  __shared__ int s_i[kWarps];
+  __shared__ float s_v[kPW];
+  __shared__ int s_i[kPW];
   __shared__ int s_res;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
     s_v[warp] = best.v;
     s_i[warp] = best.i;
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   if (warp == 0) {
-    ValIdx c = lane < kWarps ? ValIdx{s_v[lane], s_i[lane]} : ValIdx{NAN, INT_MAX};
+    ValIdx c = lane < kPW ? ValIdx{s_v[lane], s_i[lane]} : ValIdx{NAN, INT_MAX};
     c = vi_warp_best(c);
     if (lane == 0) s_res = c.i == INT_MAX ? 0 : c.i;
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   const uint32_t r = (uint32_t)s_res;
-  __syncthreads();
+  DEFER_CTA_SYNC();
   return r;
 }
 
-__device__ float max_of(const float* a, int n, bool global_src) {
+static __device__ float max_of(const float* a, int n, bool global_src) {
   float v = -INFINITY;
-  for (int k = threadIdx.x; k < n; k += kThreads) v = fmaxf(v, global_src ? ld_f(a + k) : a[k]);
+  for (int k = threadIdx.x; k < n; k += kPT) v = fmaxf(v, global_src ? ld_f(a + k) : a[k]);
   v = warp_max(v);
-  __shared__ float s_m[kWarps];
+  __shared__ float s_m[kPW];
   if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = v;
-  __syncthreads();
+  DEFER_CTA_SYNC();
   float r = -INFINITY;
-  for (int w = 0; w < kWarps; w++) r = fmaxf(r, s_m[w]);
-  __syncthreads();
+  for (int w = 0; w < kPW; w++) r = fmaxf(r, s_m[w]);
+  DEFER_CTA_SYNC();
   return r;
 }
 
 // Whole sampler on one logits vector by one CTA (same arithmetic as the
 // distributed path: the block statistics and sums are computed here).
 // smem: 5 * nblk + ng2 + ng3 floats.
-__device__ uint32_t sample_cta(const float* lg, int V, float T, uint32_t word, float* margin, float* smem) {
+static __device__ uint32_t sample_cta(const float* lg, int V, float T, uint32_t word, float* margin, float* smem) {
   const int nblk = (V + kSBlk - 1) / kSBlk;
   float* lmax = smem;
   int* larg = reinterpret_cast<int*>(smem + nblk);
@@ -486,38 +501,38 @@ __device__ uint32_t sample_cta(const float* lg, int V, float T, uint32_t word, f
   float* psum = smem + 4 * nblk;
   float* tail = smem + 5 * nblk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int k = warp; k < nblk; k += kWarps) {
+  for (int k = warp; k < nblk; k += kPW) {
     const int i = k * kSBlk + lane;
     const bool valid = i < V;
     const float l = valid ? ld_f(lg + i) : NAN;
     block_stats(l, i, valid, T, lmax + k, larg + k, smax + k);
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   if (T == 0.0f) {
     *margin = 0.0f;
     return argmax_from_blocks(lmax, larg, nblk, false);
   }
   const float M = max_of(smax, nblk, false);
-  for (int k = warp; k < nblk; k += kWarps) {
+  for (int k = warp; k < nblk; k += kPW) {
     const int i = k * kSBlk + lane;
     const float e = i < V ? e_of(ld_f(lg + i), T, M) : 0.0f;
     const float s = warp_seq_sum(e);
     if (lane == 0) esum[k] = s;
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   const float Z = hier_total(esum, nblk, tail, tail + (nblk + 31) / 32, false);
   if (!(Z > 0.0f) || !isfinite(Z)) {
     *margin = NAN;
     return argmax_from_blocks(lmax, larg, nblk, false);
   }
   const float inv = __fdiv_rn(1.0f, Z);
-  for (int k = warp; k < nblk; k += kWarps) {
+  for (int k = warp; k < nblk; k += kPW) {
     const int i = k * kSBlk + lane;
     const float p = i < V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
     const float s = warp_seq_sum(p);
     if (lane == 0) psum[k] = s;
   }
-  __syncthreads();
+  DEFER_CTA_SYNC();
   const float r = (float)(word >> 8) * (1.0f / 16777216.0f);
   return cdf_find(lg, V, psum, false, nblk, T, M, inv, r, margin, tail);
 }
@@ -558,9 +573,9 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
       s_go = !st->done;
       s_step = st->step;
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
     if (!s_go) {
-      __syncthreads();
+      DEFER_CTA_SYNC();
       continue;
     }
     const int s = s_step;
@@ -625,24 +640,24 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
         }
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
     const uint32_t t = s_tok;
     if (t != 0xFFFFFFFFu) {
       float* x = bt.x + (size_t)b * m.H;
       if (BF16) {
         const uint16_t* e = reinterpret_cast<const uint16_t*>(m.embed) + (size_t)t * m.H;
-        for (int i = tid; i < m.H; i += kThreads) x[i] = __uint_as_float((uint32_t)e[i] << 16);
+        for (int i = tid; i < m.H; i += kPT) x[i] = __uint_as_float((uint32_t)e[i] << 16);
       } else {
         const float* e = reinterpret_cast<const float*>(m.embed) + (size_t)t * m.H;
-        for (int i = tid; i < m.H; i += kThreads) x[i] = e[i];
+        for (int i = tid; i < m.H; i += kPT) x[i] = e[i];
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
   }
 }
 
 // Slots that fed in the last step of a run advance their position.
-__device__ void ph_finalize(const DBatch& bt, int cta, int ncta) {
+static __device__ void ph_finalize(const DBatch& bt, int cta, int ncta) {
   if (threadIdx.x != 0) return;
   for (int b = cta; b < bt.B; b += ncta) {
     DSlotState* st = bt.st + b;
@@ -672,7 +687,7 @@ __device__ void ph_qkv(const DModel& m, const DBatch& bt, int l, int cta, int nc
   const int qh = m.QD / 2, kh = m.KVD / 2;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
     stage_norm<G>(m, bt, b0, Ly.attn_norm, bt.x, smem);
-    for (int u = u0 + warp; u < u1; u += kWarps) {
+    for (int u = u0 + warp; u < u1; u += kPW) {
       const char* base = reinterpret_cast<const char*>(Ly.wqkv);
       const void* rows[2] = {base + (size_t)(2 * u) * rb, base + (size_t)(2 * u + 1) * rb};
       float acc[2][G];
@@ -721,7 +736,7 @@ __device__ void ph_qkv(const DModel& m, const DBatch& bt, int l, int cta, int nc
         }
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
   }
 }
 
@@ -737,7 +752,7 @@ __device__ void ph_residual_gemv(const DModel& m, const DBatch& bt, const void* 
   const bool staged = (size_t)G * K <= smem_floats;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
     if (staged) stage_copy<G>(bt, b0, xin, K, smem);
-    for (int r = u0 + warp; r < u1; r += kWarps) {
+    for (int r = u0 + warp; r < u1; r += kPW) {
       const void* rows[1] = {reinterpret_cast<const char*>(W) + (size_t)r * rb};
       float acc[1][G];
       if (staged) warp_dot<BF16, true, 1, G>(rows, K, smem, K, acc);
@@ -750,7 +765,7 @@ __device__ void ph_residual_gemv(const DModel& m, const DBatch& bt, const void* 
         *x = __fadd_rn(ld_f(x), acc[0][g]);
       }
     }
-    if (staged) __syncthreads();
+    if (staged) DEFER_CTA_SYNC();
   }
 }
 
@@ -766,7 +781,7 @@ __device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int
   const size_t rb = row_bytes(m.H, BF16);
   for (int b0 = 0; b0 < bt.B; b0 += G) {
     stage_norm<G>(m, bt, b0, Ly.ffn_norm, bt.x, smem);
-    for (int j = u0 + warp; j < u1; j += kWarps) {
+    for (int j = u0 + warp; j < u1; j += kPW) {
       const char* base = reinterpret_cast<const char*>(Ly.wgu);
       const void* rows[2] = {base + (size_t)(2 * j) * rb, base + (size_t)(2 * j + 1) * rb};
       float acc[2][G];
@@ -787,7 +802,7 @@ __device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int
         bt.g[(size_t)b * m.FF + j] = __fmul_rn(act, up);
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
   }
 }
 
@@ -804,7 +819,7 @@ __device__ void ph_head(const DModel& m, const DBatch& bt, int cta, int ncta, fl
   const size_t rb = row_bytes(m.H, BF16);
   for (int b0 = 0; b0 < bt.B; b0 += G) {
     stage_norm<G>(m, bt, b0, m.norm, bt.x, smem);
-    for (int k = u0 + warp; k < u1; k += kWarps) {
+    for (int k = u0 + warp; k < u1; k += kPW) {
       float mine[G];
 #pragma unroll
       for (int g = 0; g < G; g++) mine[g] = NAN;
@@ -831,7 +846,7 @@ __device__ void ph_head(const DModel& m, const DBatch& bt, int cta, int ncta, fl
         block_stats(mine[g], i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
   }
 }
 
@@ -850,7 +865,7 @@ __device__ __forceinline__ bool any_first(const DBatch& bt, bool need_temperatur
 
 // Block statistics of the resident logits of every slot whose run starts
 // with a sampling step. Unit = block of kSBlk logits.
-__device__ void ph_restat(const DModel& m, const DBatch& bt, int cta, int ncta) {
+static __device__ void ph_restat(const DModel& m, const DBatch& bt, int cta, int ncta) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = bt.nblk;
   int u0, u1;
@@ -859,7 +874,7 @@ __device__ void ph_restat(const DModel& m, const DBatch& bt, int cta, int ncta) 
     if (!samples_first(bt, b)) continue;
     const float T = bt.sess[b].temperature;
     const float* lg = bt.logits + (size_t)b * m.V;
-    for (int k = u0 + warp; k < u1; k += kWarps) {
+    for (int k = u0 + warp; k < u1; k += kPW) {
       const int i = k * kSBlk + lane;
       const bool valid = i < m.V;
       const size_t o = (size_t)b * nb + k;
@@ -888,7 +903,7 @@ __device__ void ph_sample1(const DModel& m, const DBatch& bt, int cta, int ncta)
     const float T = bt.sess[b].temperature;
     const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
     const float* lg = bt.logits + (size_t)b * m.V;
-    for (int k = u0 + warp; k < u1; k += kWarps) {
+    for (int k = u0 + warp; k < u1; k += kPW) {
       const int i = k * kSBlk + lane;
       const float e = i < m.V ? e_of(ld_f(lg + i), T, M) : 0.0f;
       const float s = warp_seq_sum(e);
@@ -913,7 +928,7 @@ __device__ void ph_sample2(const DModel& m, const DBatch& bt, int cta, int ncta,
     if (!(Z > 0.0f) || !isfinite(Z)) continue;  // SELECT falls back to argmax
     const float inv = __fdiv_rn(1.0f, Z);
     const float* lg = bt.logits + (size_t)b * m.V;
-    for (int k = u0 + warp; k < u1; k += kWarps) {
+    for (int k = u0 + warp; k < u1; k += kPW) {
       const int i = k * kSBlk + lane;
       const float p = i < m.V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
       const float s = warp_seq_sum(p);
@@ -933,7 +948,7 @@ __device__ __forceinline__ bool any_sampling(const DBatch& bt) {
 // Partial attention of one key chunk for the query heads of one KV head;
 // the CTA finishing the last chunk of a (slot, KV head) combines all its
 // chunks in chunk order. CTA unit = (slot, kv head, chunk).
-__device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
+static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   {  // the gate/up projection comes after the O projection
     const DLayer& Ly = m.layers[l];
     prefetch_rows(Ly.wgu, 2 * m.FF, m.H, m.bf16 != 0, m.FF, 2, cta, ncta);
@@ -957,11 +972,11 @@ __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int n
     const int t0 = c * kAttnChunk;
     const int tn = min(kAttnChunk, pos + 1 - t0);
     const float* qsrc = bt.q + (size_t)b * m.QD + (size_t)kvh * G * m.HD;
-    for (int i = tid; i < G * m.HD; i += kThreads) qs[i] = ld_f(qsrc + i);
-    __syncthreads();
+    for (int i = tid; i < G * m.HD; i += kPT) qs[i] = ld_f(qsrc + i);
+    DEFER_CTA_SYNC();
     const size_t head_base = ((size_t)l * m.NKV + kvh) * S.cap;
     const float* kb = S.kc + (head_base + t0) * m.HD;
-    for (int idx = tid; idx < G * kAttnChunk; idx += kThreads) {
+    for (int idx = tid; idx < G * kAttnChunk; idx += kPT) {
       const int h = idx / kAttnChunk, tt = idx % kAttnChunk;
       float s = -INFINITY;
       const int t = t0 + tt;
@@ -981,9 +996,9 @@ __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int n
       }
       sc[idx] = s;
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
     float* part_b = bt.part + (size_t)b * m.NH * maxc * (m.HD + 2);
-    for (int h = warp; h < G; h += kWarps) {
+    for (int h = warp; h < G; h += kPW) {
       float* row = sc + h * kAttnChunk;
       const float v0 = row[lane], v1 = row[lane + 32];
       const float mx = warp_max(fmaxf(v0, v1));
@@ -998,9 +1013,9 @@ __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int n
         p[1] = ls;
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
     const float* vb = S.vc + (head_base + t0) * m.HD;
-    for (int idx = tid; idx < G * m.HD; idx += kThreads) {
+    for (int idx = tid; idx < G * m.HD; idx += kPT) {
       const int h = idx / m.HD, d = idx % m.HD;
       const float* e = sc + h * kAttnChunk;
       float acc = 0.0f;
@@ -1010,7 +1025,7 @@ __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int n
     // The last chunk of this (slot, KV head) to finish combines; every
     // writer makes its partials visible GPU-wide before the ticket.
     __threadfence();
-    __syncthreads();
+    DEFER_CTA_SYNC();
     if (tid == 0) {
       __threadfence();
       int* tk = bt.tickets + (size_t)b * m.NKV + kvh;
@@ -1021,9 +1036,9 @@ __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int n
         *tk = 0;  // ready for the next layer (a barrier separates them)
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
     if (s_last) {
-      for (int idx = tid; idx < G * m.HD; idx += kThreads) {
+      for (int idx = tid; idx < G * m.HD; idx += kPT) {
         const int h = idx / m.HD, d = idx % m.HD;
         const float* p = part_b + (size_t)(kvh * G + h) * maxc * (m.HD + 2);
         float M = -INFINITY;
@@ -1039,7 +1054,7 @@ __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int n
         bt.att[(size_t)b * m.QD + (size_t)(kvh * G + h) * m.HD + d] = __fdiv_rn(O, L);
       }
     }
-    __syncthreads();
+    DEFER_CTA_SYNC();
   }
 }
 

@@ -1,7 +1,8 @@
 """Parity of the CUDA path against the CPU oracle through the C ABI:
 forward logits and KV entries at the contract tolerance, token streams,
-the device sampler on crafted logits, and bit-identity between the
-persistent token loop and the one-launch-per-phase path."""
+the device sampler on crafted logits, and bit-identity between the three
+token-loop paths (dataflow kernel, grid-barrier kernel, one launch per
+phase)."""
 import os
 
 import numpy as np
@@ -59,21 +60,66 @@ def test_masked_forward_matches_oracle(mdir):
         assert gm.forward(t, c1).tobytes() == gm.forward_ext(t, c2, []).tobytes()
 
 
-def test_persistent_and_phased_paths_are_bit_identical(mdir):
-    path = model_file(mdir, "test-small")
+# The three token-loop paths: the dataflow kernel (required), the
+# grid-barrier persistent kernel, and one launch per phase.
+PATHS = {"flow": {"DEFER_B200_LOOP": "flow"},
+         "barrier": {"DEFER_B200_LOOP": "barrier"},
+         "phased": {"DEFER_B200_PHASED": "1"}}
+
+
+def _on_path(path, fn):
+    keys = ("DEFER_B200_LOOP", "DEFER_B200_PHASED")
+    old = {k: os.environ.pop(k, None) for k in keys}
+    os.environ.update(PATHS[path])
+    try:
+        return fn()
+    finally:
+        for k in keys:
+            os.environ.pop(k, None)
+            if old[k] is not None:
+                os.environ[k] = old[k]
+
+
+@pytest.mark.parametrize("name,t", [("test-small", 0.8), ("test-gqa4", 0.0), ("test-bf16", 1.0), ("tiny", 0.7)])
+def test_token_loop_paths_are_bit_identical(mdir, name, t):
+    path = model_file(mdir, name)
     gm = D.Model.load(path)
-    toks = _tokens(gm.config.vocab_size, 80, 3)
-    outs = []
-    for phased in ("0", "1"):
-        os.environ["DEFER_B200_PHASED"] = phased
-        try:
-            s = D.Session(gm, D.seed_from_u64(9), 0.8)
-            s.prompt(toks)
-            gen = s.generate(40)
-            outs.append((gen, s.last_logits().tobytes(), s.cache().fingerprint()))
-        finally:
-            os.environ.pop("DEFER_B200_PHASED", None)
-    assert outs[0] == outs[1]
+    toks = _tokens(gm.config.vocab_size, 80, 3)  # crosses an attention chunk
+
+    def run():
+        s = D.Session(gm, D.seed_from_u64(9), t)
+        s.prompt(toks)
+        gen = s.generate(40)
+        return gen, s.last_logits().tobytes(), s.cache().fingerprint()
+
+    outs = {p: _on_path(p, run) for p in PATHS}
+    assert outs["flow"] == outs["barrier"] == outs["phased"]
+
+
+def test_token_loop_paths_agree_on_a_batch(mdir):
+    """Slot groups of 3 sessions (one group of 4 slots) with different
+    prompts, temperatures and lengths: every path gives the same tokens."""
+    gm = D.Model.load(model_file(mdir, "test-gqa4"))
+    prompts = [_tokens(gm.config.vocab_size, n, 10 + n) for n in (5, 70, 33)]
+    seeds = [D.seed_from_u64(i) for i in range(3)]
+    temps, maxt = [0.0, 0.9, 1.3], [30, 12, 25]
+    outs = {p: _on_path(p, lambda: D.generate_batch(gm, prompts, seeds, temps, maxt)[0]) for p in PATHS}
+    assert outs["flow"] == outs["barrier"] == outs["phased"]
+
+
+def test_token_loop_paths_agree_on_benchmark_shape(mdir):
+    """The 135M shape across all SMs: the dataflow and grid-barrier kernels
+    give the same sampled stream, logits and cache bits."""
+    gm = D.Model.load(model_file(mdir, "smollm2-135m"))
+    toks = _tokens(gm.config.vocab_size, 66, 5)
+
+    def run():
+        s = D.Session(gm, D.seed_from_u64(42), 0.7)
+        s.prompt(toks)
+        gen = s.generate(24)
+        return gen, s.last_logits().tobytes(), s.cache().fingerprint()
+
+    assert _on_path("flow", run) == _on_path("barrier", run)
 
 
 # ------------------------------------------------------------------ sampler
