@@ -31,14 +31,17 @@
 // when their inputs arrive.
 //
 // The two plain (untagged) buffers read across CTAs:
-//  * KV cache: the thread appending (K, V) of a (head, dim pair) executes
-//    fence.acq_rel.gpu before its stores of each step, which orders its
-//    appends of earlier steps before its tagged new-k/v words of this step;
-//    an attention unit polls those words and fences before loading the cache.
-//  * logits: every p-sum writer executes fence.acq_rel.gpu (after CTA
+//  * KV cache: after its QKV stage appended K/V rows, every thread of an
+//    appending CTA executes fence.release.gpu at the start of its O stage
+//    (after the attention stage's CTA barriers), so every later tagged word
+//    of that CTA releases the appends. Every CTA owns gate/up rows, whose
+//    words every CTA polls in its down stage; a fence.acquire.gpu after the
+//    next QKV poll then acquires all appends of earlier steps, and attention
+//    loads the cached rows before (and while) the new q/k/v are polled.
+//  * logits: every p-sum writer executes fence.release.gpu (after CTA
 //    barriers that follow the logits stores) before storing its p-sums; the
-//    select phase polls the p-sums and fences before it reads the chosen
-//    block's logits.
+//    select phase polls the p-sums, fences (acquire) and then reads the
+//    chosen block's logits.
 //
 // Every wait is bounded: a poll or mbarrier wait past its limit, or one that
 // sees another CTA's failure in the status word, marks the CTA failed; its
@@ -67,8 +70,9 @@ constexpr int kProducerWarp = kPW;       // the weight producer
 constexpr int kFlowThreads = kPT + 32;
 constexpr int kMaxRing = 8;
 constexpr int kPollBatch = 5;    // words one thread has in flight per poll round (more spills registers)
+constexpr int kCombineBatch = 10;  // the same for the attention combine (its poll site holds little else)
 constexpr int kNormRegs = 19;    // norm weights held per thread (H <= 19 * 224 = 4256)
-constexpr int kKvBatch = 4;      // float4 K (and V) loads one thread has in flight
+constexpr int kKvBatch = 5;      // float4 K (and V) loads one thread has in flight (5 * 224 >= 64 rows * 16)
 constexpr int kStopCache = 8;    // stop tokens per slot kept in shared memory
 constexpr int kSlotBytesMin = 32 * 1024;
 constexpr size_t kStaticSmemReserve = 4096;
@@ -111,7 +115,12 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
   return w;
 }
 
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// One-directional gpu-scope fences: an acquire fence after relaxed reads
+// that observed a release pattern orders this thread's later accesses after
+// them (it does not wait for this thread's own earlier stores); a release
+// fence before relaxed stores orders this thread's earlier writes before them.
+__device__ __forceinline__ void fence_acquire_gpu() { asm volatile("fence.acquire.gpu;" ::: "memory"); }
+__device__ __forceinline__ void fence_release_gpu() { asm volatile("fence.release.gpu;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -212,16 +221,17 @@ __device__ __forceinline__ Seg seg1(const uint64_t* src, float* dst, int n, uint
 // the CTA is marked failed (the caller checks after its next barrier). With
 // `acquire`, a fence after the last observation orders this thread's later
 // loads after the writers' release fences.
+template <int PB = kPollBatch>
 __device__ __forceinline__ void poll(const Seg& s, bool acquire, FlowShared& sh, int* status) {
   const int tid = threadIdx.x;
   const int total = s.rows * s.n;
   const unsigned long long t0 = now_ns();
   bool ok = true;
-  for (int base = 0; ok && base < total; base += kPT * kPollBatch) {
-    uint32_t so[kPollBatch], dof[kPollBatch];
+  for (int base = 0; ok && base < total; base += kPT * PB) {
+    uint32_t so[PB], dof[PB];
     unsigned pend = 0;
 #pragma unroll
-    for (int k = 0; k < kPollBatch; k++) {
+    for (int k = 0; k < PB; k++) {
       const int f = base + tid + k * kPT;
       so[k] = 0;
       dof[k] = 0;
@@ -236,12 +246,12 @@ __device__ __forceinline__ void poll(const Seg& s, bool acquire, FlowShared& sh,
     }
     unsigned spins = 0;
     while (pend) {
-      uint64_t w[kPollBatch];
+      uint64_t w[PB];
 #pragma unroll
-      for (int k = 0; k < kPollBatch; k++)
+      for (int k = 0; k < PB; k++)
         if ((pend >> k) & 1u) w[k] = ld_word(s.src + so[k]);
 #pragma unroll
-      for (int k = 0; k < kPollBatch; k++) {
+      for (int k = 0; k < PB; k++) {
         if (((pend >> k) & 1u) && (uint32_t)(w[k] >> 32) == s.want) {
           s.dst[dof[k]] = __uint_as_float((uint32_t)w[k]);
           pend &= ~(1u << k);
@@ -261,7 +271,7 @@ __device__ __forceinline__ void poll(const Seg& s, bool acquire, FlowShared& sh,
       }
     }
   }
-  if (acquire) fence_acq_rel_gpu();
+  if (acquire) fence_acquire_gpu();
 }
 
 // ------------------------------------------------------------ weight ring
@@ -513,7 +523,8 @@ struct Flow {
       if (sh.act[g]) mk |= 1u << g;
     return mk;
   }
-  __device__ void do_poll(const Seg& s, bool acquire) { poll(s, acquire, sh, bt.status); }
+  template <int PB = kPollBatch>
+  __device__ void do_poll(const Seg& s, bool acquire) { poll<PB>(s, acquire, sh, bt.status); }
 
   // Norm weights of a stage: copied global -> shared with cp.async before
   // the poll (no registers held, the copy overlaps the wait); norm_ready()
@@ -550,7 +561,8 @@ struct Flow {
   // epi(row, acc_row[G], has_second_row, acc_second[G]). With NORM the inputs
   // are RMS-normalised on the fly, n = (x * inv) * w with the norm weights
   // staged in nw (the rounding of stage_norm); each warp computes inv.
-  template <bool NORM, class Epi>
+  // NR rows (2 or 4) per warp pass; the epilogue still sees row pairs.
+  template <bool NORM, int NR = 2, class Epi>
   __device__ void gemv(const Slice& sl, const float* xs, int xstride, int K, Epi&& epi) {
     const int warp = threadIdx.x >> 5;
     float inv[G];
@@ -559,12 +571,16 @@ struct Flow {
     for (int done = 0; done < sl.nrows;) {
       const int n = min(sl.per, sl.nrows - done);
       const unsigned char* base = ring_wait(rg, sh, bt.status);
-      for (int pr = warp; 2 * pr < n; pr += kPW) {
-        const int i0 = 2 * pr, i1 = min(i0 + 1, n - 1);
-        const void* rows[2] = {base + (size_t)i0 * sl.rb, base + (size_t)i1 * sl.rb};
-        float acc[2][G];
-        warp_dot_smem<BF16, NORM, 2, G>(rows, K, xs, xstride, nw, inv, acc);
-        epi(sl.row0 + done + i0, acc[0], i0 + 1 < n, acc[1]);
+      for (int pr = warp; NR * pr < n; pr += kPW) {
+        const int i0 = NR * pr;
+        const void* rows[NR];
+#pragma unroll
+        for (int r = 0; r < NR; r++) rows[r] = base + (size_t)min(i0 + r, n - 1) * sl.rb;
+        float acc[NR][G];
+        warp_dot_smem<BF16, NORM, NR, G>(rows, K, xs, xstride, nw, inv, acc);
+#pragma unroll
+        for (int q = 0; q < NR / 2; q++)
+          if (i0 + 2 * q < n) epi(sl.row0 + done + i0 + 2 * q, acc[2 * q], i0 + 2 * q + 1 < n, acc[2 * q + 1]);
       }
       ring_release(rg);
       done += n;
@@ -743,6 +759,7 @@ struct Flow {
         if (r1 > r0) do_poll(Seg{fb.xt + r0, xr + r0, r1 - r0, bt.B, xw, xw, all, tg}, false);
       }
       if (sl.nrows > 0) norm_ready();
+      fence_acquire_gpu();  // as acquire_cache (the positions are known below)
       csync_();
       if (fail()) return false;
       if (threadIdx.x < G) {
@@ -764,6 +781,7 @@ struct Flow {
       }
       csync_();
       if (!act_mask()) return false;
+      prefetch_chunks(0);
       xstride = xw;
     } else {
       const unsigned act = act_mask();
@@ -774,6 +792,7 @@ struct Flow {
       } else if (r1 > r0) {
         do_poll(Seg{fb.xt + r0, xr + r0, r1 - r0, G, xw, H, act, tg}, false);
       }
+      acquire_cache(l);
       csync_();
       if (fail()) return false;
       // own residual rows (the O projection adds to them; read after barriers)
@@ -842,18 +861,46 @@ struct Flow {
     return true;
   }
 
+  // Acquire: every CTA's KV-cache appends of earlier steps were released
+  // before tagged words this thread has already observed (their O-stage
+  // release, then gate/up words polled in the down stage), so after this
+  // fence this layer's cached rows may be read. Placed after a poll, when
+  // the thread's own recent stores (which the fence waits for) have drained.
+  __device__ void acquire_cache(int l) {
+    fence_acquire_gpu();
+    prefetch_chunks(l);
+  }
+
+  // Moves the cached rows of this CTA's attention units of layer l into L2
+  // (prefetches have no ordering effect).
+  __device__ void prefetch_chunks(int l) {
+    if (threadIdx.x != 0) return;
+    const int maxc = bt.max_chunks, units = bt.B * m.NKV * maxc;
+    for (int u = cta; u < units; u += ncta) {
+      const int b = u / (m.NKV * maxc), rem = u % (m.NKV * maxc);
+      const int kvh = rem / maxc, c = rem % maxc;
+      if (!sh.act[b]) continue;
+      const int pos = sh.pos[b], t0 = c * kAttnChunk;
+      const int tc = min(kAttnChunk, pos - t0);
+      if (tc <= 0) continue;
+      const DSession& S = sh.sess[b];
+      const size_t off = (((size_t)l * m.NKV + kvh) * S.cap + t0) * m.HD;
+      prefetch_l2(S.kc + off, (size_t)tc * m.HD * sizeof(float));
+      prefetch_l2(S.vc + off, (size_t)tc * m.HD * sizeof(float));
+    }
+  }
+
   // --------------------------------------------------------- attention
   // Units (slot, KV head, chunk of kAttnChunk positions) over the CTAs. The
   // cached rows (positions < pos) are loaded before the new q/k/v arrive:
   // every appending CTA released them at its O stage (release fence by all
   // its threads, then later tagged words that every CTA polls), and the
-  // fence at the start of this stage acquires them. A single-chunk unit
+  // fence at the start of the QKV stage acquired them. A single-chunk unit
   // writes the output directly (the combine of one chunk is acc / l, bit for
-  // bit); otherwise its partials are combined, in chunk order, by the CTA of
-  // chunk 0.
+  // bit); otherwise the partials of each (slot, query head) are combined, in
+  // chunk order, by one CTA placed after the unit CTAs.
   __device__ bool attn(int s, int l) {
     csync_();  // the QKV warps are done with the staging area
-    fence_acq_rel_gpu();
     const int Gh = m.NH / m.NKV, HD = m.HD, maxc = bt.max_chunks;
     const int grp = (Gh + 2) * HD;
     const int qkvd = m.QD + 2 * m.KVD;
@@ -881,16 +928,29 @@ struct Flow {
       const int tn = min(kAttnChunk, pos + 1 - t0);  // rows of this chunk
       const int tc = min(tn, pos - t0);              // of which cached (t < pos)
       const size_t head_base = ((size_t)l * m.NKV + kvh) * S.cap;
-      // cached rows -> shared memory, every load of a batch before its stores
-      for (int base = 0; base < tc * c4n; base += kKvBatch * kPT) {
-        float4 kv[kKvBatch], vv[kKvBatch];
+      // Cached rows -> shared memory. The first batch's loads stay in flight
+      // across the q/k/v poll; later batches (long heads) follow it.
+      float4 kv[kKvBatch], vv[kKvBatch];
 #pragma unroll
-        for (int k = 0; k < kKvBatch; k++) {
-          const int idx = base + tid + k * kPT;
-          if (idx < tc * c4n) {
-            const int tt = idx / c4n, c4 = idx - tt * c4n;
-            kv[k] = ld_act(S.kc + (head_base + t0 + tt) * HD + 4 * c4);
-            vv[k] = ld_act(S.vc + (head_base + t0 + tt) * HD + 4 * c4);
+      for (int k = 0; k < kKvBatch; k++) {
+        const int idx = tid + k * kPT;
+        if (idx < tc * c4n) {
+          const int tt = idx / c4n, c4 = idx - tt * c4n;
+          kv[k] = ld_act(S.kc + (head_base + t0 + tt) * HD + 4 * c4);
+          vv[k] = ld_act(S.vc + (head_base + t0 + tt) * HD + 4 * c4);
+        }
+      }
+      do_poll(seg1(fb.qt + (size_t)b * qkvd + (size_t)kvh * grp, qs, grp, tq), false);
+      for (int base = 0; base < tc * c4n; base += kKvBatch * kPT) {
+        if (base > 0) {
+#pragma unroll
+          for (int k = 0; k < kKvBatch; k++) {
+            const int idx = base + tid + k * kPT;
+            if (idx < tc * c4n) {
+              const int tt = idx / c4n, c4 = idx - tt * c4n;
+              kv[k] = ld_act(S.kc + (head_base + t0 + tt) * HD + 4 * c4);
+              vv[k] = ld_act(S.vc + (head_base + t0 + tt) * HD + 4 * c4);
+            }
           }
         }
 #pragma unroll
@@ -903,7 +963,6 @@ struct Flow {
           }
         }
       }
-      do_poll(seg1(fb.qt + (size_t)b * qkvd + (size_t)kvh * grp, qs, grp, tq), false);
       csync_();
       if (fail()) return false;
       // scores; the row of position pos (t == pos, last of the last chunk) is the new k
@@ -965,39 +1024,32 @@ struct Flow {
       }
       csync_();
     }
-    // Combine: the CTA of chunk 0 of each (slot, KV head), chunks in order.
-    for (int bk = 0; bk < bt.B * m.NKV; bk++) {
-      if ((bk * maxc) % ncta != cta) continue;
-      const int b = bk / m.NKV, kvh = bk % m.NKV;
+    // Combine per (slot, query head), chunks in order.
+    for (int bh = 0; bh < bt.B * m.NH; bh++) {
+      if ((units + bh) % ncta != cta) continue;
+      const int b = bh / m.NH, h = bh % m.NH;
       if (!sh.act[b]) continue;
       const int nch = sh.pos[b] / kAttnChunk + 1;
       if (nch == 1) continue;  // written by its only unit
       const int row = nch * (HD + 2);
-      const int hp = max(1, min(min(Gh, 16), geo.stage_f / row));
-      for (int h0 = 0; h0 < Gh; h0 += hp) {
-        const int nh = min(hp, Gh - h0);
-        const uint64_t* src = fb.pt + ((size_t)b * m.NH + (size_t)kvh * Gh + h0) * maxc * (HD + 2);
-        do_poll(Seg{src, stage, row, nh, maxc * (HD + 2), row, (nh >= 32 ? 0xFFFFFFFFu : (1u << nh) - 1u), tp},
-                false);
-        csync_();
-        if (fail()) return false;
-        for (int idx = tid; idx < nh * HD; idx += kPT) {
-          const int h = idx / HD, d = idx - h * HD;
-          const float* p = stage + (size_t)h * row;
-          float M = -INFINITY;
-          for (int cc = 0; cc < nch; cc++) M = fmaxf(M, p[cc * (HD + 2)]);
-          float L = 0.0f, O = 0.0f;
-          for (int cc = 0; cc < nch; cc++) {
-            const float* pc = p + cc * (HD + 2);
-            const float mc = pc[0], lc = pc[1], ac = pc[2 + d];
-            const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
-            L = fmaf(w, lc, L);
-            O = fmaf(w, ac, O);
-          }
-          st_f(fb.at + (size_t)b * m.QD + (size_t)(kvh * Gh + h0 + h) * HD + d, __fdiv_rn(O, L), tp);
+      const uint64_t* src = fb.pt + ((size_t)b * m.NH + h) * maxc * (HD + 2);
+      do_poll<kCombineBatch>(seg1(src, stage, row, tp), false);
+      csync_();
+      if (fail()) return false;
+      for (int d = tid; d < HD; d += kPT) {
+        float M = -INFINITY;
+        for (int cc = 0; cc < nch; cc++) M = fmaxf(M, stage[cc * (HD + 2)]);
+        float L = 0.0f, O = 0.0f;
+        for (int cc = 0; cc < nch; cc++) {
+          const float* pc = stage + cc * (HD + 2);
+          const float mc = pc[0], lc = pc[1], ac = pc[2 + d];
+          const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
+          L = fmaf(w, lc, L);
+          O = fmaf(w, ac, O);
         }
-        csync_();
+        st_f(fb.at + (size_t)b * m.QD + (size_t)h * HD + d, __fdiv_rn(O, L), tp);
       }
+      csync_();
     }
     return true;
   }
@@ -1008,7 +1060,7 @@ struct Flow {
     // of an appending CTA orders this layer's cache appends before any later
     // tagged word of the CTA; readers acquire them at their next attention
     // stage of this layer.
-    if (has_kv) fence_acq_rel_gpu();
+    if (has_kv) fence_release_gpu();
     const Slice sl = slice_of(m, ly, nblk, 1, l, cta, ncta, geo.slot_bytes);
     if (sl.nrows == 0) return true;
     csync_();
@@ -1207,7 +1259,7 @@ struct Flow {
       if (threadIdx.x == 0) sh.Z[g] = Z;
     }
     csync_();
-    if (lane == 0) fence_acq_rel_gpu();  // logits stores before the p-sums
+    if (lane == 0) fence_release_gpu();  // logits stores before the p-sums
     const uint32_t t2 = tag(s, sid_s2(m.L));
     for (int k = k0 + warp; k < k1; k += kPW) {
       const int i = k * kSBlk + lane;
