@@ -235,6 +235,8 @@ def run_b200(args):
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
 
+    # single-session runs use the dataflow token-loop kernel; fail loudly if it does not apply
+    os.environ.setdefault("DEFER_B200_LOOP", "flow")
     import defer_b200 as D
     from defer_b200 import synthetic
 
@@ -309,7 +311,7 @@ def run_b200(args):
     achieved = tm["hbm_bytes"] / (tm["device_ms"] / 1e3) / 1e9
     tpt = traffic_per_token()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "peak_kind": peak_kind, "kernel": "k_persistent (token loop)",
+                "peak_kind": peak_kind, "kernel": "k_flow (dataflow token loop, one launch per run)",
                 "bytes_per_launch": tm["hbm_bytes"] / runs,
                 "traffic": (tpt * tokens / runs) if tpt else None,
                 "launch_ms": tm["device_ms"] / runs}
@@ -341,10 +343,30 @@ def main(argv=None):
     ap.add_argument("--cpu-gen", type=int, default=150, help="sampled tokens of the CPU baseline sample")
     ap.add_argument("--ref-gen", type=int, default=48, help="sampled tokens per reference-arm step")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="no measurement: the small case profiles are captured on (135M model, "
+                         "16-token prompt, then one launch of 32 sampled tokens)")
     a = ap.parse_args(argv)
     if a.impl == "reference":
         return run_reference(a)
+    if a.profile_case:
+        return profile_case()
     return run_b200(a)
+
+
+def profile_case():
+    """Two token-loop launches on the benchmark model: a 16-token prompt, then
+    32 sampled tokens (the launch profiles capture)."""
+    os.environ.setdefault("DEFER_B200_LOOP", "flow")
+    import numpy as np
+    import defer_b200 as D
+    from defer_b200 import synthetic
+    m = D.Model.load(synthetic.model_path(MODEL, model_dir(), 0))
+    s = D.Session(m, D.seed_from_u64(1), 0.7)
+    s.prompt([int(t) for t in np.random.default_rng(1).integers(0, m.config.vocab_size, 16)])
+    s.generate(32)
+    print(json.dumps({"profile_case": "ok", **m.timing()}))
+    return 0
 
 
 if __name__ == "__main__":
