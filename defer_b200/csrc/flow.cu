@@ -566,8 +566,22 @@ struct Flow {
   __device__ void gemv(const Slice& sl, const float* xs, int xstride, int K, Epi&& epi) {
     const int warp = threadIdx.x >> 5;
     float inv[G];
+    if (NORM && G == 1) {
+      inv[0] = sh.act[0] ? inv_rms(xs, xstride, 0) : 0.0f;  // every warp, no barrier
+    } else if (NORM) {
+      // slot g's statistic once for the CTA, by warp g mod 7 (same rule)
+      for (int g = warp; g < G; g += kPW) {
+        if (!sh.act[g]) continue;
+        const float v = inv_rms(xs, xstride, g);
+        if ((threadIdx.x & 31) == 0) sh.inv[g] = v;
+      }
+      csync_();
 #pragma unroll
-    for (int g = 0; g < G; g++) inv[g] = (NORM && sh.act[g]) ? inv_rms(xs, xstride, g) : 0.0f;
+      for (int g = 0; g < G; g++) inv[g] = sh.act[g] ? sh.inv[g] : 0.0f;
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; g++) inv[g] = 0.0f;
+    }
     for (int done = 0; done < sl.nrows;) {
       const int n = min(sl.per, sl.nrows - done);
       const unsigned char* base = ring_wait(rg, sh, bt.status);

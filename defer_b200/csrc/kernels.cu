@@ -201,10 +201,11 @@ static size_t step_smem_floats(const DModel& m, int B) {
 
 size_t step_smem_bytes(const DModel& m, int B) { return step_smem_floats(m, B) * sizeof(float); }
 
+// Always set: the default limit covers dynamic plus static shared memory,
+// so a request just under 48 KB can still exceed it.
 template <class K>
 static void allow_smem(K kernel, size_t bytes) {
-  if (bytes > 48 * 1024)
-    DEFER_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  DEFER_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
 }
 
 template <bool BF16, int G>

@@ -96,13 +96,17 @@ def test_token_loop_paths_are_bit_identical(mdir, name, t):
     assert outs["flow"] == outs["barrier"] == outs["phased"]
 
 
-def test_token_loop_paths_agree_on_a_batch(mdir):
-    """Slot groups of 3 sessions (one group of 4 slots) with different
-    prompts, temperatures and lengths: every path gives the same tokens."""
+@pytest.mark.parametrize("n", [3, 7])
+def test_token_loop_paths_agree_on_a_batch(mdir, n):
+    """Slot groups of 3 and 7 sessions (groups of 4 and 8 slots) with
+    different prompts, temperatures and lengths: every path gives the same
+    tokens."""
     gm = D.Model.load(model_file(mdir, "test-gqa4"))
-    prompts = [_tokens(gm.config.vocab_size, n, 10 + n) for n in (5, 70, 33)]
-    seeds = [D.seed_from_u64(i) for i in range(3)]
-    temps, maxt = [0.0, 0.9, 1.3], [30, 12, 25]
+    lens = [5, 70, 33, 12, 64, 1, 40][:n]
+    prompts = [_tokens(gm.config.vocab_size, k, 10 + k) for k in lens]
+    seeds = [D.seed_from_u64(i) for i in range(n)]
+    temps = [[0.0, 0.9, 1.3][i % 3] for i in range(n)]
+    maxt = [[30, 12, 25, 7][i % 4] for i in range(n)]
     outs = {p: _on_path(p, lambda: D.generate_batch(gm, prompts, seeds, temps, maxt)[0]) for p in PATHS}
     assert outs["flow"] == outs["barrier"] == outs["phased"]
 

@@ -208,6 +208,28 @@ def test_replay_batch_equals_single_checkout(tiny):
         assert res[11].div_step == len(tam.history_tokens) - 1
 
 
+def test_sharded_replay_blocks_equal_one_batched_replay(tiny):
+    """Row e: each rank's block of a partition (here two ranks run one after
+    the other on one GPU) gives exactly the outcomes and KV fingerprints of
+    one batched replay of everything."""
+    from defer_b200.partition import replay_sharded
+    m, _, _ = tiny
+    rng = np.random.default_rng(5)
+    cks = []
+    for i in range(9):
+        prompt = [int(t) for t in rng.integers(0, 256, int(rng.integers(3, 25)))]
+        _, s = generate(m, [0.0, 0.8, 1.3][i % 3], 50 + i, int(rng.integers(1, 30)), prompt)
+        cks.append(s.checkpoint())
+    whole, _ = D.replay_batch(m, cks, batch=8, fingerprints=True)
+    parts = []
+    for rank in range(2):
+        out, ms, blocks = replay_sharded(m, cks, rank, 2, batch=4)
+        assert ms > 0.0
+        parts.extend(out)
+    assert [b for blk in blocks for b in blk] == list(range(9))
+    assert [(r.status, r.fingerprint) for r in parts] == [(r.status, r.fingerprint) for r in whole]
+
+
 def test_generate_batch_equals_sessions(tiny):
     m, _, _ = tiny
     rng = np.random.default_rng(1)
