@@ -41,7 +41,8 @@ constexpr int kThreads = 256;       // threads per CTA for every phase
 constexpr int kWarps = kThreads / 32;
 constexpr int kAttnChunk = 64;      // key positions per attention chunk
 constexpr int kSBlk = 32;           // sampler block: elements per block (one per lane)
-constexpr int kMaxGroup = 8;        // sessions per GEMV register tile
+constexpr int kMaxGroup = 8;        // slots per register tile of the dataflow kernel
+constexpr int kMaxGroupWide = 32;   // slots per register tile of the grid-barrier / per-phase kernels
 
 enum StatusCode : int {
   kStOk = 0,
@@ -133,6 +134,8 @@ struct DBatch {
   int* status;            // global status word
   int* any_active;        // [2] set by the select phase (indexed by step parity)
   unsigned* bar;          // grid barrier counter
+  unsigned smem_bytes;    // dynamic shared memory of the launch (stages copy
+                          // their weight rows into what their inputs leave free)
 };
 
 }  // namespace defer

@@ -33,12 +33,15 @@ Runner::Runner(const Model* m, int B, int max_cap) : m_(m), B_(B), max_cap_(max_
   max_chunks_ = (max_cap + kAttnChunk - 1) / kAttnChunk;
   if (max_chunks_ < 1) max_chunks_ = 1;
   nblk_ = (d.V + kSBlk - 1) / kSBlk;
-  DEFER_CUDA(cudaMalloc(&x_, (size_t)B * d.H * 4));
+  // Activation rows padded to whole 32-slot groups: a group's kernels may
+  // read (never use) the rows of slots past the batch.
+  const size_t Bp = ((size_t)B + kMaxGroupWide - 1) / kMaxGroupWide * kMaxGroupWide;
+  DEFER_CUDA(cudaMalloc(&x_, Bp * d.H * 4));
   DEFER_CUDA(cudaMalloc(&tickets_, (size_t)B * d.NKV * sizeof(int)));
   DEFER_CUDA(cudaMalloc(&stats_, (size_t)5 * B * nblk_ * 4));
-  DEFER_CUDA(cudaMalloc(&q_, (size_t)B * d.QD * 4));
-  DEFER_CUDA(cudaMalloc(&att_, (size_t)B * d.QD * 4));
-  DEFER_CUDA(cudaMalloc(&g_, (size_t)B * d.FF * 4));
+  DEFER_CUDA(cudaMalloc(&q_, Bp * d.QD * 4));
+  DEFER_CUDA(cudaMalloc(&att_, Bp * d.QD * 4));
+  DEFER_CUDA(cudaMalloc(&g_, Bp * d.FF * 4));
   DEFER_CUDA(cudaMalloc(&logits_, (size_t)B * d.V * 4));
   DEFER_CUDA(cudaMalloc(&part_, (size_t)B * d.NH * max_chunks_ * (d.HD + 2) * 4));
   DEFER_CUDA(cudaMalloc(&d_sess_, sizeof(DSession) * B));

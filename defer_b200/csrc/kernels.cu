@@ -180,26 +180,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
 // ------------------------------------------------------------ launchers
 static int div_up(long a, long b) { return (int)((a + b - 1) / b); }
 
-static int group_for(int B) { return B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8; }
+// Slots per register tile: enough for the batch, at most 32, and small
+// enough that the group's normalised rows fit comfortably in shared memory.
+static int group_for(const DModel& m, int B) {
+  int G = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : B <= 8 ? 8 : B <= 16 ? 16 : kMaxGroupWide;
+  while (G > 8 && (size_t)G * std::max(m.H, m.QD) * sizeof(float) > 96 * 1024) G /= 2;
+  return G;
+}
 
 // Dynamic shared memory (floats) of the step phases for a batch of B: the
 // staged activations of one slot group (normed inputs, O-projection input,
 // the down-projection input when it fits), the attention chunk, and the
 // sampler's group sums.
-static size_t step_smem_floats(const DModel& m, int B) {
-  const int G = group_for(B);
+static size_t step_smem_floats(const DModel& m, int B, int max_chunks) {
+  const int G = group_for(m, B);
   const int Gh = m.NH / m.NKV;
   size_t f = (size_t)G * std::max(m.H, m.QD);
   const size_t ffs = (size_t)G * m.FF;
-  if (ffs * 4 <= 96 * 1024) f = std::max(f, ffs);
-  f = std::max(f, (size_t)(Gh * m.HD + Gh * kAttnChunk));
+  if (ffs * 4 <= 200 * 1024) f = std::max(f, ffs);  // the down projection's input, when it fits
+  // attention: q, scores, the chunk's K (padded rows) and V; the combine
+  // reuses the K/V area for one head's partials of every chunk
+  const size_t kv = std::max((size_t)kAttnChunk * (m.HD + 4) + (size_t)kAttnChunk * m.HD,
+                             (size_t)max_chunks * (m.HD + 2));
+  f = std::max(f, (size_t)(Gh * m.HD + Gh * kAttnChunk) + kv);
+  // the wide head: normalized rows plus one [8][kSBlk] tile buffer per warp
+  if (G >= 8) f = std::max(f, (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)kPW * 8 * kSBlk);
   const int nblk = (m.V + kSBlk - 1) / kSBlk;
   const int ng2 = (nblk + 31) / 32;
   f = std::max(f, (size_t)(ng2 + (ng2 + 31) / 32 + 8));
   return (f + 3) & ~(size_t)3;
 }
 
-size_t step_smem_bytes(const DModel& m, int B) { return step_smem_floats(m, B) * sizeof(float); }
+size_t step_smem_bytes(const DModel& m, int B, int max_chunks) {
+  return step_smem_floats(m, B, max_chunks) * sizeof(float);
+}
 
 // Always set: the default limit covers dynamic plus static shared memory,
 // so a request just under 48 KB can still exceed it.
@@ -209,10 +223,12 @@ static void allow_smem(K kernel, size_t bytes) {
 }
 
 template <bool BF16, int G>
-static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt, int first_step, int nsteps, int sms,
+static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, int first_step, int nsteps, int sms,
                         cudaStream_t st) {
-  const size_t sf = step_smem_floats(m, bt.B);
+  const size_t sf = step_smem_floats(m, bt0.B, bt0.max_chunks);
   const size_t smem = sf * sizeof(float);
+  DBatch bt = bt0;
+  bt.smem_bytes = (unsigned)smem;
   allow_smem(k_select<BF16>, smem);
   allow_smem(k_qkv<BF16, G>, smem);
   allow_smem(k_attn, smem);
@@ -253,29 +269,41 @@ int launches_per_step_phased(const DModel& m) { return 4 + 5 * m.L; }
 
 void launch_steps_phased(const DModel& m, const DLayer* host_layers, const DBatch& bt, int first_step, int nsteps,
                          int sms, cudaStream_t st) {
-  const int G = group_for(bt.B);
+  const int G = group_for(m, bt.B);
   if (m.bf16) {
     switch (G) {
       case 1: phased_impl<true, 1>(m, host_layers, bt, first_step, nsteps, sms, st); break;
       case 2: phased_impl<true, 2>(m, host_layers, bt, first_step, nsteps, sms, st); break;
       case 4: phased_impl<true, 4>(m, host_layers, bt, first_step, nsteps, sms, st); break;
-      default: phased_impl<true, 8>(m, host_layers, bt, first_step, nsteps, sms, st); break;
+      case 8: phased_impl<true, 8>(m, host_layers, bt, first_step, nsteps, sms, st); break;
+      case 16: phased_impl<true, 16>(m, host_layers, bt, first_step, nsteps, sms, st); break;
+      default: phased_impl<true, 32>(m, host_layers, bt, first_step, nsteps, sms, st); break;
     }
   } else {
     switch (G) {
       case 1: phased_impl<false, 1>(m, host_layers, bt, first_step, nsteps, sms, st); break;
       case 2: phased_impl<false, 2>(m, host_layers, bt, first_step, nsteps, sms, st); break;
       case 4: phased_impl<false, 4>(m, host_layers, bt, first_step, nsteps, sms, st); break;
-      default: phased_impl<false, 8>(m, host_layers, bt, first_step, nsteps, sms, st); break;
+      case 8: phased_impl<false, 8>(m, host_layers, bt, first_step, nsteps, sms, st); break;
+      case 16: phased_impl<false, 16>(m, host_layers, bt, first_step, nsteps, sms, st); break;
+      default: phased_impl<false, 32>(m, host_layers, bt, first_step, nsteps, sms, st); break;
     }
   }
 }
 
 template <bool BF16, int G>
 static void persistent_impl(const DModel& m, const DBatch& bt, int nsteps, int sms, cudaStream_t st) {
-  const size_t sf = step_smem_floats(m, bt.B);
-  const size_t smem = sf * sizeof(float);
+  const size_t sf = step_smem_floats(m, bt.B, bt.max_chunks);
   auto kern = k_persistent<BF16, G>;
+  // One CTA per SM: take all the shared memory the SM offers; each stage
+  // copies its weight rows into what its inputs leave free.
+  int dev = 0, optin = 0;
+  DEFER_CUDA(cudaGetDevice(&dev));
+  DEFER_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  cudaFuncAttributes fa;
+  DEFER_CUDA(cudaFuncGetAttributes(&fa, kern));
+  const size_t avail = (size_t)optin > fa.sharedSizeBytes + 1024 ? (size_t)optin - fa.sharedSizeBytes - 1024 : 0;
+  const size_t smem = std::max(sf * sizeof(float), avail & ~(size_t)15);
   allow_smem(kern, smem);
   int per_sm = 0;
   DEFER_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
@@ -285,6 +313,7 @@ static void persistent_impl(const DModel& m, const DBatch& bt, int nsteps, int s
   DEFER_CUDA(cudaMemsetAsync(bt.any_active, 0, 2 * sizeof(int), st));
   DModel mm = m;
   DBatch bb = bt;
+  bb.smem_bytes = (unsigned)smem;
   int ns = nsteps;
   unsigned sfl = (unsigned)sf;
   void* args[] = {&mm, &bb, &ns, &sfl};
@@ -292,20 +321,24 @@ static void persistent_impl(const DModel& m, const DBatch& bt, int nsteps, int s
 }
 
 void launch_steps_persistent(const DModel& m, const DBatch& bt, int nsteps, int sms, cudaStream_t st) {
-  const int G = group_for(bt.B);
+  const int G = group_for(m, bt.B);
   if (m.bf16) {
     switch (G) {
       case 1: persistent_impl<true, 1>(m, bt, nsteps, sms, st); break;
       case 2: persistent_impl<true, 2>(m, bt, nsteps, sms, st); break;
       case 4: persistent_impl<true, 4>(m, bt, nsteps, sms, st); break;
-      default: persistent_impl<true, 8>(m, bt, nsteps, sms, st); break;
+      case 8: persistent_impl<true, 8>(m, bt, nsteps, sms, st); break;
+      case 16: persistent_impl<true, 16>(m, bt, nsteps, sms, st); break;
+      default: persistent_impl<true, 32>(m, bt, nsteps, sms, st); break;
     }
   } else {
     switch (G) {
       case 1: persistent_impl<false, 1>(m, bt, nsteps, sms, st); break;
       case 2: persistent_impl<false, 2>(m, bt, nsteps, sms, st); break;
       case 4: persistent_impl<false, 4>(m, bt, nsteps, sms, st); break;
-      default: persistent_impl<false, 8>(m, bt, nsteps, sms, st); break;
+      case 8: persistent_impl<false, 8>(m, bt, nsteps, sms, st); break;
+      case 16: persistent_impl<false, 16>(m, bt, nsteps, sms, st); break;
+      default: persistent_impl<false, 32>(m, bt, nsteps, sms, st); break;
     }
   }
 }

@@ -7,7 +7,7 @@
 namespace defer {
 
 // Dynamic shared memory of the step phases for a batch of B slots.
-size_t step_smem_bytes(const DModel& m, int B);
+size_t step_smem_bytes(const DModel& m, int B, int max_chunks);
 
 // One launch per phase for `nsteps` steps (stream ordered, no grid
 // barriers). `host_layers` is the host copy of m.layers.

@@ -101,6 +101,14 @@ struct WChunk;
 template <>
 struct WChunk<false> {
   static constexpr int E = 4;
+  // L1-allocating variant, for rows several warps of a CTA read in turn
+  __device__ __forceinline__ static void load_l1(const void* row, int j, float* w) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(row) + j);
+    w[0] = t.x;
+    w[1] = t.y;
+    w[2] = t.z;
+    w[3] = t.w;
+  }
   __device__ __forceinline__ static void load(const void* row, int j, float* w) {
     float4 t = ld_stream(reinterpret_cast<const float4*>(row) + j);
     w[0] = t.x;
@@ -112,6 +120,17 @@ struct WChunk<false> {
 template <>
 struct WChunk<true> {
   static constexpr int E = 8;
+  __device__ __forceinline__ static void load_l1(const void* row, int j, float* w) {
+    const uint4 t = __ldg(reinterpret_cast<const uint4*>(row) + j);
+    w[0] = bf16_lo(t.x);
+    w[1] = bf16_hi(t.x);
+    w[2] = bf16_lo(t.y);
+    w[3] = bf16_hi(t.y);
+    w[4] = bf16_lo(t.z);
+    w[5] = bf16_hi(t.z);
+    w[6] = bf16_lo(t.w);
+    w[7] = bf16_hi(t.w);
+  }
   __device__ __forceinline__ static void load(const void* row, int j, float* w) {
     uint4 t = ld_stream_u4(reinterpret_cast<const uint4*>(row) + j);
     w[0] = bf16_lo(t.x);
@@ -134,7 +153,7 @@ __device__ __forceinline__ float4 ld_x(const float* p) {
 
 // Canonical warp dot product of NR weight rows against G activation
 // vectors x_g = xs + g * xstride (all lanes return the same sums).
-template <bool BF16, bool SMEM, int NR, int G>
+template <bool BF16, bool SMEM, int NR, int G, bool WSMEM = false>
 __device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, const float* xs, int xstride,
                                          float (&acc)[NR][G]) {
   constexpr int E = WChunk<BF16>::E;
@@ -144,11 +163,34 @@ __device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, c
   for (int r = 0; r < NR; r++)
 #pragma unroll
     for (int g = 0; g < G; g++) acc[r][g] = 0.0f;
-#pragma unroll 4
+  // wide slot groups keep one chunk in flight (registers)
+#pragma unroll(G <= 8 ? 4 : 1)
   for (int j = lane; j < nch; j += 32) {
     float w[NR][E];
 #pragma unroll
-    for (int r = 0; r < NR; r++) WChunk<BF16>::load(rows[r], j, w[r]);
+    for (int r = 0; r < NR; r++) {
+      if constexpr (WSMEM) {  // weight rows staged in shared memory
+        if constexpr (BF16) {
+          const uint4 t = reinterpret_cast<const uint4*>(rows[r])[j];
+          w[r][0] = bf16_lo(t.x);
+          w[r][1] = bf16_hi(t.x);
+          w[r][2] = bf16_lo(t.y);
+          w[r][3] = bf16_hi(t.y);
+          w[r][4] = bf16_lo(t.z);
+          w[r][5] = bf16_hi(t.z);
+          w[r][6] = bf16_lo(t.w);
+          w[r][7] = bf16_hi(t.w);
+        } else {
+          const float4 t = reinterpret_cast<const float4*>(rows[r])[j];
+          w[r][0] = t.x;
+          w[r][1] = t.y;
+          w[r][2] = t.z;
+          w[r][3] = t.w;
+        }
+      } else {
+        WChunk<BF16>::load(rows[r], j, w[r]);
+      }
+    }
 #pragma unroll
     for (int g = 0; g < G; g++) {
       float xv[E];
@@ -170,6 +212,90 @@ __device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, c
   for (int r = 0; r < NR; r++)
 #pragma unroll
     for (int g = 0; g < G; g++) acc[r][g] = warp_sum_butterfly(acc[r][g]);
+}
+
+// Register-tiled canonical dot of NR weight rows (row r at w0 + min(r, rmax)
+// * wstride bytes; global memory, or shared memory when WSMEM) against NS
+// activation vectors xs + s * xstride (shared memory when XSMEM, else
+// global): the same per-lane chunk sums
+// as warp_dot, but one warp carries all NR * NS = N (a power of two, >= 32)
+// sums at once, so each chunk of x feeds NR rows and each chunk of W feeds
+// NS slots. The cross-lane sum is a transpose reduction: at the level of
+// lane distance d a lane keeps half of its sums and adds the partner's
+// copy of the same half. Every sum is formed over the same pairs of lanes,
+// in the same order, as warp_sum_butterfly, so the result is bit-identical;
+// it needs N - N/32 shuffles instead of 5 N. Lane L ends holding the sums
+// k = L * (N/32) + i (k = s * NR + r) as res[i], i < N/32.
+template <bool BF16, bool WSMEM, bool XSMEM, int NR, int NS>
+__device__ __forceinline__ void warp_tile(const unsigned char* w0, size_t wstride, int rmax, int K, const float* xs,
+                                          int xstride, float (&res)[NR * NS / 32]) {
+  constexpr int E = WChunk<BF16>::E;
+  constexpr int N = NR * NS;
+  static_assert(N >= 32 && (N & (N - 1)) == 0, "tile must be a power of two of at least 32 sums");
+  const int lane = threadIdx.x & 31;
+  const int nch = K / E;
+  float acc[N];
+#pragma unroll
+  for (int k = 0; k < N; k++) acc[k] = 0.0f;
+  for (int j = lane; j < nch; j += 32) {
+    float w[NR][E];
+#pragma unroll
+    for (int r = 0; r < NR; r++) {
+      const unsigned char* row = w0 + (size_t)(r < rmax ? r : rmax) * wstride;
+      if constexpr (WSMEM) {
+        if constexpr (BF16) {
+          const uint4 t = reinterpret_cast<const uint4*>(row)[j];
+          w[r][0] = bf16_lo(t.x);
+          w[r][1] = bf16_hi(t.x);
+          w[r][2] = bf16_lo(t.y);
+          w[r][3] = bf16_hi(t.y);
+          w[r][4] = bf16_lo(t.z);
+          w[r][5] = bf16_hi(t.z);
+          w[r][6] = bf16_lo(t.w);
+          w[r][7] = bf16_hi(t.w);
+        } else {
+          const float4 t = reinterpret_cast<const float4*>(row)[j];
+          w[r][0] = t.x;
+          w[r][1] = t.y;
+          w[r][2] = t.z;
+          w[r][3] = t.w;
+        }
+      } else {
+        WChunk<BF16>::load_l1(row, j, w[r]);
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+      float xv[E];
+#pragma unroll
+      for (int q = 0; q < E / 4; q++) {
+        const float4 t = ld_x<XSMEM>(xs + (size_t)s * xstride + j * E + 4 * q);
+        xv[4 * q] = t.x;
+        xv[4 * q + 1] = t.y;
+        xv[4 * q + 2] = t.z;
+        xv[4 * q + 3] = t.w;
+      }
+#pragma unroll
+      for (int r = 0; r < NR; r++)
+#pragma unroll
+        for (int e = 0; e < E; e++) acc[s * NR + r] = fmaf(w[r][e], xv[e], acc[s * NR + r]);
+    }
+  }
+  // transpose reduction, lane distances 16, 8, 4, 2, 1 (the butterfly's order)
+#pragma unroll
+  for (int lv = 0; lv < 5; lv++) {
+    const int d = 16 >> lv;
+    const int n = N >> lv, h = n >> 1;
+    const bool up = (lane & d) != 0;
+#pragma unroll
+    for (int k = 0; k < h; k++) {
+      const float send = up ? acc[k] : acc[k + h];
+      const float keep = up ? acc[k + h] : acc[k];
+      acc[k] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, d));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N / 32; i++) res[i] = acc[i];
 }
 
 __device__ __forceinline__ size_t row_bytes(int K, bool bf16) { return (size_t)K * (bf16 ? 2 : 4); }
@@ -196,38 +322,81 @@ __device__ __forceinline__ void prefetch_rows(const void* W, int rows_total, int
 }
 
 // ------------------------------------------------------------ RMSNorm
+// Per-group slot state of the stage in flight (load_slot_state): whether
+// slot b0 + g feeds a token this step, and its position; g_live marks the
+// rows stage_rows copied.
+static __shared__ int g_act[kMaxGroupWide];
+static __shared__ int g_pos[kMaxGroupWide];
+static __shared__ int g_live[kMaxGroupWide];
+
+template <int G>
+__device__ void load_slot_state(const DBatch& bt, int b0) {
+  if (threadIdx.x < G) {
+    const int b = b0 + threadIdx.x;
+    g_act[threadIdx.x] = b < bt.B ? ld_i(&bt.st[b].active) : 0;
+    g_pos[threadIdx.x] = b < bt.B ? ld_i(&bt.st[b].pos) : 0;
+  }
+  DEFER_CTA_SYNC();
+}
+
+__device__ __forceinline__ void cp_async16_g2s(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+// Slot b0 + g's activations src[(b0 + g) * K + i] into dst[g * K + i] with
+// cp.async (every copy in flight at once, no registers); slots past the
+// batch, or inactive ones when `need_active`, become zeros. Also records the
+// group's slot state in g_live / g_pos.
+template <int G>
+__device__ void stage_rows(const DBatch& bt, int b0, const float* src, int K, float* dst, bool need_active) {
+  load_slot_state<G>(bt, b0);
+  if (threadIdx.x < G) g_live[threadIdx.x] = b0 + (int)threadIdx.x < bt.B && (!need_active || g_act[threadIdx.x]);
+  DEFER_CTA_SYNC();
+  const int n4 = G * K / 4;  // K % 4 == 0
+  for (int f = threadIdx.x; f < n4; f += kPT) {
+    const int g = (4 * f) / K;
+    if (g_live[g])
+      cp_async16_g2s(dst + 4 * (size_t)f, src + (size_t)b0 * K + 4 * (size_t)f);
+    else
+      *reinterpret_cast<float4*>(dst + 4 * (size_t)f) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  DEFER_CTA_SYNC();
+}
+
 // dst[g][i] = rmsnorm(x of slot b0+g)[i] for the G slots of a group
-// (inactive or missing slots get zeros). Warp g computes slot g's sum of
-// squares with the canonical dot; all threads then write the products.
+// (inactive or missing slots get zeros). The raw rows are staged first; a
+// warp then computes each slot's sum of squares with the canonical dot
+// (lane-strided float4 chunks, fmaf in element order, butterfly), and
+// every element is scaled (x * inv) * w in place.
 template <int G>
 __device__ void stage_norm(const DModel& m, const DBatch& bt, int b0, const float* w_of_layer, const float* x,
                            float* dst) {
-  __shared__ float s_inv[kMaxGroup];
+  __shared__ float s_inv[kMaxGroupWide];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp < G) {
-    const int b = b0 + warp;
+  stage_rows<G>(bt, b0, x, m.H, dst, true);
+  for (int g = warp; g < G; g += kPW) {
+    const float4* x4 = reinterpret_cast<const float4*>(dst + (size_t)g * m.H);
     float acc = 0.0f;
-    if (b < bt.B && ld_i(&bt.st[b].active)) {
-      const float* xb = x + (size_t)b * m.H;
-      for (int j = lane; j < m.H / 4; j += 32) {
-        float4 t = ld_act(xb + 4 * j);
-        acc = fmaf(t.x, t.x, acc);
-        acc = fmaf(t.y, t.y, acc);
-        acc = fmaf(t.z, t.z, acc);
-        acc = fmaf(t.w, t.w, acc);
-      }
+    for (int j = lane; j < m.H / 4; j += 32) {
+      const float4 t = x4[j];
+      acc = fmaf(t.x, t.x, acc);
+      acc = fmaf(t.y, t.y, acc);
+      acc = fmaf(t.z, t.z, acc);
+      acc = fmaf(t.w, t.w, acc);
     }
     acc = warp_sum_butterfly(acc);
-    if (lane == 0) s_inv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)m.H), m.eps)));
+    if (lane == 0) s_inv[g] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)m.H), m.eps)));
   }
   DEFER_CTA_SYNC();
-  for (int g = 0; g < G; g++) {
-    const int b = b0 + g;
-    const bool live = b < bt.B && ld_i(&bt.st[b].active);
-    const float inv = s_inv[g];
-    const float* xb = x + (size_t)(live ? b : 0) * m.H;
-    for (int i = threadIdx.x; i < m.H; i += kPT)
-      dst[(size_t)g * m.H + i] = live ? __fmul_rn(__fmul_rn(ld_f(xb + i), inv), w_of_layer[i]) : 0.0f;
+  for (int i = threadIdx.x; i < m.H; i += kPT) {
+    const float w = w_of_layer[i];
+#pragma unroll 4
+    for (int g = 0; g < G; g++) {
+      float* p = dst + (size_t)g * m.H + i;
+      *p = g_live[g] ? __fmul_rn(__fmul_rn(*p, s_inv[g]), w) : 0.0f;
+    }
   }
   DEFER_CTA_SYNC();
 }
@@ -235,15 +404,27 @@ __device__ void stage_norm(const DModel& m, const DBatch& bt, int b0, const floa
 // Copies slot activations [b0, b0+G) (stride K) into shared memory.
 template <int G>
 static __device__ void stage_copy(const DBatch& bt, int b0, const float* src, int K, float* dst) {
-  for (int g = 0; g < G; g++) {
-    const int b = b0 + g;
-    const bool live = b < bt.B;
-    const float* s = src + (size_t)(live ? b : 0) * K;
-    for (int i = threadIdx.x * 4; i < K; i += kPT * 4) {
-      float4 v = live ? ld_act(s + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4*>(dst + (size_t)g * K + i) = v;
-    }
-  }
+  stage_rows<G>(bt, b0, src, K, dst, false);
+}
+
+// Starts copying this CTA's weight rows [row0, row0 + nrows) (rb bytes
+// each, 16-byte multiples) of W into shared memory after the stage's first
+// x_floats floats, with cp.async; the next stage_rows (or cp_async_join)
+// waits for them. Returns the copy, or null when it does not fit (the rows
+// are then read from global memory).
+static __device__ const unsigned char* stage_weights(const void* W, int row0, int nrows, size_t rb, float* smem,
+                                                     size_t x_floats, unsigned smem_bytes) {
+  const size_t off = ((x_floats + 3) & ~(size_t)3) * sizeof(float);
+  const size_t bytes = (size_t)nrows * rb;
+  if (nrows <= 0 || off + bytes > smem_bytes) return nullptr;
+  unsigned char* dst = reinterpret_cast<unsigned char*>(smem) + off;
+  const unsigned char* src = static_cast<const unsigned char*>(W) + (size_t)row0 * rb;
+  for (size_t c = threadIdx.x; c < bytes / 16; c += kPT) cp_async16_g2s(dst + 16 * c, src + 16 * c);
+  return dst;
+}
+
+__device__ __forceinline__ void cp_async_join() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
   DEFER_CTA_SYNC();
 }
 
@@ -672,68 +853,213 @@ static __device__ void ph_finalize(const DBatch& bt, int cta, int ncta) {
 }
 
 // ----------------------------------------------------------------- GEMVs
+// Register-tiled projections for wide slot groups (G >= 8): a warp task is
+// a tile of NU row units x 8 slots (warp_tile). The CTA's units [u0, u1)
+// are cut into blocks of NU from u0; a block that would run past the last
+// unit of the matrix is shifted back (its first units, which belong to the
+// block or CTA before, are computed again and not written), so every tile
+// reads whole rows. The CTA stages the union of its blocks' rows, [s0, s1).
+struct TileBlocks {
+  int nblk;    // blocks of this CTA
+  int s0, s1;  // units the blocks read
+};
+
+__device__ __forceinline__ TileBlocks tile_blocks(int u0, int u1, int units, int NU) {
+  TileBlocks t;
+  t.nblk = (u1 - u0 + NU - 1) / NU;
+  t.s0 = min(u0, units - NU);
+  t.s1 = min(u0 + NU * t.nblk, units);
+  return t;
+}
+
+// Nominal first unit of block i (the units it writes are [ub, min(ub + NU,
+// u1))) and the first unit it computes.
+__device__ __forceinline__ void tile_block(int u0, int i, int units, int NU, int& ub, int& ua) {
+  ub = u0 + NU * i;
+  ua = min(ub, units - NU);
+}
+
+// Epilogue of QKV unit u (rows 2u, 2u+1) for slot b at position pos: bias,
+// RoPE of the pair (i, i + HALF) of a Q or K head, store to q or the cache.
+__device__ __forceinline__ void qkv_store(const DModel& m, const DLayer& Ly, const DBatch& bt, int l, int u, int b,
+                                          int pos, float a, float c) {
+  const int qh = m.QD / 2, kh = m.KVD / 2;
+  int sect, h, i;
+  if (u < qh) {
+    sect = 0;
+    h = u / m.HALF;
+    i = u % m.HALF;
+  } else if (u < qh + kh) {
+    sect = 1;
+    h = (u - qh) / m.HALF;
+    i = (u - qh) % m.HALF;
+  } else {
+    sect = 2;
+    h = (u - qh - kh) / m.HALF;
+    i = (u - qh - kh) % m.HALF;
+  }
+  if (Ly.bqkv) {
+    a = __fadd_rn(a, Ly.bqkv[2 * u]);
+    c = __fadd_rn(c, Ly.bqkv[2 * u + 1]);
+  }
+  if (sect < 2) {
+    const float cs = m.rope_cos[(size_t)pos * m.HALF + i];
+    const float sn = m.rope_sin[(size_t)pos * m.HALF + i];
+    const float a2 = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(c, sn));
+    const float c2 = __fadd_rn(__fmul_rn(c, cs), __fmul_rn(a, sn));
+    a = a2;
+    c = c2;
+  }
+  if (sect == 0) {
+    float* q = bt.q + (size_t)b * m.QD + h * m.HD;
+    q[i] = a;
+    q[i + m.HALF] = c;
+  } else {
+    const DSession& S = bt.sess[b];
+    float* dst = (sect == 1 ? S.kc : S.vc) + (((size_t)l * m.NKV + h) * S.cap + pos) * m.HD;
+    dst[i] = a;
+    dst[i + m.HALF] = c;
+  }
+}
+
+// act(gate) * up (SiLU or tanh-GELU), ops.rs:120-134.
+__device__ __forceinline__ float gate_act_mul(const DModel& m, float gate, float up) {
+  float act;
+  if (m.gelu) {
+    const float C = 0.7978846f;
+    const float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, gate), gate), gate);
+    act = __fmul_rn(__fmul_rn(0.5f, gate), __fadd_rn(1.0f, tanhf(__fmul_rn(C, __fadd_rn(gate, x3)))));
+  } else {
+    act = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
+  }
+  return __fmul_rn(act, up);
+}
+
+// Pair projection (QKV or gate/up) of a wide slot group: tiles of 4 row
+// pairs x 8 slots; lane L ends holding slot L / 4 of the group's sub-group
+// and the pair (rows 2 (L % 4), 2 (L % 4) + 1) of its block.
+template <bool BF16, int G, bool GU>
+__device__ void ph_pairs_wide(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
+  const DLayer& Ly = m.layers[l];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = GU ? m.FF : m.QKVR / 2;
+  const void* W = GU ? Ly.wgu : Ly.wqkv;
+  const float* nw = GU ? Ly.ffn_norm : Ly.attn_norm;
+  constexpr int NU = 4, NSUB = G / 8;
+  int u0, u1;
+  cta_range(units, cta, ncta, u0, u1);
+  if (u0 >= u1) return;
+  const TileBlocks tb = tile_blocks(u0, u1, units, NU);
+  const size_t rb = row_bytes(m.H, BF16);
+  const unsigned char* wsm =
+      stage_weights(W, 2 * tb.s0, 2 * (tb.s1 - tb.s0), rb, smem, (size_t)G * m.H, bt.smem_bytes);
+  const unsigned char* wg = static_cast<const unsigned char*>(W);
+  for (int b0 = 0; b0 < bt.B; b0 += G) {
+    stage_norm<G>(m, bt, b0, nw, bt.x, smem);
+    for (int task = warp; task < tb.nblk * NSUB; task += kPW) {
+      const int blk = task / NSUB, sub = task % NSUB;
+      int ub, ua;
+      tile_block(u0, blk, units, NU, ub, ua);
+      float res[2];
+      const float* xs = smem + (size_t)sub * 8 * m.H;
+      if (wsm) warp_tile<BF16, true, true, 8, 8>(wsm + (size_t)2 * (ua - tb.s0) * rb, rb, 7, m.H, xs, m.H, res);
+      else warp_tile<BF16, false, true, 8, 8>(wg + (size_t)2 * ua * rb, rb, 7, m.H, xs, m.H, res);
+      const int u = ua + (lane & 3), gg = sub * 8 + (lane >> 2), b = b0 + gg;
+      if (u < ub || u >= u1 || !g_act[gg]) continue;
+      if (GU) bt.g[(size_t)b * m.FF + u] = gate_act_mul(m, res[0], res[1]);
+      else qkv_store(m, Ly, bt, l, u, b, g_pos[gg], res[0], res[1]);
+    }
+    DEFER_CTA_SYNC();
+  }
+}
+
+// x[b] += W x_in[b] for a wide slot group: tiles of 4 rows x 8 slots; lane
+// L ends holding row L % 4 of its block for slot L / 4 of the sub-group.
+template <bool BF16, int G>
+__device__ void ph_residual_wide(const DModel& m, const DBatch& bt, const void* W, int K, const float* xin, int cta,
+                                 int ncta, float* smem, size_t smem_floats) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NU = 4, NSUB = G / 8;
+  const int units = m.H;
+  int u0, u1;
+  cta_range(units, cta, ncta, u0, u1);
+  if (u0 >= u1) return;
+  const TileBlocks tb = tile_blocks(u0, u1, units, NU);
+  const size_t rb = row_bytes(K, BF16);
+  const bool staged = (size_t)G * K <= smem_floats;
+  const unsigned char* wsm =
+      stage_weights(W, tb.s0, tb.s1 - tb.s0, rb, smem, staged ? (size_t)G * K : 0, bt.smem_bytes);
+  const unsigned char* wg = static_cast<const unsigned char*>(W);
+  for (int b0 = 0; b0 < bt.B; b0 += G) {
+    if (staged) {
+      stage_copy<G>(bt, b0, xin, K, smem);
+    } else {
+      load_slot_state<G>(bt, b0);
+      cp_async_join();  // the weight rows
+    }
+    for (int task = warp; task < tb.nblk * NSUB; task += kPW) {
+      const int blk = task / NSUB, sub = task % NSUB;
+      int ub, ua;
+      tile_block(u0, blk, units, NU, ub, ua);
+      float res[1];
+      const unsigned char* w0 = wsm ? wsm + (size_t)(ua - tb.s0) * rb : wg + (size_t)ua * rb;
+      if (staged) {
+        const float* xs = smem + (size_t)sub * 8 * K;
+        if (wsm) warp_tile<BF16, true, true, 4, 8>(w0, rb, 3, K, xs, K, res);
+        else warp_tile<BF16, false, true, 4, 8>(w0, rb, 3, K, xs, K, res);
+      } else {
+        const float* xs = xin + (size_t)(b0 + sub * 8) * K;
+        if (wsm) warp_tile<BF16, true, false, 4, 8>(w0, rb, 3, K, xs, K, res);
+        else warp_tile<BF16, false, false, 4, 8>(w0, rb, 3, K, xs, K, res);
+      }
+      const int r = ua + (lane & 3), gg = sub * 8 + (lane >> 2), b = b0 + gg;
+      if (r < ub || r >= u1 || !g_act[gg]) continue;
+      float* x = bt.x + (size_t)b * m.H + r;
+      *x = __fadd_rn(ld_f(x), res[0]);
+    }
+    DEFER_CTA_SYNC();  // the group's slot state and staged rows are reused by the next group
+  }
+}
+
 // QKV projection (RMSNorm staged in smem) + bias + RoPE + KV append.
 // Unit = row pair (rows 2u, 2u+1 of the pair-interleaved wqkv).
 template <bool BF16, int G>
 __device__ void ph_qkv(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   const DLayer& Ly = m.layers[l];
   prefetch_rows(Ly.wo, m.H, m.QD, BF16, m.H, 1, cta, ncta);  // the O projection comes next
+  if constexpr (G >= 8) {
+    ph_pairs_wide<BF16, G, false>(m, bt, l, cta, ncta, smem);
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = m.QKVR / 2;
   int u0, u1;
   cta_range(units, cta, ncta, u0, u1);
   if (u0 >= u1) return;
   const size_t rb = row_bytes(m.H, BF16);
-  const int qh = m.QD / 2, kh = m.KVD / 2;
+  const unsigned char* wsm =
+      stage_weights(Ly.wqkv, 2 * u0, 2 * (u1 - u0), rb, smem, (size_t)G * m.H, bt.smem_bytes);
+  // a wide slot group is split into sub-groups of up to 8 slots; tasks
+  // (row unit, sub-group) spread over the warps (same arithmetic per slot)
+  constexpr int GS = G < 8 ? G : 8, NS = G / GS;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
     stage_norm<G>(m, bt, b0, Ly.attn_norm, bt.x, smem);
-    for (int u = u0 + warp; u < u1; u += kPW) {
-      const char* base = reinterpret_cast<const char*>(Ly.wqkv);
-      const void* rows[2] = {base + (size_t)(2 * u) * rb, base + (size_t)(2 * u + 1) * rb};
-      float acc[2][G];
-      warp_dot<BF16, true, 2, G>(rows, m.H, smem, m.H, acc);
-      int sect, h, i;
-      if (u < qh) {
-        sect = 0;
-        h = u / m.HALF;
-        i = u % m.HALF;
-      } else if (u < qh + kh) {
-        sect = 1;
-        h = (u - qh) / m.HALF;
-        i = (u - qh) % m.HALF;
+    for (int task = warp; task < (u1 - u0) * NS; task += kPW) {
+      const int u = u0 + task / NS, sub = task % NS;
+      float acc[2][GS];
+      if (wsm) {
+        const void* rows[2] = {wsm + (size_t)(2 * (u - u0)) * rb, wsm + (size_t)(2 * (u - u0) + 1) * rb};
+        warp_dot<BF16, true, 2, GS, true>(rows, m.H, smem + (size_t)sub * GS * m.H, m.H, acc);
       } else {
-        sect = 2;
-        h = (u - qh - kh) / m.HALF;
-        i = (u - qh - kh) % m.HALF;
+        const char* base = reinterpret_cast<const char*>(Ly.wqkv);
+        const void* rows[2] = {base + (size_t)(2 * u) * rb, base + (size_t)(2 * u + 1) * rb};
+        warp_dot<BF16, true, 2, GS>(rows, m.H, smem + (size_t)sub * GS * m.H, m.H, acc);
       }
 #pragma unroll
-      for (int g = 0; g < G; g++) {
-        const int b = b0 + g;
-        if (lane != g || b >= bt.B || !ld_i(&bt.st[b].active)) continue;
-        float a = acc[0][g], c = acc[1][g];
-        if (Ly.bqkv) {
-          a = __fadd_rn(a, Ly.bqkv[2 * u]);
-          c = __fadd_rn(c, Ly.bqkv[2 * u + 1]);
-        }
-        const int pos = ld_i(&bt.st[b].pos);
-        if (sect < 2) {
-          const float cs = m.rope_cos[(size_t)pos * m.HALF + i];
-          const float sn = m.rope_sin[(size_t)pos * m.HALF + i];
-          const float a2 = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(c, sn));
-          const float c2 = __fadd_rn(__fmul_rn(c, cs), __fmul_rn(a, sn));
-          a = a2;
-          c = c2;
-        }
-        if (sect == 0) {
-          float* q = bt.q + (size_t)b * m.QD + h * m.HD;
-          q[i] = a;
-          q[i + m.HALF] = c;
-        } else {
-          const DSession& S = bt.sess[b];
-          float* dst = (sect == 1 ? S.kc : S.vc) + (((size_t)l * m.NKV + h) * S.cap + pos) * m.HD;
-          dst[i] = a;
-          dst[i + m.HALF] = c;
-        }
+      for (int g = 0; g < GS; g++) {
+        const int gg = sub * GS + g, b = b0 + gg;
+        if (lane != g || !g_act[gg]) continue;
+        qkv_store(m, Ly, bt, l, u, b, g_pos[gg], acc[0][g], acc[1][g]);
       }
     }
     DEFER_CTA_SYNC();
@@ -744,28 +1070,48 @@ __device__ void ph_qkv(const DModel& m, const DBatch& bt, int l, int cta, int nc
 template <bool BF16, int G>
 __device__ void ph_residual_gemv(const DModel& m, const DBatch& bt, const void* W, int K, const float* xin,
                                  int cta, int ncta, float* smem, size_t smem_floats) {
+  if constexpr (G >= 8) {
+    ph_residual_wide<BF16, G>(m, bt, W, K, xin, cta, ncta, smem, smem_floats);
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int u0, u1;
   cta_range(m.H, cta, ncta, u0, u1);
   if (u0 >= u1) return;
   const size_t rb = row_bytes(K, BF16);
   const bool staged = (size_t)G * K <= smem_floats;
+  const unsigned char* wsm = stage_weights(W, u0, u1 - u0, rb, smem, staged ? (size_t)G * K : 0, bt.smem_bytes);
+  // a wide slot group is split into sub-groups of up to 8 slots; tasks
+  // (row unit, sub-group) spread over the warps (same arithmetic per slot)
+  constexpr int GS = G < 8 ? G : 8, NS = G / GS;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
-    if (staged) stage_copy<G>(bt, b0, xin, K, smem);
-    for (int r = u0 + warp; r < u1; r += kPW) {
-      const void* rows[1] = {reinterpret_cast<const char*>(W) + (size_t)r * rb};
-      float acc[1][G];
-      if (staged) warp_dot<BF16, true, 1, G>(rows, K, smem, K, acc);
-      else warp_dot<BF16, false, 1, G>(rows, K, xin + (size_t)b0 * K, K, acc);
+    if (staged) {
+      stage_copy<G>(bt, b0, xin, K, smem);
+    } else {
+      load_slot_state<G>(bt, b0);
+      cp_async_join();  // the weight rows
+    }
+    for (int task = warp; task < (u1 - u0) * NS; task += kPW) {
+      const int r = u0 + task / NS, sub = task % NS;
+      float acc[1][GS];
+      if (wsm) {
+        const void* rows[1] = {wsm + (size_t)(r - u0) * rb};
+        if (staged) warp_dot<BF16, true, 1, GS, true>(rows, K, smem + (size_t)sub * GS * K, K, acc);
+        else warp_dot<BF16, false, 1, GS, true>(rows, K, xin + (size_t)(b0 + sub * GS) * K, K, acc);
+      } else {
+        const void* rows[1] = {reinterpret_cast<const char*>(W) + (size_t)r * rb};
+        if (staged) warp_dot<BF16, true, 1, GS>(rows, K, smem + (size_t)sub * GS * K, K, acc);
+        else warp_dot<BF16, false, 1, GS>(rows, K, xin + (size_t)(b0 + sub * GS) * K, K, acc);
+      }
 #pragma unroll
-      for (int g = 0; g < G; g++) {
-        const int b = b0 + g;
-        if (lane != g || b >= bt.B || !ld_i(&bt.st[b].active)) continue;
+      for (int g = 0; g < GS; g++) {
+        const int gg = sub * GS + g, b = b0 + gg;
+        if (lane != g || !g_act[gg]) continue;
         float* x = bt.x + (size_t)b * m.H + r;
         *x = __fadd_rn(ld_f(x), acc[0][g]);
       }
     }
-    if (staged) DEFER_CTA_SYNC();
+    DEFER_CTA_SYNC();  // the group's slot state and staged rows are reused by the next group
   }
 }
 
@@ -774,33 +1120,86 @@ template <bool BF16, int G>
 __device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   const DLayer& Ly = m.layers[l];
   prefetch_rows(Ly.wdown, m.H, m.FF, BF16, m.H, 1, cta, ncta);  // the down projection comes next
+  if constexpr (G >= 8) {
+    ph_pairs_wide<BF16, G, true>(m, bt, l, cta, ncta, smem);
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int u0, u1;
   cta_range(m.FF, cta, ncta, u0, u1);
   if (u0 >= u1) return;
   const size_t rb = row_bytes(m.H, BF16);
+  const unsigned char* wsm = stage_weights(Ly.wgu, 2 * u0, 2 * (u1 - u0), rb, smem, (size_t)G * m.H, bt.smem_bytes);
+  // a wide slot group is split into sub-groups of up to 8 slots; tasks
+  // (row unit, sub-group) spread over the warps (same arithmetic per slot)
+  constexpr int GS = G < 8 ? G : 8, NS = G / GS;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
     stage_norm<G>(m, bt, b0, Ly.ffn_norm, bt.x, smem);
-    for (int j = u0 + warp; j < u1; j += kPW) {
-      const char* base = reinterpret_cast<const char*>(Ly.wgu);
-      const void* rows[2] = {base + (size_t)(2 * j) * rb, base + (size_t)(2 * j + 1) * rb};
-      float acc[2][G];
-      warp_dot<BF16, true, 2, G>(rows, m.H, smem, m.H, acc);
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-        const int b = b0 + g;
-        if (lane != g || b >= bt.B || !ld_i(&bt.st[b].active)) continue;
-        const float gate = acc[0][g], up = acc[1][g];
-        float act;
-        if (m.gelu) {
-          const float C = 0.7978846f;
-          const float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, gate), gate), gate);
-          act = __fmul_rn(__fmul_rn(0.5f, gate), __fadd_rn(1.0f, tanhf(__fmul_rn(C, __fadd_rn(gate, x3)))));
-        } else {
-          act = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
-        }
-        bt.g[(size_t)b * m.FF + j] = __fmul_rn(act, up);
+    for (int task = warp; task < (u1 - u0) * NS; task += kPW) {
+      const int j = u0 + task / NS, sub = task % NS;
+      float acc[2][GS];
+      if (wsm) {
+        const void* rows[2] = {wsm + (size_t)(2 * (j - u0)) * rb, wsm + (size_t)(2 * (j - u0) + 1) * rb};
+        warp_dot<BF16, true, 2, GS, true>(rows, m.H, smem + (size_t)sub * GS * m.H, m.H, acc);
+      } else {
+        const char* base = reinterpret_cast<const char*>(Ly.wgu);
+        const void* rows[2] = {base + (size_t)(2 * j) * rb, base + (size_t)(2 * j + 1) * rb};
+        warp_dot<BF16, true, 2, GS>(rows, m.H, smem + (size_t)sub * GS * m.H, m.H, acc);
       }
+#pragma unroll
+      for (int g = 0; g < GS; g++) {
+        const int gg = sub * GS + g, b = b0 + gg;
+        if (lane != g || !g_act[gg]) continue;
+        bt.g[(size_t)b * m.FF + j] = gate_act_mul(m, acc[0][g], acc[1][g]);
+      }
+    }
+    DEFER_CTA_SYNC();
+  }
+}
+
+// Final RMSNorm + lm_head + sampler block statistics for a wide slot group:
+// a warp task is (vocabulary block of kSBlk rows, sub-group of 8 slots),
+// four tiles of 8 rows x 8 slots; the tile sums pass through a per-warp
+// [8 slots][kSBlk rows] buffer so that lane r holds row r of each slot.
+template <bool BF16, int G>
+__device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = bt.nblk;
+  constexpr int NSUB = G / 8;
+  static_assert(kSBlk == 32, "head tiles cover a 32-row block");
+  int u0, u1;
+  cta_range(nb, cta, ncta, u0, u1);
+  if (u0 >= u1) return;
+  const size_t rb = row_bytes(m.H, BF16);
+  float* tbuf = smem + (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)warp * 8 * kSBlk;
+  const unsigned char* wg = static_cast<const unsigned char*>(m.head);
+  for (int b0 = 0; b0 < bt.B; b0 += G) {
+    stage_norm<G>(m, bt, b0, m.norm, bt.x, smem);
+    for (int task = warp; task < (u1 - u0) * NSUB; task += kPW) {
+      const int k = u0 + task / NSUB, sub = task % NSUB;
+      const float* xs = smem + (size_t)sub * 8 * m.H;
+#pragma unroll 1
+      for (int t = 0; t < kSBlk / 8; t++) {
+        const int r0 = min(k * kSBlk + 8 * t, m.V - 1);
+        float res[2];
+        warp_tile<BF16, false, true, 8, 8>(wg + (size_t)r0 * rb, rb, m.V - 1 - r0, m.H, xs, m.H, res);
+        const int s = lane >> 2, r = 8 * t + 2 * (lane & 3);
+        tbuf[s * kSBlk + r] = res[0];
+        tbuf[s * kSBlk + r + 1] = res[1];
+      }
+      __syncwarp();
+      const int i = k * kSBlk + lane;
+      const bool valid = i < m.V;
+#pragma unroll 1
+      for (int s = 0; s < 8; s++) {
+        const int gg = sub * 8 + s, b = b0 + gg;
+        if (!g_act[gg]) continue;
+        const float v = tbuf[s * kSBlk + lane];
+        if (valid) bt.logits[(size_t)b * m.V + i] = v;
+        const size_t o = (size_t)b * nb + k;
+        block_stats(v, i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+      }
+      __syncwarp();
     }
     DEFER_CTA_SYNC();
   }
@@ -811,26 +1210,34 @@ __device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int
 template <bool BF16, int G>
 __device__ void ph_head(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
   prefetch_rows(m.layers[0].wqkv, m.QKVR, m.H, BF16, m.QKVR / 2, 2, cta, ncta);  // next step's first phase
+  if constexpr (G >= 8) {
+    ph_head_wide<BF16, G>(m, bt, cta, ncta, smem);
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = bt.nblk;
   int u0, u1;
   cta_range(nb, cta, ncta, u0, u1);
   if (u0 >= u1) return;
   const size_t rb = row_bytes(m.H, BF16);
+  // a wide slot group is split into sub-groups of up to 8 slots; tasks
+  // (row unit, sub-group) spread over the warps (same arithmetic per slot)
+  constexpr int GS = G < 8 ? G : 8, NS = G / GS;
   for (int b0 = 0; b0 < bt.B; b0 += G) {
     stage_norm<G>(m, bt, b0, m.norm, bt.x, smem);
-    for (int k = u0 + warp; k < u1; k += kPW) {
-      float mine[G];
+    for (int task = warp; task < (u1 - u0) * NS; task += kPW) {
+      const int k = u0 + task / NS, sub = task % NS;
+      float mine[GS];
 #pragma unroll
-      for (int g = 0; g < G; g++) mine[g] = NAN;
+      for (int g = 0; g < GS; g++) mine[g] = NAN;
       for (int r = 0; r < kSBlk; r += 2) {
         const int row0 = min(k * kSBlk + r, m.V - 1), row1 = min(k * kSBlk + r + 1, m.V - 1);
         const void* rows[2] = {reinterpret_cast<const char*>(m.head) + (size_t)row0 * rb,
                                reinterpret_cast<const char*>(m.head) + (size_t)row1 * rb};
-        float acc[2][G];
-        warp_dot<BF16, true, 2, G>(rows, m.H, smem, m.H, acc);
+        float acc[2][GS];
+        warp_dot<BF16, true, 2, GS>(rows, m.H, smem + (size_t)sub * GS * m.H, m.H, acc);
 #pragma unroll
-        for (int g = 0; g < G; g++) {
+        for (int g = 0; g < GS; g++) {
           if (lane == r) mine[g] = acc[0][g];
           if (lane == r + 1) mine[g] = acc[1][g];
         }
@@ -838,9 +1245,9 @@ __device__ void ph_head(const DModel& m, const DBatch& bt, int cta, int ncta, fl
       const int i = k * kSBlk + lane;
       const bool valid = i < m.V;
 #pragma unroll
-      for (int g = 0; g < G; g++) {
-        const int b = b0 + g;
-        if (b >= bt.B || !ld_i(&bt.st[b].active)) continue;
+      for (int g = 0; g < GS; g++) {
+        const int gg = sub * GS + g, b = b0 + gg;
+        if (!g_act[gg]) continue;
         if (valid) bt.logits[(size_t)b * m.V + i] = mine[g];
         const size_t o = (size_t)b * nb + k;
         block_stats(mine[g], i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
@@ -947,18 +1354,26 @@ __device__ __forceinline__ bool any_sampling(const DBatch& bt) {
 // ------------------------------------------------------------- attention
 // Partial attention of one key chunk for the query heads of one KV head;
 // the CTA finishing the last chunk of a (slot, KV head) combines all its
-// chunks in chunk order. CTA unit = (slot, kv head, chunk).
+// chunks in chunk order. CTA unit = (slot, kv head, chunk). The chunk's K/V
+// rows and, for the combine, each head's partials are staged in shared
+// memory with every load of a batch issued before its stores.
+constexpr int kAttnBatch = 4;  // float4 loads of K (and of V) per thread in flight
+
 static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   {  // the gate/up projection comes after the O projection
     const DLayer& Ly = m.layers[l];
     prefetch_rows(Ly.wgu, 2 * m.FF, m.H, m.bf16 != 0, m.FF, 2, cta, ncta);
   }
-  const int G = m.NH / m.NKV;
+  const int G = m.NH / m.NKV, HD = m.HD;
   const int maxc = bt.max_chunks;
   const int units = bt.B * m.NKV * maxc;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* qs = smem;             // [G][HD]
-  float* sc = smem + G * m.HD;  // [G][kAttnChunk]
+  const int c4n = HD / 4;
+  float* qs = smem;                         // [G][HD]
+  float* sc = qs + G * HD;                  // [G][kAttnChunk]
+  float* ks = sc + G * kAttnChunk;          // [kAttnChunk][HD + 4]
+  float* vs = ks + kAttnChunk * (HD + 4);   // [kAttnChunk][HD]
+  float* pc = ks;                           // combine: [nch][HD + 2] of one head (reuses ks/vs)
   __shared__ int s_last;
   for (int u = cta; u < units; u += ncta) {
     const int b = u / (m.NKV * maxc);
@@ -971,22 +1386,43 @@ static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta
     const DSession& S = bt.sess[b];
     const int t0 = c * kAttnChunk;
     const int tn = min(kAttnChunk, pos + 1 - t0);
-    const float* qsrc = bt.q + (size_t)b * m.QD + (size_t)kvh * G * m.HD;
-    for (int i = tid; i < G * m.HD; i += kPT) qs[i] = ld_f(qsrc + i);
-    DEFER_CTA_SYNC();
+    const float* qsrc = bt.q + (size_t)b * m.QD + (size_t)kvh * G * HD;
     const size_t head_base = ((size_t)l * m.NKV + kvh) * S.cap;
-    const float* kb = S.kc + (head_base + t0) * m.HD;
+    for (int i = tid; i < G * HD; i += kPT) qs[i] = ld_f(qsrc + i);
+    for (int base = 0; base < tn * c4n; base += kAttnBatch * kPT) {
+      float4 kv[kAttnBatch], vv[kAttnBatch];
+#pragma unroll
+      for (int k = 0; k < kAttnBatch; k++) {
+        const int idx = base + tid + k * kPT;
+        if (idx < tn * c4n) {
+          const int tt = idx / c4n, c4 = idx - tt * c4n;
+          kv[k] = ld_act(S.kc + (head_base + t0 + tt) * HD + 4 * c4);
+          vv[k] = ld_act(S.vc + (head_base + t0 + tt) * HD + 4 * c4);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kAttnBatch; k++) {
+        const int idx = base + tid + k * kPT;
+        if (idx < tn * c4n) {
+          const int tt = idx / c4n, c4 = idx - tt * c4n;
+          *reinterpret_cast<float4*>(ks + (size_t)tt * (HD + 4) + 4 * c4) = kv[k];
+          *reinterpret_cast<float4*>(vs + (size_t)tt * HD + 4 * c4) = vv[k];
+        }
+      }
+    }
+    DEFER_CTA_SYNC();
     for (int idx = tid; idx < G * kAttnChunk; idx += kPT) {
-      const int h = idx / kAttnChunk, tt = idx % kAttnChunk;
+      const int h = idx / kAttnChunk, tt = idx - h * kAttnChunk;
       float s = -INFINITY;
       const int t = t0 + tt;
       const bool masked = S.mask && t < pos && ((S.mask[t >> 5] >> (t & 31)) & 1u);
       if (tt < tn && !masked) {
-        const float* kr = kb + (size_t)tt * m.HD;
-        const float* qr = qs + h * m.HD;
+        const float* kr = ks + (size_t)tt * (HD + 4);
+        const float* qr = qs + h * HD;
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-        for (int d = 0; d < m.HD; d += 4) {
-          const float4 k4 = ld_act(kr + d);
+#pragma unroll 4
+        for (int d = 0; d < HD; d += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
           a0 = fmaf(qr[d], k4.x, a0);
           a1 = fmaf(qr[d + 1], k4.y, a1);
           a2 = fmaf(qr[d + 2], k4.z, a2);
@@ -997,7 +1433,7 @@ static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta
       sc[idx] = s;
     }
     DEFER_CTA_SYNC();
-    float* part_b = bt.part + (size_t)b * m.NH * maxc * (m.HD + 2);
+    float* part_b = bt.part + (size_t)b * m.NH * maxc * (HD + 2);
     for (int h = warp; h < G; h += kPW) {
       float* row = sc + h * kAttnChunk;
       const float v0 = row[lane], v1 = row[lane + 32];
@@ -1008,19 +1444,19 @@ static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta
       row[lane + 32] = e1;
       const float ls = warp_sum_butterfly(__fadd_rn(e0, e1));
       if (lane == 0) {
-        float* p = part_b + ((size_t)(kvh * G + h) * maxc + c) * (m.HD + 2);
+        float* p = part_b + ((size_t)(kvh * G + h) * maxc + c) * (HD + 2);
         p[0] = mx;
         p[1] = ls;
       }
     }
     DEFER_CTA_SYNC();
-    const float* vb = S.vc + (head_base + t0) * m.HD;
-    for (int idx = tid; idx < G * m.HD; idx += kPT) {
-      const int h = idx / m.HD, d = idx % m.HD;
+    for (int idx = tid; idx < G * HD; idx += kPT) {
+      const int h = idx / HD, d = idx - h * HD;
       const float* e = sc + h * kAttnChunk;
       float acc = 0.0f;
-      for (int tt = 0; tt < tn; tt++) acc = fmaf(e[tt], ld_f(vb + (size_t)tt * m.HD + d), acc);
-      part_b[((size_t)(kvh * G + h) * maxc + c) * (m.HD + 2) + 2 + d] = acc;
+#pragma unroll 8
+      for (int tt = 0; tt < tn; tt++) acc = fmaf(e[tt], vs[(size_t)tt * HD + d], acc);
+      part_b[((size_t)(kvh * G + h) * maxc + c) * (HD + 2) + 2 + d] = acc;
     }
     // The last chunk of this (slot, KV head) to finish combines; every
     // writer makes its partials visible GPU-wide before the ticket.
@@ -1038,20 +1474,36 @@ static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta
     }
     DEFER_CTA_SYNC();
     if (s_last) {
-      for (int idx = tid; idx < G * m.HD; idx += kPT) {
-        const int h = idx / m.HD, d = idx % m.HD;
-        const float* p = part_b + (size_t)(kvh * G + h) * maxc * (m.HD + 2);
-        float M = -INFINITY;
-        for (int cc = 0; cc < nch; cc++) M = fmaxf(M, ld_f(p + (size_t)cc * (m.HD + 2)));
-        float L = 0.0f, O = 0.0f;
-        for (int cc = 0; cc < nch; cc++) {
-          const float* pc = p + (size_t)cc * (m.HD + 2);
-          const float mc = ld_f(pc), lc = ld_f(pc + 1), ac = ld_f(pc + 2 + d);
-          const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
-          L = fmaf(w, lc, L);
-          O = fmaf(w, ac, O);
+      const int row = HD + 2;
+      for (int h = 0; h < G; h++) {
+        const float* p = part_b + (size_t)(kvh * G + h) * maxc * row;
+        for (int base = 0; base < nch * row; base += kAttnBatch * kPT) {
+          float v[kAttnBatch];
+#pragma unroll
+          for (int k = 0; k < kAttnBatch; k++) {
+            const int idx = base + tid + k * kPT;
+            if (idx < nch * row) v[k] = ld_f(p + idx);
+          }
+#pragma unroll
+          for (int k = 0; k < kAttnBatch; k++) {
+            const int idx = base + tid + k * kPT;
+            if (idx < nch * row) pc[idx] = v[k];
+          }
         }
-        bt.att[(size_t)b * m.QD + (size_t)(kvh * G + h) * m.HD + d] = __fdiv_rn(O, L);
+        DEFER_CTA_SYNC();
+        for (int d = tid; d < HD; d += kPT) {
+          float M = -INFINITY;
+          for (int cc = 0; cc < nch; cc++) M = fmaxf(M, pc[cc * row]);
+          float L = 0.0f, O = 0.0f;
+          for (int cc = 0; cc < nch; cc++) {
+            const float mc = pc[cc * row], lc = pc[cc * row + 1], ac = pc[cc * row + 2 + d];
+            const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
+            L = fmaf(w, lc, L);
+            O = fmaf(w, ac, O);
+          }
+          bt.att[(size_t)b * m.QD + (size_t)(kvh * G + h) * HD + d] = __fdiv_rn(O, L);
+        }
+        DEFER_CTA_SYNC();
       }
     }
     DEFER_CTA_SYNC();

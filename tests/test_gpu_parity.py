@@ -111,6 +111,21 @@ def test_token_loop_paths_agree_on_a_batch(mdir, n):
     assert outs["flow"] == outs["barrier"] == outs["phased"]
 
 
+def test_wide_slot_groups_agree_with_single_sessions(mdir):
+    """20 sessions run as one 32-slot group (grid-barrier and per-phase
+    kernels) give the tokens each session gives alone (dataflow kernel)."""
+    gm = D.Model.load(model_file(mdir, "test-small"))
+    n = 20
+    prompts = [_tokens(gm.config.vocab_size, 3 + (7 * i) % 40, 200 + i) for i in range(n)]
+    seeds = [D.seed_from_u64(300 + i) for i in range(n)]
+    temps = [[0.0, 0.8, 1.2][i % 3] for i in range(n)]
+    maxt = [5 + (11 * i) % 23 for i in range(n)]
+    wide = {p: _on_path(p, lambda: D.generate_batch(gm, prompts, seeds, temps, maxt, batch=32)[0])
+            for p in ("barrier", "phased")}
+    alone = _on_path("flow", lambda: D.generate_batch(gm, prompts, seeds, temps, maxt, batch=1)[0])
+    assert wide["barrier"] == wide["phased"] == alone
+
+
 def test_token_loop_paths_agree_on_benchmark_shape(mdir):
     """The 135M shape across all SMs: the dataflow and grid-barrier kernels
     give the same sampled stream, logits and cache bits."""
