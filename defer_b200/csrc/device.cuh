@@ -136,6 +136,8 @@ struct DBatch {
   unsigned* bar;          // grid barrier counter
   unsigned smem_bytes;    // dynamic shared memory of the launch (stages copy
                           // their weight rows into what their inputs leave free)
+  int parts;              // wide projections: CTA partitions, each owning every
+                          // parts-th slot group and all rows of the matrix
 };
 
 }  // namespace defer

@@ -173,6 +173,8 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   bt.status = d_ctrl_;
   bt.any_active = d_ctrl_ + 1;
   bt.bar = reinterpret_cast<unsigned*>(d_ctrl_ + 3);
+  bt.smem_bytes = 0;  // set by the launchers
+  bt.parts = 1;
   last_steps_ = nsteps;
   const bool persistent = use_persistent();
   FlowPlan plan;

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 
 #include "common.h"
 #include "kernels.h"
@@ -204,11 +205,33 @@ static size_t step_smem_floats(const DModel& m, int B, int max_chunks) {
                              (size_t)max_chunks * (m.HD + 2));
   f = std::max(f, (size_t)(Gh * m.HD + Gh * kAttnChunk) + kv);
   // the wide head: normalized rows plus one [8][kSBlk] tile buffer per warp
-  if (G >= 8) f = std::max(f, (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)kPW * 8 * kSBlk);
+  if (G >= 8) {
+    f = std::max(f, (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)kPW * 8 * kSBlk);
+    const size_t hs = head_staged_floats(G, m.H, m.bf16 != 0);  // staged head, when it fits
+    if (hs * 4 <= 200 * 1024) f = std::max(f, hs);
+  }
   const int nblk = (m.V + kSBlk - 1) / kSBlk;
   const int ng2 = (nblk + 31) / 32;
   f = std::max(f, (size_t)(ng2 + (ng2 + 31) / 32 + 8));
   return (f + 3) & ~(size_t)3;
+}
+
+// CTA partitions of the wide projections (Part in phases.cuh). Each
+// partition reads every weight of a layer through L2 once and each CTA
+// re-reads the activation rows of its partition's slots, so for one layer
+//   L2 bytes ~ P * W + ncta * (B / P) * X
+// with W the weight bytes and X the activation bytes one slot stages; the
+// minimum is at P = sqrt(ncta * B * X / W), capped by the slot groups and
+// by keeping at least 8 CTAs per partition.
+static int parts_for(const DModel& m, int B, int ncta) {
+  const int G = group_for(m, B);
+  if (G < 8) return 1;
+  const int ngroups = (B + G - 1) / G;
+  const double ws = m.bf16 ? 2.0 : 4.0;
+  const double X = 4.0 * (2.0 * m.H + m.QD + m.FF);
+  const double W = ws * ((double)m.QKVR * m.H + (double)m.H * m.QD + 3.0 * (double)m.FF * m.H);
+  int P = (int)std::lround(std::sqrt((double)ncta * B * X / W));
+  return std::max(1, std::min({P, ngroups, ncta / 8}));
 }
 
 size_t step_smem_bytes(const DModel& m, int B, int max_chunks) {
@@ -229,6 +252,7 @@ static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, in
   const size_t smem = sf * sizeof(float);
   DBatch bt = bt0;
   bt.smem_bytes = (unsigned)smem;
+  bt.parts = parts_for(m, bt.B, sms);
   allow_smem(k_select<BF16>, smem);
   allow_smem(k_qkv<BF16, G>, smem);
   allow_smem(k_attn, smem);
@@ -314,6 +338,7 @@ static void persistent_impl(const DModel& m, const DBatch& bt, int nsteps, int s
   DModel mm = m;
   DBatch bb = bt;
   bb.smem_bytes = (unsigned)smem;
+  bb.parts = parts_for(m, bb.B, grid);
   int ns = nsteps;
   unsigned sfl = (unsigned)sf;
   void* args[] = {&mm, &bb, &ns, &sfl};

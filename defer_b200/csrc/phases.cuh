@@ -226,9 +226,14 @@ __device__ __forceinline__ void warp_dot(const void* const (&rows)[NR], int K, c
 // in the same order, as warp_sum_butterfly, so the result is bit-identical;
 // it needs N - N/32 shuffles instead of 5 N. Lane L ends holding the sums
 // k = L * (N/32) + i (k = s * NR + r) as res[i], i < N/32.
-template <bool BF16, bool WSMEM, bool XSMEM, int NR, int NS>
+//
+// With NORM, x_s holds raw rows and every element is normalized as it is
+// loaded, n = (x * inv[s]) * nw[i] (the RMSNorm of ops.rs:84-95, the same
+// products as a staged normalized row).
+template <bool BF16, bool WSMEM, bool XSMEM, int NR, int NS, bool NORM = false>
 __device__ __forceinline__ void warp_tile(const unsigned char* w0, size_t wstride, int rmax, int K, const float* xs,
-                                          int xstride, float (&res)[NR * NS / 32]) {
+                                          int xstride, float (&res)[NR * NS / 32], const float* nw = nullptr,
+                                          const float* inv = nullptr) {
   constexpr int E = WChunk<BF16>::E;
   constexpr int N = NR * NS;
   static_assert(N >= 32 && (N & (N - 1)) == 0, "tile must be a power of two of at least 32 sums");
@@ -237,7 +242,23 @@ __device__ __forceinline__ void warp_tile(const unsigned char* w0, size_t wstrid
   float acc[N];
 #pragma unroll
   for (int k = 0; k < N; k++) acc[k] = 0.0f;
+  float sinv[NORM ? NS : 1];
+  if constexpr (NORM) {
+#pragma unroll
+    for (int s = 0; s < NS; s++) sinv[s] = inv[s];
+  }
   for (int j = lane; j < nch; j += 32) {
+    float wn[NORM ? E : 1];
+    if constexpr (NORM) {
+#pragma unroll
+      for (int q = 0; q < E / 4; q++) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(nw + j * E) + q);
+        wn[4 * q] = t.x;
+        wn[4 * q + 1] = t.y;
+        wn[4 * q + 2] = t.z;
+        wn[4 * q + 3] = t.w;
+      }
+    }
     float w[NR][E];
 #pragma unroll
     for (int r = 0; r < NR; r++) {
@@ -274,6 +295,10 @@ __device__ __forceinline__ void warp_tile(const unsigned char* w0, size_t wstrid
         xv[4 * q + 1] = t.y;
         xv[4 * q + 2] = t.z;
         xv[4 * q + 3] = t.w;
+      }
+      if constexpr (NORM) {
+#pragma unroll
+        for (int e = 0; e < E; e++) xv[e] = __fmul_rn(__fmul_rn(xv[e], sinv[s]), wn[e]);
       }
 #pragma unroll
       for (int r = 0; r < NR; r++)
@@ -354,7 +379,11 @@ __device__ void stage_rows(const DBatch& bt, int b0, const float* src, int K, fl
   if (threadIdx.x < G) g_live[threadIdx.x] = b0 + (int)threadIdx.x < bt.B && (!need_active || g_act[threadIdx.x]);
   DEFER_CTA_SYNC();
   const int n4 = G * K / 4;  // K % 4 == 0
-  for (int f = threadIdx.x; f < n4; f += kPT) {
+  // every CTA copies the same rows: each starts at its own offset so that
+  // they do not all request the same L2 lines at the same moment
+  const int rot = (int)((blockIdx.x * 32u) % (unsigned)n4);
+  for (int f0 = threadIdx.x; f0 < n4; f0 += kPT) {
+    const int f = f0 + rot < n4 ? f0 + rot : f0 + rot - n4;
     const int g = (4 * f) / K;
     if (g_live[g])
       cp_async16_g2s(dst + 4 * (size_t)f, src + (size_t)b0 * K + 4 * (size_t)f);
@@ -365,37 +394,55 @@ __device__ void stage_rows(const DBatch& bt, int b0, const float* src, int K, fl
   DEFER_CTA_SYNC();
 }
 
-// dst[g][i] = rmsnorm(x of slot b0+g)[i] for the G slots of a group
-// (inactive or missing slots get zeros). The raw rows are staged first; a
-// warp then computes each slot's sum of squares with the canonical dot
-// (lane-strided float4 chunks, fmaf in element order, butterfly), and
-// every element is scaled (x * inv) * w in place.
+// Per-slot RMSNorm factors inv = 1 / sqrt(sum(x^2) / n + eps) of the group
+// (g_inv), ops.rs:84-95. The raw rows are staged first; a warp computes the
+// sums of squares of its slots g = warp, warp + kPW, ... side by side, each
+// with the canonical dot (lane-strided float4 chunks, fmaf in element order,
+// butterfly). Missing or inactive slots are zero rows.
+static __shared__ float g_inv[kMaxGroupWide];
+
+template <int G>
+__device__ void stage_rows_inv(const DModel& m, const DBatch& bt, int b0, const float* x, float* dst) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  stage_rows<G>(bt, b0, x, m.H, dst, true);
+  constexpr int Q = (G + kPW - 1) / kPW;
+  float acc[Q];
+#pragma unroll
+  for (int q = 0; q < Q; q++) acc[q] = 0.0f;
+  for (int j = lane; j < m.H / 4; j += 32) {
+#pragma unroll
+    for (int q = 0; q < Q; q++) {
+      const int g = warp + q * kPW;
+      if (g < G) {
+        const float4 t = reinterpret_cast<const float4*>(dst + (size_t)g * m.H)[j];
+        acc[q] = fmaf(t.x, t.x, acc[q]);
+        acc[q] = fmaf(t.y, t.y, acc[q]);
+        acc[q] = fmaf(t.z, t.z, acc[q]);
+        acc[q] = fmaf(t.w, t.w, acc[q]);
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < Q; q++) {
+    const int g = warp + q * kPW;
+    const float ss = warp_sum_butterfly(acc[q]);
+    if (lane == 0 && g < G) g_inv[g] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)m.H), m.eps)));
+  }
+  DEFER_CTA_SYNC();
+}
+
+// dst[g][i] = rmsnorm(x of slot b0+g)[i] = (x * inv) * w for the G slots of
+// a group (inactive or missing slots get zeros), scaled in place.
 template <int G>
 __device__ void stage_norm(const DModel& m, const DBatch& bt, int b0, const float* w_of_layer, const float* x,
                            float* dst) {
-  __shared__ float s_inv[kMaxGroupWide];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  stage_rows<G>(bt, b0, x, m.H, dst, true);
-  for (int g = warp; g < G; g += kPW) {
-    const float4* x4 = reinterpret_cast<const float4*>(dst + (size_t)g * m.H);
-    float acc = 0.0f;
-    for (int j = lane; j < m.H / 4; j += 32) {
-      const float4 t = x4[j];
-      acc = fmaf(t.x, t.x, acc);
-      acc = fmaf(t.y, t.y, acc);
-      acc = fmaf(t.z, t.z, acc);
-      acc = fmaf(t.w, t.w, acc);
-    }
-    acc = warp_sum_butterfly(acc);
-    if (lane == 0) s_inv[g] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)m.H), m.eps)));
-  }
-  DEFER_CTA_SYNC();
+  stage_rows_inv<G>(m, bt, b0, x, dst);
   for (int i = threadIdx.x; i < m.H; i += kPT) {
     const float w = w_of_layer[i];
 #pragma unroll 4
     for (int g = 0; g < G; g++) {
       float* p = dst + (size_t)g * m.H + i;
-      *p = g_live[g] ? __fmul_rn(__fmul_rn(*p, s_inv[g]), w) : 0.0f;
+      *p = g_live[g] ? __fmul_rn(__fmul_rn(*p, g_inv[g]), w) : 0.0f;
     }
   }
   DEFER_CTA_SYNC();
@@ -872,6 +919,25 @@ __device__ __forceinline__ TileBlocks tile_blocks(int u0, int u1, int units, int
   return t;
 }
 
+// CTA partitions of the wide projections: CTA `cta` belongs to partition
+// cta % P, whose CTAs split every row of the matrix among them and take the
+// slot groups P * k + partition. Each CTA then stages only its partition's
+// slots (the activations every CTA re-reads shrink by P) while the weights
+// are read once per partition.
+struct Part {
+  int first;  // first slot of the partition's first group
+  int step;   // slots between its groups
+  int ci;     // CTA index inside the partition
+  int nci;    // CTAs of the partition
+};
+
+template <int G>
+__device__ __forceinline__ Part part_of(const DBatch& bt, int cta, int ncta) {
+  const int P = bt.parts > 1 ? bt.parts : 1;
+  const int p = cta % P;
+  return Part{p * G, P * G, cta / P, (ncta - p + P - 1) / P};
+}
+
 // Nominal first unit of block i (the units it writes are [ub, min(ub + NU,
 // u1))) and the first unit it computes.
 __device__ __forceinline__ void tile_block(int u0, int i, int units, int NU, int& ub, int& ua) {
@@ -946,24 +1012,28 @@ __device__ void ph_pairs_wide(const DModel& m, const DBatch& bt, int l, int cta,
   const void* W = GU ? Ly.wgu : Ly.wqkv;
   const float* nw = GU ? Ly.ffn_norm : Ly.attn_norm;
   constexpr int NU = 4, NSUB = G / 8;
+  const Part pt = part_of<G>(bt, cta, ncta);
   int u0, u1;
-  cta_range(units, cta, ncta, u0, u1);
+  cta_range(units, pt.ci, pt.nci, u0, u1);
   if (u0 >= u1) return;
   const TileBlocks tb = tile_blocks(u0, u1, units, NU);
   const size_t rb = row_bytes(m.H, BF16);
   const unsigned char* wsm =
       stage_weights(W, 2 * tb.s0, 2 * (tb.s1 - tb.s0), rb, smem, (size_t)G * m.H, bt.smem_bytes);
   const unsigned char* wg = static_cast<const unsigned char*>(W);
-  for (int b0 = 0; b0 < bt.B; b0 += G) {
-    stage_norm<G>(m, bt, b0, nw, bt.x, smem);
+  for (int b0 = pt.first; b0 < bt.B; b0 += pt.step) {
+    stage_rows_inv<G>(m, bt, b0, bt.x, smem);
     for (int task = warp; task < tb.nblk * NSUB; task += kPW) {
       const int blk = task / NSUB, sub = task % NSUB;
       int ub, ua;
       tile_block(u0, blk, units, NU, ub, ua);
       float res[2];
       const float* xs = smem + (size_t)sub * 8 * m.H;
-      if (wsm) warp_tile<BF16, true, true, 8, 8>(wsm + (size_t)2 * (ua - tb.s0) * rb, rb, 7, m.H, xs, m.H, res);
-      else warp_tile<BF16, false, true, 8, 8>(wg + (size_t)2 * ua * rb, rb, 7, m.H, xs, m.H, res);
+      const float* inv = g_inv + sub * 8;
+      if (wsm)
+        warp_tile<BF16, true, true, 8, 8, true>(wsm + (size_t)2 * (ua - tb.s0) * rb, rb, 7, m.H, xs, m.H, res, nw, inv);
+      else
+        warp_tile<BF16, false, true, 8, 8, true>(wg + (size_t)2 * ua * rb, rb, 7, m.H, xs, m.H, res, nw, inv);
       const int u = ua + (lane & 3), gg = sub * 8 + (lane >> 2), b = b0 + gg;
       if (u < ub || u >= u1 || !g_act[gg]) continue;
       if (GU) bt.g[(size_t)b * m.FF + u] = gate_act_mul(m, res[0], res[1]);
@@ -981,8 +1051,9 @@ __device__ void ph_residual_wide(const DModel& m, const DBatch& bt, const void* 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int NU = 4, NSUB = G / 8;
   const int units = m.H;
+  const Part pt = part_of<G>(bt, cta, ncta);
   int u0, u1;
-  cta_range(units, cta, ncta, u0, u1);
+  cta_range(units, pt.ci, pt.nci, u0, u1);
   if (u0 >= u1) return;
   const TileBlocks tb = tile_blocks(u0, u1, units, NU);
   const size_t rb = row_bytes(K, BF16);
@@ -990,7 +1061,7 @@ __device__ void ph_residual_wide(const DModel& m, const DBatch& bt, const void* 
   const unsigned char* wsm =
       stage_weights(W, tb.s0, tb.s1 - tb.s0, rb, smem, staged ? (size_t)G * K : 0, bt.smem_bytes);
   const unsigned char* wg = static_cast<const unsigned char*>(W);
-  for (int b0 = 0; b0 < bt.B; b0 += G) {
+  for (int b0 = pt.first; b0 < bt.B; b0 += pt.step) {
     if (staged) {
       stage_copy<G>(bt, b0, xin, K, smem);
     } else {
@@ -1161,20 +1232,17 @@ __device__ void ph_gateup(const DModel& m, const DBatch& bt, int l, int cta, int
 // a warp task is (vocabulary block of kSBlk rows, sub-group of 8 slots),
 // four tiles of 8 rows x 8 slots; the tile sums pass through a per-warp
 // [8 slots][kSBlk rows] buffer so that lane r holds row r of each slot.
+// Used when the staged variant below does not fit.
 template <bool BF16, int G>
-__device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
+__device__ void ph_head_wide_direct(const DModel& m, const DBatch& bt, const Part& pt, int u0, int u1, float* smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = bt.nblk;
   constexpr int NSUB = G / 8;
-  static_assert(kSBlk == 32, "head tiles cover a 32-row block");
-  int u0, u1;
-  cta_range(nb, cta, ncta, u0, u1);
-  if (u0 >= u1) return;
   const size_t rb = row_bytes(m.H, BF16);
   float* tbuf = smem + (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)warp * 8 * kSBlk;
   const unsigned char* wg = static_cast<const unsigned char*>(m.head);
-  for (int b0 = 0; b0 < bt.B; b0 += G) {
-    stage_norm<G>(m, bt, b0, m.norm, bt.x, smem);
+  for (int b0 = pt.first; b0 < bt.B; b0 += pt.step) {
+    stage_rows_inv<G>(m, bt, b0, bt.x, smem);
     for (int task = warp; task < (u1 - u0) * NSUB; task += kPW) {
       const int k = u0 + task / NSUB, sub = task % NSUB;
       const float* xs = smem + (size_t)sub * 8 * m.H;
@@ -1182,7 +1250,8 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
       for (int t = 0; t < kSBlk / 8; t++) {
         const int r0 = min(k * kSBlk + 8 * t, m.V - 1);
         float res[2];
-        warp_tile<BF16, false, true, 8, 8>(wg + (size_t)r0 * rb, rb, m.V - 1 - r0, m.H, xs, m.H, res);
+        warp_tile<BF16, false, true, 8, 8, true>(wg + (size_t)r0 * rb, rb, m.V - 1 - r0, m.H, xs, m.H, res, m.norm,
+                                                 g_inv + sub * 8);
         const int s = lane >> 2, r = 8 * t + 2 * (lane & 3);
         tbuf[s * kSBlk + r] = res[0];
         tbuf[s * kSBlk + r + 1] = res[1];
@@ -1201,6 +1270,90 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
       }
       __syncwarp();
     }
+    DEFER_CTA_SYNC();
+  }
+}
+
+// Shared-memory floats of the staged wide head: raw rows of the group, the
+// [G][kSBlk] block of sums, and two half blocks (kSBlk / 2 rows) of weights.
+__device__ __host__ __forceinline__ size_t head_staged_floats(int G, int H, bool bf16) {
+  const size_t rows = (((size_t)G * H + 3) & ~(size_t)3) + (size_t)G * kSBlk;
+  return rows + 2 * ((size_t)(kSBlk / 2) * H * (bf16 ? 2 : 4) / 4);
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prior1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// The staged wide head: the CTA walks its vocabulary blocks in half blocks
+// of 16 rows, each copied into shared memory with cp.async while the
+// previous half is multiplied (two buffers); the 8 warps take the 8 tiles
+// (2 row tiles x 4 sub-groups of a 32-slot group) of a half, so every
+// weight row crosses L2 once per group and CTA. After both halves the
+// block's [G][32] sums give each slot's logits and block statistics.
+template <bool BF16, int G>
+__device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = bt.nblk;
+  static_assert(kSBlk == 32, "head tiles cover a 32-row block");
+  const Part pt = part_of<G>(bt, cta, ncta);
+  int u0, u1;
+  cta_range(nb, pt.ci, pt.nci, u0, u1);
+  if (u0 >= u1) return;
+  constexpr int NSUB = G / 8;
+  constexpr int HALF = kSBlk / 2;
+  constexpr int TILES = (HALF / 8) * NSUB;  // warp tasks of a half block
+  if (m.V % kSBlk != 0 || head_staged_floats(G, m.H, BF16) * sizeof(float) > bt.smem_bytes) {
+    ph_head_wide_direct<BF16, G>(m, bt, pt, u0, u1, smem);
+    return;
+  }
+  const size_t rb = row_bytes(m.H, BF16);
+  float* sums = smem + (((size_t)G * m.H + 3) & ~(size_t)3);  // [G][kSBlk]
+  unsigned char* wbuf = reinterpret_cast<unsigned char*>(sums + (size_t)G * kSBlk);
+  const size_t half_bytes = (size_t)HALF * rb;
+  const unsigned char* wg = static_cast<const unsigned char*>(m.head);
+  const int nh = 2 * (u1 - u0);  // half blocks of this CTA
+  for (int b0 = pt.first; b0 < bt.B; b0 += pt.step) {
+    stage_rows_inv<G>(m, bt, b0, bt.x, smem);
+    auto issue = [&](int h) {
+      if (h < nh) {
+        const unsigned char* src = wg + ((size_t)u0 * kSBlk + (size_t)h * HALF) * rb;
+        unsigned char* dst = wbuf + (size_t)(h & 1) * half_bytes;
+        for (size_t c = threadIdx.x; c < half_bytes / 16; c += kPT) cp_async16_g2s(dst + 16 * c, src + 16 * c);
+      }
+      cp_async_commit();
+    };
+    issue(0);
+    for (int h = 0; h < nh; h++) {
+      issue(h + 1);
+      cp_async_wait_prior1();  // this thread's copies of half h have landed
+      DEFER_CTA_SYNC();        // ... and every thread's
+      const unsigned char* wh = wbuf + (size_t)(h & 1) * half_bytes;
+      for (int task = warp; task < TILES; task += kPW) {
+        const int t = task / NSUB, sub = task % NSUB;
+        float res[2];
+        warp_tile<BF16, true, true, 8, 8, true>(wh + (size_t)8 * t * rb, rb, 7, m.H, smem + (size_t)sub * 8 * m.H,
+                                                m.H, res, m.norm, g_inv + sub * 8);
+        const int s = lane >> 2, r = (h & 1) * HALF + 8 * t + 2 * (lane & 3);
+        float* row = sums + (size_t)(sub * 8 + s) * kSBlk;
+        row[r] = res[0];
+        row[r + 1] = res[1];
+      }
+      DEFER_CTA_SYNC();  // the half's buffer is free again; after an odd half the block's sums are complete
+      if (h & 1) {
+        const int k = u0 + h / 2;
+        const int i = k * kSBlk + lane;
+        for (int gg = warp; gg < G; gg += kPW) {
+          if (!g_act[gg]) continue;
+          const int b = b0 + gg;
+          const float v = sums[(size_t)gg * kSBlk + lane];
+          bt.logits[(size_t)b * m.V + i] = v;
+          const size_t o = (size_t)b * nb + k;
+          block_stats(v, i, true, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+        }
+        // the sums are rewritten from the next half on, after its barrier
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     DEFER_CTA_SYNC();
   }
 }
