@@ -16,6 +16,12 @@ replayed = 4096 single-token forward passes (each with its sampler step).
   e2e   : the same tokens per wall-clock second through the public API with
           host buffers (prompt / WAL / checkpoint bytes in, tokens out),
           including every host<->device copy and the WAL file writes.
+  batched_replay : BASELINE configs[2] (512 sessions, prompts 16-256 tokens,
+          seeds 0..511, T=0.8, 512 generated tokens each) on the same ranks:
+          each rank generates the checkpoints of its contiguous token-balanced
+          block with the batched token loop, then the timed batched verified
+          replay; aggregate tokens / max-over-ranks device time, with the fp32
+          SIMT roofline of the batched projections.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 """
@@ -220,6 +226,76 @@ def session_step(D, m, prompt, seed_bytes, wal_path):
     return tokens, h2d, d2h
 
 
+# -------------------------------------------------- batched replay (config 3)
+REPLAY_T = 0.8
+REPLAY_WORKLOAD = ("config3: the same 135M-shape model; {n} independent sessions (prompt lengths uniform 16-256, "
+                   "token IDs uniform, ChaCha8 seeds 0..{n1}, T=0.8, {gen} generated tokens each); their "
+                   "checkpoints generated by the batched token loop, then a batched verified replay (every "
+                   "recorded token re-sampled and compared), sessions partitioned over the GPUs in contiguous "
+                   "token-balanced blocks, no collective on the data path")
+FP32_FMA_PER_SM_CLK = 128  # fp32 FMA lanes per SM per clock (sm_100)
+
+
+def replay_sessions(n: int, vocab: int):
+    import numpy as np
+    rng = np.random.default_rng(3)
+    lens = [int(x) for x in rng.integers(16, 257, n)]
+    return [[int(t) for t in rng.integers(0, vocab, k)] for k in lens]
+
+
+def batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barrier, sms, clk_mhz):
+    """Config 3 on this rank's block: generate the checkpoints (batched token
+    loop), then the timed batched verified replay. Returns the JSON object."""
+    from defer_b200.partition import partition
+    n, gen = args.replay_sessions, args.replay_gen
+    prompts = replay_sessions(n, m.config.vocab_size)
+    blocks = partition([len(p) + gen for p in prompts], world)
+    mine = list(blocks[rank])
+    batch = max(1, min(len(mine), args.replay_batch))
+    pr = [prompts[i] for i in mine]
+    seeds = [D.seed_from_u64(i) for i in mine]
+    toks, gen_ms = D.generate_batch(m, pr, seeds, [REPLAY_T] * len(mine), [gen] * len(mine), batch=batch)
+    cks = [D.DeferCheckpoint(m.signature, seeds[k], REPLAY_T, pr[k] + toks[k], len(pr[k]), len(toks[k]))
+           for k in range(len(mine))]
+    tokens = sum(len(c.history_tokens) for c in cks)
+    m.timing(reset=True)
+    barrier()
+    t0 = time.perf_counter()
+    res, ms = D.replay_batch(m, cks, batch=batch) if cks else ([], 0.0)
+    wall = time.perf_counter() - t0
+    barrier()
+    launches = m.timing(reset=True)["launches"]
+    failures = sum(1 for r in res if r.status != 0)
+    dev_s = max_over_ranks(ms / 1e3)
+    wall_s = max_over_ranks(wall)
+    gen_s = max_over_ranks(gen_ms / 1e3)
+    all_tokens = sum_over_ranks(tokens)
+    all_fail = sum_over_ranks(failures)
+    value = all_tokens / dev_s
+    c = m.config
+    H, FF, QD, KVD = c.hidden_size, c.intermediate_size, c.q_dim, c.kv_dim
+    mac = c.num_layers * (H * (QD + 2 * KVD) + QD * H + 3 * FF * H) + c.vocab_size * H  # projections + head
+    flops_tok = 2.0 * mac  # attention (O(pos)) not counted
+    peak_tf = world * sms * FP32_FMA_PER_SM_CLK * 2 * clk_mhz * 1e6 / 1e12
+    achieved_tf = value * flops_tok / 1e12
+    # host->device: the checkpoint bytes; device->host: status, step, token per session
+    h2d = sum(len(c.to_bytes()) for c in cks)
+    d2h = 12 * len(cks)
+    return {"metric": "batched replay tok/s (verified checkout of many WALs)", "value": value, "unit": "tok/s",
+            "n_gpus": world, "sessions": n, "tokens": int(all_tokens), "divergences": int(all_fail),
+            "batch_per_gpu": batch, "device_s": dev_s, "generate_tok_s": all_tokens / gen_s,
+            "gpu_launches": launches,
+            "config": {"workload": REPLAY_WORKLOAD.format(n=n, n1=n - 1, gen=gen),
+                       "parallelism": f"{world} GPU(s), contiguous token-balanced session blocks"},
+            "roofline": {"bound": "fp32 simt (batched GEMMs keep the reference's fp32 arithmetic)",
+                         "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved_tf / peak_tf,
+                         "peak_kind": f"nominal: {sms} SMs x {FP32_FMA_PER_SM_CLK} fp32 FMA/clk x 2 x "
+                                      f"{clk_mhz:.0f} MHz per GPU",
+                         "flops_per_token": flops_tok, "sm_count": sms},
+            "e2e": {"value": all_tokens / wall_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h}}
+
+
 def run_b200(args):
     import numpy as np  # noqa: F401
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -296,6 +372,14 @@ def run_b200(args):
         barrier()
     tm = m.timing(reset=True)
     clocks = clk.summary()
+    replay = None
+    if args.replay_sessions > 0:
+        import torch
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        clk_mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
+        os.environ.pop("DEFER_B200_LOOP", None)  # wide batches take the grid-barrier token loop
+        replay = batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barrier, sms, clk_mhz)
+        m.timing(reset=True)
     try:
         os.unlink(wal)
     except OSError:
@@ -326,7 +410,7 @@ def run_b200(args):
                 "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d // max(args.steps, 1),
                         "d2h_bytes_per_step": d2h // max(args.steps, 1)},
-                "gpu_launches": tm["launches"], "clocks": clocks,
+                "gpu_launches": tm["launches"], "clocks": clocks, "batched_replay": replay,
                 "device": {"tokens": tokens, "device_ms": tm["device_ms"], "runs": tm["runs"]}}
         print(json.dumps(line), flush=True)
     if dist:
@@ -343,6 +427,10 @@ def main(argv=None):
     ap.add_argument("--cpu-gen", type=int, default=150, help="sampled tokens of the CPU baseline sample")
     ap.add_argument("--ref-gen", type=int, default=48, help="sampled tokens per reference-arm step")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--replay-sessions", type=int, default=512,
+                    help="sessions of the batched replay measurement (config 3); 0 skips it")
+    ap.add_argument("--replay-gen", type=int, default=512, help="generated tokens per replay session")
+    ap.add_argument("--replay-batch", type=int, default=512, help="slots per GPU of the batched replay")
     ap.add_argument("--profile-case", action="store_true",
                     help="no measurement: the small case profiles are captured on (135M model, "
                          "16-token prompt, then one launch of 32 sampled tokens)")

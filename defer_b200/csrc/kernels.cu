@@ -67,7 +67,10 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DModel m, DBatch bt, int l) {
   ph_qkv<BF16, G>(m, bt, l, blockIdx.x, gridDim.x, dyn_smem);
 }
 __global__ void __launch_bounds__(kThreads) k_attn(DModel m, DBatch bt, int l) {
-  ph_attn(m, bt, l, blockIdx.x, gridDim.x, dyn_smem);
+  ph_attn_chunks(m, bt, l, blockIdx.x, gridDim.x, dyn_smem);
+}
+__global__ void __launch_bounds__(kThreads) k_attn_combine(DModel m, DBatch bt) {
+  ph_attn_combine(m, bt, blockIdx.x, gridDim.x);
 }
 template <bool BF16, int G>
 __global__ void __launch_bounds__(kThreads) k_oproj(DModel m, DBatch bt, int l, unsigned smem_floats) {
@@ -150,7 +153,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
       const DLayer& Ly = m.layers[l];
       ph_qkv<BF16, G>(m, bt, l, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
-      ph_attn(m, bt, l, cta, ncta, dyn_smem);
+      ph_attn_chunks(m, bt, l, cta, ncta, dyn_smem);
+      grid_barrier(bt.bar, target, bt.status);
+      ph_attn_combine(m, bt, cta, ncta);
       grid_barrier(bt.bar, target, bt.status);
       ph_residual_gemv<BF16, G>(m, bt, Ly.wo, m.QD, bt.att, cta, ncta, dyn_smem, smem_floats);
       grid_barrier(bt.bar, target, bt.status);
@@ -199,11 +204,8 @@ static size_t step_smem_floats(const DModel& m, int B, int max_chunks) {
   size_t f = (size_t)G * std::max(m.H, m.QD);
   const size_t ffs = (size_t)G * m.FF;
   if (ffs * 4 <= 200 * 1024) f = std::max(f, ffs);  // the down projection's input, when it fits
-  // attention: q, scores, the chunk's K (padded rows) and V; the combine
-  // reuses the K/V area for one head's partials of every chunk
-  const size_t kv = std::max((size_t)kAttnChunk * (m.HD + 4) + (size_t)kAttnChunk * m.HD,
-                             (size_t)max_chunks * (m.HD + 2));
-  f = std::max(f, (size_t)(Gh * m.HD + Gh * kAttnChunk) + kv);
+  (void)max_chunks;
+  f = std::max(f, attn_smem_floats(B, Gh, m.HD));  // attention chunks: slot state, scores, two unit buffers
   // the wide head: normalized rows plus one [8][kSBlk] tile buffer per warp
   if (G >= 8) {
     f = std::max(f, (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)kPW * 8 * kSBlk);
@@ -276,6 +278,7 @@ static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, in
     for (int l = 0; l < m.L; l++) {
       k_qkv<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l);
       k_attn<<<std::min(attn_units, sms * 8), kThreads, smem, st>>>(m, bt, l);
+      k_attn_combine<<<grid, kThreads, 0, st>>>(m, bt);
       k_oproj<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l, (unsigned)sf);
       k_gateup<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l);
       k_down<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l, (unsigned)sf);

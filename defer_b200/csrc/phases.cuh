@@ -1451,23 +1451,35 @@ __device__ __forceinline__ bool needs_sums(const DBatch& bt, int b) {
   return samples_next(bt, b);
 }
 
+// The sampler sums are split over (slot, block) pairs: CTA `cta` takes a
+// contiguous range of the flattened index b * nblk + k, so each slot's
+// whole-vector reductions (the max of s, the total of e) are computed only
+// by the one or two CTAs that hold its blocks.
+__device__ __forceinline__ void sum_range(const DBatch& bt, int cta, int ncta, int& f0, int& f1) {
+  const long long n = (long long)bt.B * bt.nblk;
+  f0 = (int)(n * cta / ncta);
+  f1 = (int)(n * (cta + 1) / ncta);
+}
+
 // Block sums of e for slots sampling next (needs the max over all blocks).
 template <bool FIRST>
 __device__ void ph_sample1(const DModel& m, const DBatch& bt, int cta, int ncta) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = bt.nblk;
-  int u0, u1;
-  cta_range(nb, cta, ncta, u0, u1);
-  for (int b = 0; b < bt.B; b++) {
+  int f0, f1;
+  sum_range(bt, cta, ncta, f0, f1);
+  if (f0 >= f1) return;
+  for (int b = f0 / nb; b <= (f1 - 1) / nb; b++) {
     if (!needs_sums<FIRST>(bt, b)) continue;
     const float T = bt.sess[b].temperature;
     const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
     const float* lg = bt.logits + (size_t)b * m.V;
-    for (int k = u0 + warp; k < u1; k += kPW) {
+    const int k1 = min(f1 - b * nb, nb);
+    for (int k = max(f0 - b * nb, 0) + warp; k < k1; k += kPW) {
       const int i = k * kSBlk + lane;
       const float e = i < m.V ? e_of(ld_f(lg + i), T, M) : 0.0f;
-      const float s = warp_seq_sum(e);
-      if (lane == 0) bt.ss.esum[(size_t)b * nb + k] = s;
+      const float sm = warp_seq_sum(e);
+      if (lane == 0) bt.ss.esum[(size_t)b * nb + k] = sm;
     }
   }
 }
@@ -1478,9 +1490,10 @@ __device__ void ph_sample2(const DModel& m, const DBatch& bt, int cta, int ncta,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = bt.nblk;
   const int ng2 = (nb + 31) / 32;
-  int u0, u1;
-  cta_range(nb, cta, ncta, u0, u1);
-  for (int b = 0; b < bt.B; b++) {
+  int f0, f1;
+  sum_range(bt, cta, ncta, f0, f1);
+  if (f0 >= f1) return;
+  for (int b = f0 / nb; b <= (f1 - 1) / nb; b++) {
     if (!needs_sums<FIRST>(bt, b)) continue;
     const float T = bt.sess[b].temperature;
     const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
@@ -1488,11 +1501,12 @@ __device__ void ph_sample2(const DModel& m, const DBatch& bt, int cta, int ncta,
     if (!(Z > 0.0f) || !isfinite(Z)) continue;  // SELECT falls back to argmax
     const float inv = __fdiv_rn(1.0f, Z);
     const float* lg = bt.logits + (size_t)b * m.V;
-    for (int k = u0 + warp; k < u1; k += kPW) {
+    const int k1 = min(f1 - b * nb, nb);
+    for (int k = max(f0 - b * nb, 0) + warp; k < k1; k += kPW) {
       const int i = k * kSBlk + lane;
       const float p = i < m.V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
-      const float s = warp_seq_sum(p);
-      if (lane == 0) bt.ss.psum[(size_t)b * nb + k] = s;
+      const float sm = warp_seq_sum(p);
+      if (lane == 0) bt.ss.psum[(size_t)b * nb + k] = sm;
     }
   }
 }
@@ -1505,68 +1519,97 @@ __device__ __forceinline__ bool any_sampling(const DBatch& bt) {
 }
 
 // ------------------------------------------------------------- attention
-// Partial attention of one key chunk for the query heads of one KV head;
-// the CTA finishing the last chunk of a (slot, KV head) combines all its
-// chunks in chunk order. CTA unit = (slot, kv head, chunk). The chunk's K/V
-// rows and, for the combine, each head's partials are staged in shared
-// memory with every load of a batch issued before its stores.
-constexpr int kAttnBatch = 4;  // float4 loads of K (and of V) per thread in flight
+// Two stages. CHUNKS: unit = (slot, KV head, chunk of kAttnChunk key
+// positions) on CTA u mod ncta; a CTA walks its units with the next unit's
+// queries, K rows and V rows copied into shared memory (cp.async, two
+// buffers) while the current one is computed, and writes the chunk's
+// partials (max m, sum l, unnormalised output acc) for each query head of
+// the KV head; a head with a single chunk writes its output acc / l
+// directly (what the combine gives for one chunk, bit for bit). COMBINE
+// (after a grid-wide dependency): a warp per (slot, query head) with two or
+// more chunks merges the partials in chunk order.
 
-static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
+// Floats of one unit buffer: queries [Gh][HD], K rows [kAttnChunk][HD + 4]
+// (padded: threads of a warp read different rows at the same column), V
+// rows [kAttnChunk][HD].
+__host__ __device__ __forceinline__ size_t attn_buf_floats(int Gh, int HD) {
+  return (size_t)Gh * HD + (size_t)kAttnChunk * (HD + 4) + (size_t)kAttnChunk * HD;
+}
+
+// Shared-memory floats of the chunk stage: slot state (2 B ints), scores
+// [Gh][kAttnChunk], chunk sums [Gh], two unit buffers.
+__host__ __device__ __forceinline__ size_t attn_smem_floats(int B, int Gh, int HD) {
+  return (((size_t)2 * B + 3) & ~(size_t)3) + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3) +
+         2 * attn_buf_floats(Gh, HD);
+}
+
+static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   {  // the gate/up projection comes after the O projection
     const DLayer& Ly = m.layers[l];
     prefetch_rows(Ly.wgu, 2 * m.FF, m.H, m.bf16 != 0, m.FF, 2, cta, ncta);
   }
-  const int G = m.NH / m.NKV, HD = m.HD;
+  const int Gh = m.NH / m.NKV, HD = m.HD;
   const int maxc = bt.max_chunks;
-  const int units = bt.B * m.NKV * maxc;
+  const int per_slot = m.NKV * maxc;
+  const int units = bt.B * per_slot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int c4n = HD / 4;
-  float* qs = smem;                         // [G][HD]
-  float* sc = qs + G * HD;                  // [G][kAttnChunk]
-  float* ks = sc + G * kAttnChunk;          // [kAttnChunk][HD + 4]
-  float* vs = ks + kAttnChunk * (HD + 4);   // [kAttnChunk][HD]
-  float* pc = ks;                           // combine: [nch][HD + 2] of one head (reuses ks/vs)
-  __shared__ int s_last;
-  for (int u = cta; u < units; u += ncta) {
-    const int b = u / (m.NKV * maxc);
-    const int rem = u % (m.NKV * maxc);
-    const int kvh = rem / maxc, c = rem % maxc;
-    if (!ld_i(&bt.st[b].active)) continue;
-    const int pos = ld_i(&bt.st[b].pos);
-    const int nch = pos / kAttnChunk + 1;
-    if (c >= nch) continue;
-    const DSession& S = bt.sess[b];
-    const int t0 = c * kAttnChunk;
-    const int tn = min(kAttnChunk, pos + 1 - t0);
-    const float* qsrc = bt.q + (size_t)b * m.QD + (size_t)kvh * G * HD;
-    const size_t head_base = ((size_t)l * m.NKV + kvh) * S.cap;
-    for (int i = tid; i < G * HD; i += kPT) qs[i] = ld_f(qsrc + i);
-    for (int base = 0; base < tn * c4n; base += kAttnBatch * kPT) {
-      float4 kv[kAttnBatch], vv[kAttnBatch];
-#pragma unroll
-      for (int k = 0; k < kAttnBatch; k++) {
-        const int idx = base + tid + k * kPT;
-        if (idx < tn * c4n) {
-          const int tt = idx / c4n, c4 = idx - tt * c4n;
-          kv[k] = ld_act(S.kc + (head_base + t0 + tt) * HD + 4 * c4);
-          vv[k] = ld_act(S.vc + (head_base + t0 + tt) * HD + 4 * c4);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < kAttnBatch; k++) {
-        const int idx = base + tid + k * kPT;
-        if (idx < tn * c4n) {
-          const int tt = idx / c4n, c4 = idx - tt * c4n;
-          *reinterpret_cast<float4*>(ks + (size_t)tt * (HD + 4) + 4 * c4) = kv[k];
-          *reinterpret_cast<float4*>(vs + (size_t)tt * HD + 4 * c4) = vv[k];
-        }
+  int* s_act = reinterpret_cast<int*>(smem);
+  int* s_pos = s_act + bt.B;
+  float* sc = smem + (((size_t)2 * bt.B + 3) & ~(size_t)3);  // [Gh][kAttnChunk]
+  float* lsum = sc + Gh * kAttnChunk;                          // [Gh]
+  float* buf0 = sc + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3);
+  const size_t bfl = attn_buf_floats(Gh, HD);
+  for (int b = tid; b < bt.B; b += kPT) {
+    s_act[b] = ld_i(&bt.st[b].active);
+    s_pos[b] = ld_i(&bt.st[b].pos);
+  }
+  DEFER_CTA_SYNC();
+  auto live = [&](int u) {
+    const int b = u / per_slot, c = u % maxc;
+    return s_act[b] && c <= s_pos[b] / kAttnChunk;
+  };
+  auto next = [&](int u) {
+    for (u += ncta; u < units; u += ncta)
+      if (live(u)) return u;
+    return -1;
+  };
+  auto issue = [&](int u, float* buf) {
+    if (u >= 0) {
+      const int b = u / per_slot, rem = u % per_slot, kvh = rem / maxc, c = rem % maxc;
+      const DSession& S = bt.sess[b];
+      const int t0 = c * kAttnChunk, tn = min(kAttnChunk, s_pos[b] + 1 - t0);
+      const size_t base = ((size_t)l * m.NKV + kvh) * S.cap + t0;
+      const float* qsrc = bt.q + (size_t)b * m.QD + (size_t)kvh * Gh * HD;
+      float* qs = buf;
+      float* ks = qs + Gh * HD;
+      float* vs = ks + kAttnChunk * (HD + 4);
+      const int c4n = HD / 4;
+      for (int f = tid; f < Gh * c4n; f += kPT) cp_async16_g2s(qs + 4 * f, qsrc + 4 * f);
+      for (int f = tid; f < tn * c4n; f += kPT) {
+        const int tt = f / c4n, c4 = f - tt * c4n;
+        cp_async16_g2s(ks + (size_t)tt * (HD + 4) + 4 * c4, S.kc + (base + tt) * HD + 4 * c4);
+        cp_async16_g2s(vs + (size_t)tt * HD + 4 * c4, S.vc + (base + tt) * HD + 4 * c4);
       }
     }
+    cp_async_commit();
+  };
+  int u = cta < units ? (live(cta) ? cta : next(cta)) : -1;
+  issue(u, buf0);
+  for (int it = 0; u >= 0; it++) {
+    const int un = next(u);
+    issue(un, buf0 + (size_t)((it + 1) & 1) * bfl);
+    cp_async_wait_prior1();
     DEFER_CTA_SYNC();
-    for (int idx = tid; idx < G * kAttnChunk; idx += kPT) {
+    const float* qs = buf0 + (size_t)(it & 1) * bfl;
+    const float* ks = qs + Gh * HD;
+    const float* vs = ks + kAttnChunk * (HD + 4);
+    const int b = u / per_slot, rem = u % per_slot, kvh = rem / maxc, c = rem % maxc;
+    const DSession& S = bt.sess[b];
+    const int pos = s_pos[b], nch = pos / kAttnChunk + 1;
+    const int t0 = c * kAttnChunk, tn = min(kAttnChunk, pos + 1 - t0);
+    for (int idx = tid; idx < Gh * kAttnChunk; idx += kPT) {
       const int h = idx / kAttnChunk, tt = idx - h * kAttnChunk;
-      float s = -INFINITY;
+      float sv = -INFINITY;
       const int t = t0 + tt;
       const bool masked = S.mask && t < pos && ((S.mask[t >> 5] >> (t & 31)) & 1u);
       if (tt < tn && !masked) {
@@ -1581,13 +1624,13 @@ static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta
           a2 = fmaf(qr[d + 2], k4.z, a2);
           a3 = fmaf(qr[d + 3], k4.w, a3);
         }
-        s = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), m.scale);
+        sv = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), m.scale);
       }
-      sc[idx] = s;
+      sc[idx] = sv;
     }
     DEFER_CTA_SYNC();
     float* part_b = bt.part + (size_t)b * m.NH * maxc * (HD + 2);
-    for (int h = warp; h < G; h += kPW) {
+    for (int h = warp; h < Gh; h += kPW) {
       float* row = sc + h * kAttnChunk;
       const float v0 = row[lane], v1 = row[lane + 32];
       const float mx = warp_max(fmaxf(v0, v1));
@@ -1597,69 +1640,59 @@ static __device__ void ph_attn(const DModel& m, const DBatch& bt, int l, int cta
       row[lane + 32] = e1;
       const float ls = warp_sum_butterfly(__fadd_rn(e0, e1));
       if (lane == 0) {
-        float* p = part_b + ((size_t)(kvh * G + h) * maxc + c) * (HD + 2);
-        p[0] = mx;
-        p[1] = ls;
+        lsum[h] = ls;
+        if (nch > 1) {
+          float* pp = part_b + ((size_t)(kvh * Gh + h) * maxc + c) * (HD + 2);
+          pp[0] = mx;
+          pp[1] = ls;
+        }
       }
     }
     DEFER_CTA_SYNC();
-    for (int idx = tid; idx < G * HD; idx += kPT) {
+    for (int idx = tid; idx < Gh * HD; idx += kPT) {
       const int h = idx / HD, d = idx - h * HD;
       const float* e = sc + h * kAttnChunk;
       float acc = 0.0f;
 #pragma unroll 8
       for (int tt = 0; tt < tn; tt++) acc = fmaf(e[tt], vs[(size_t)tt * HD + d], acc);
-      part_b[((size_t)(kvh * G + h) * maxc + c) * (HD + 2) + 2 + d] = acc;
+      if (nch > 1) part_b[((size_t)(kvh * Gh + h) * maxc + c) * (HD + 2) + 2 + d] = acc;
+      else bt.att[(size_t)b * m.QD + (size_t)(kvh * Gh + h) * HD + d] = __fdiv_rn(acc, lsum[h]);
     }
-    // The last chunk of this (slot, KV head) to finish combines; every
-    // writer makes its partials visible GPU-wide before the ticket.
-    __threadfence();
-    DEFER_CTA_SYNC();
-    if (tid == 0) {
-      __threadfence();
-      int* tk = bt.tickets + (size_t)b * m.NKV + kvh;
-      const int done = atomicAdd(tk, 1) + 1;
-      s_last = (done == nch);
-      if (s_last) {
-        __threadfence();
-        *tk = 0;  // ready for the next layer (a barrier separates them)
+    DEFER_CTA_SYNC();  // the buffer, the scores and the sums are reused
+    u = un;
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Merge of the chunk partials of every (slot, query head) with two or more
+// chunks, in chunk order: M = max m_c; w_c = exp(m_c - M) (0 for m_c = -inf);
+// L = sum w_c l_c, O = sum w_c acc_c (fmaf, chunk order); out = O / L.
+static __device__ void ph_attn_combine(const DModel& m, const DBatch& bt, int cta, int ncta) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int HD = m.HD, row = HD + 2, maxc = bt.max_chunks;
+  const int tasks = bt.B * m.NH;
+  for (int t = cta * kPW + warp; t < tasks; t += ncta * kPW) {
+    const int b = t / m.NH, h = t - b * m.NH;
+    if (!ld_i(&bt.st[b].active)) continue;
+    const int nch = ld_i(&bt.st[b].pos) / kAttnChunk + 1;
+    if (nch == 1) continue;  // written by the chunk stage
+    const float* p = bt.part + ((size_t)b * m.NH + h) * maxc * row;
+    float M = -INFINITY;
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, ld_f(p + (size_t)c * row));
+    M = warp_max(M);
+    for (int d0 = 0; d0 < HD; d0 += 32) {
+      const int d = d0 + lane;
+      float L = 0.0f, O = 0.0f;
+#pragma unroll 4
+      for (int c = 0; c < nch; c++) {
+        const float mc = ld_f(p + (size_t)c * row), lc = ld_f(p + (size_t)c * row + 1);
+        const float ac = d < HD ? ld_f(p + (size_t)c * row + 2 + d) : 0.0f;
+        const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
+        L = fmaf(w, lc, L);
+        O = fmaf(w, ac, O);
       }
+      if (d < HD) bt.att[(size_t)b * m.QD + (size_t)h * HD + d] = __fdiv_rn(O, L);
     }
-    DEFER_CTA_SYNC();
-    if (s_last) {
-      const int row = HD + 2;
-      for (int h = 0; h < G; h++) {
-        const float* p = part_b + (size_t)(kvh * G + h) * maxc * row;
-        for (int base = 0; base < nch * row; base += kAttnBatch * kPT) {
-          float v[kAttnBatch];
-#pragma unroll
-          for (int k = 0; k < kAttnBatch; k++) {
-            const int idx = base + tid + k * kPT;
-            if (idx < nch * row) v[k] = ld_f(p + idx);
-          }
-#pragma unroll
-          for (int k = 0; k < kAttnBatch; k++) {
-            const int idx = base + tid + k * kPT;
-            if (idx < nch * row) pc[idx] = v[k];
-          }
-        }
-        DEFER_CTA_SYNC();
-        for (int d = tid; d < HD; d += kPT) {
-          float M = -INFINITY;
-          for (int cc = 0; cc < nch; cc++) M = fmaxf(M, pc[cc * row]);
-          float L = 0.0f, O = 0.0f;
-          for (int cc = 0; cc < nch; cc++) {
-            const float mc = pc[cc * row], lc = pc[cc * row + 1], ac = pc[cc * row + 2 + d];
-            const float w = (mc == -INFINITY) ? 0.0f : expf(__fsub_rn(mc, M));
-            L = fmaf(w, lc, L);
-            O = fmaf(w, ac, O);
-          }
-          bt.att[(size_t)b * m.QD + (size_t)(kvh * G + h) * HD + d] = __fdiv_rn(O, L);
-        }
-        DEFER_CTA_SYNC();
-      }
-    }
-    DEFER_CTA_SYNC();
   }
 }
 
