@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kThreads) k_head(DModel m, DBatch bt) {
 }
 template <bool FIRST>
 __global__ void __launch_bounds__(kThreads) k_sample1(DModel m, DBatch bt) {
-  ph_sample1<FIRST>(m, bt, blockIdx.x, gridDim.x);
+  ph_sample1<FIRST>(m, bt, blockIdx.x, gridDim.x, dyn_smem);
 }
 template <bool FIRST>
 __global__ void __launch_bounds__(kThreads) k_sample2(DModel m, DBatch bt) {
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
     ph_restat(m, bt, cta, ncta);
     grid_barrier(bt.bar, target, bt.status);
     if (any_first(bt, true)) {
-      ph_sample1<true>(m, bt, cta, ncta);
+      ph_sample1<true>(m, bt, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
       ph_sample2<true>(m, bt, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
     const bool sampling = any_sampling(bt);
     grid_barrier(bt.bar, target, bt.status);
     if (sampling) {
-      ph_sample1<false>(m, bt, cta, ncta);
+      ph_sample1<false>(m, bt, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
       ph_sample2<false>(m, bt, cta, ncta, dyn_smem);
       grid_barrier(bt.bar, target, bt.status);
@@ -205,7 +205,11 @@ static size_t step_smem_floats(const DModel& m, int B, int max_chunks) {
   const size_t ffs = (size_t)G * m.FF;
   if (ffs * 4 <= 200 * 1024) f = std::max(f, ffs);  // the down projection's input, when it fits
   (void)max_chunks;
-  f = std::max(f, attn_smem_floats(B, Gh, m.HD));  // attention chunks: slot state, scores, two unit buffers
+  // attention chunks: slot state, scores and at least two unit buffers (more
+  // when the other stages leave room, up to kAttnMaxBuf)
+  f = std::max(f, attn_smem_floats(B, Gh, m.HD, 2));
+  const size_t a4 = attn_smem_floats(B, Gh, m.HD, kAttnMaxBuf);
+  if (a4 * 4 <= 200 * 1024) f = std::max(f, a4);
   // the wide head: normalized rows plus one [8][kSBlk] tile buffer per warp
   if (G >= 8) {
     f = std::max(f, (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)kPW * 8 * kSBlk);
@@ -214,7 +218,8 @@ static size_t step_smem_floats(const DModel& m, int B, int max_chunks) {
   }
   const int nblk = (m.V + kSBlk - 1) / kSBlk;
   const int ng2 = (nblk + 31) / 32;
-  f = std::max(f, (size_t)(ng2 + (ng2 + 31) / 32 + 8));
+  // sampler sums: the hierarchy's group sums, then a [32][33] buffer per warp
+  f = std::max(f, (((size_t)ng2 + (ng2 + 31) / 32 + 3) & ~(size_t)3) + (size_t)kPW * 32 * 33);
   return (f + 3) & ~(size_t)3;
 }
 
@@ -262,6 +267,8 @@ static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, in
   allow_smem(k_gateup<BF16, G>, smem);
   allow_smem(k_down<BF16, G>, smem);
   allow_smem(k_head<BF16, G>, smem);
+  allow_smem(k_sample1<false>, smem);
+  allow_smem(k_sample1<true>, smem);
   allow_smem(k_sample2<false>, smem);
   allow_smem(k_sample2<true>, smem);
   const int B = bt.B;
@@ -271,7 +278,7 @@ static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, in
   // statistics of the resident logits for slots whose first step samples
   // (each kernel skips the slots that do not)
   k_restat<<<grid, kThreads, 0, st>>>(m, bt);
-  k_sample1<true><<<grid, kThreads, 0, st>>>(m, bt);
+  k_sample1<true><<<grid, kThreads, smem, st>>>(m, bt);
   k_sample2<true><<<grid, kThreads, smem, st>>>(m, bt);
   for (int s = 0; s < nsteps; s++) {
     k_select<BF16><<<B, kThreads, smem, st>>>(m, bt, first_step + s);
@@ -285,7 +292,7 @@ static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, in
     }
     k_head<BF16, G><<<grid, kThreads, smem, st>>>(m, bt);
     // The sample phases skip every slot that does not sample next.
-    k_sample1<false><<<grid, kThreads, 0, st>>>(m, bt);
+    k_sample1<false><<<grid, kThreads, smem, st>>>(m, bt);
     k_sample2<false><<<grid, kThreads, smem, st>>>(m, bt);
   }
   k_finalize<<<B, kThreads, 0, st>>>(bt);

@@ -369,6 +369,9 @@ __device__ __forceinline__ void cp_async16_g2s(void* dst, const void* src) {
                : "memory");
 }
 
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prior1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 // Slot b0 + g's activations src[(b0 + g) * K + i] into dst[g * K + i] with
 // cp.async (every copy in flight at once, no registers); slots past the
 // batch, or inactive ones when `need_active`, become zeros. Also records the
@@ -431,21 +434,37 @@ __device__ void stage_rows_inv(const DModel& m, const DBatch& bt, int b0, const 
   DEFER_CTA_SYNC();
 }
 
+// Staged raw rows of a group -> normalised rows (x * inv) * w in place,
+// four consecutive elements per thread (H % 4 == 0); missing or inactive
+// slots stay zero rows.
+template <int G>
+__device__ void scale_rows(const DModel& m, const float* w_of_layer, float* dst) {
+  const int n4 = G * m.H / 4;
+  for (int f = threadIdx.x; f < n4; f += kPT) {
+    const int g = (4 * f) / m.H, i = 4 * f - g * m.H;
+    float4 x = reinterpret_cast<float4*>(dst)[f];
+    if (g_live[g]) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(w_of_layer + i));
+      const float inv = g_inv[g];
+      x.x = __fmul_rn(__fmul_rn(x.x, inv), w.x);
+      x.y = __fmul_rn(__fmul_rn(x.y, inv), w.y);
+      x.z = __fmul_rn(__fmul_rn(x.z, inv), w.z);
+      x.w = __fmul_rn(__fmul_rn(x.w, inv), w.w);
+    } else {
+      x = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    reinterpret_cast<float4*>(dst)[f] = x;
+  }
+  DEFER_CTA_SYNC();
+}
+
 // dst[g][i] = rmsnorm(x of slot b0+g)[i] = (x * inv) * w for the G slots of
 // a group (inactive or missing slots get zeros), scaled in place.
 template <int G>
 __device__ void stage_norm(const DModel& m, const DBatch& bt, int b0, const float* w_of_layer, const float* x,
                            float* dst) {
   stage_rows_inv<G>(m, bt, b0, x, dst);
-  for (int i = threadIdx.x; i < m.H; i += kPT) {
-    const float w = w_of_layer[i];
-#pragma unroll 4
-    for (int g = 0; g < G; g++) {
-      float* p = dst + (size_t)g * m.H + i;
-      *p = g_live[g] ? __fmul_rn(__fmul_rn(*p, g_inv[g]), w) : 0.0f;
-    }
-  }
-  DEFER_CTA_SYNC();
+  scale_rows<G>(m, w_of_layer, dst);
 }
 
 // Copies slot activations [b0, b0+G) (stride K) into shared memory.
@@ -1021,23 +1040,69 @@ __device__ void ph_pairs_wide(const DModel& m, const DBatch& bt, int l, int cta,
   const unsigned char* wsm =
       stage_weights(W, 2 * tb.s0, 2 * (tb.s1 - tb.s0), rb, smem, (size_t)G * m.H, bt.smem_bytes);
   const unsigned char* wg = static_cast<const unsigned char*>(W);
+  // When the CTA's rows do not fit shared memory whole, they stream through
+  // it: SB row blocks per step (8 warp tasks), two step buffers, the next
+  // step's copy in flight while the current one is multiplied.
+  const size_t xb = (((size_t)G * m.H + 3) & ~(size_t)3) * sizeof(float);
+  const size_t blk_bytes = (size_t)2 * NU * rb;
+  const int SB_max = kPW / NSUB > 0 ? kPW / NSUB : 1;
+  const size_t room = bt.smem_bytes > xb ? bt.smem_bytes - xb : 0;
+  const int SB = wsm ? 0 : (int)min((size_t)SB_max, room / (2 * blk_bytes));
+  unsigned char* sbuf = reinterpret_cast<unsigned char*>(smem) + xb;
+  auto epilogue = [&](int b0, int ub, int ua, int sub, const float (&res)[2]) {
+    const int u = ua + (lane & 3), gg = sub * 8 + (lane >> 2), b = b0 + gg;
+    if (u < ub || u >= u1 || !g_act[gg]) return;
+    if (GU) bt.g[(size_t)b * m.FF + u] = gate_act_mul(m, res[0], res[1]);
+    else qkv_store(m, Ly, bt, l, u, b, g_pos[gg], res[0], res[1]);
+  };
   for (int b0 = pt.first; b0 < bt.B; b0 += pt.step) {
     stage_rows_inv<G>(m, bt, b0, bt.x, smem);
+    scale_rows<G>(m, nw, smem);  // once per group: every row block of the CTA reads these rows
+    if (SB > 0) {
+      const int nsteps = (tb.nblk + SB - 1) / SB;
+      auto issue = [&](int stp) {
+        if (stp < nsteps) {
+          unsigned char* dst = sbuf + (size_t)(stp & 1) * SB * blk_bytes;
+          for (int k = 0; k < SB && stp * SB + k < tb.nblk; k++) {
+            int ub, ua;
+            tile_block(u0, stp * SB + k, units, NU, ub, ua);
+            const unsigned char* src = wg + (size_t)2 * ua * rb;
+            for (size_t c = threadIdx.x; c < blk_bytes / 16; c += kPT)
+              cp_async16_g2s(dst + (size_t)k * blk_bytes + 16 * c, src + 16 * c);
+          }
+        }
+        cp_async_commit();
+      };
+      issue(0);
+      for (int stp = 0; stp < nsteps; stp++) {
+        issue(stp + 1);
+        cp_async_wait_prior1();
+        DEFER_CTA_SYNC();
+        const unsigned char* buf = sbuf + (size_t)(stp & 1) * SB * blk_bytes;
+        for (int task = warp; task < SB * NSUB; task += kPW) {
+          const int k = task / NSUB, sub = task % NSUB, blk = stp * SB + k;
+          if (blk >= tb.nblk) continue;
+          int ub, ua;
+          tile_block(u0, blk, units, NU, ub, ua);
+          float res[2];
+          warp_tile<BF16, true, true, 8, 8>(buf + (size_t)k * blk_bytes, rb, 7, m.H, smem + (size_t)sub * 8 * m.H,
+                                            m.H, res);
+          epilogue(b0, ub, ua, sub, res);
+        }
+        DEFER_CTA_SYNC();  // the step's buffer is refilled two steps later
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      continue;
+    }
     for (int task = warp; task < tb.nblk * NSUB; task += kPW) {
       const int blk = task / NSUB, sub = task % NSUB;
       int ub, ua;
       tile_block(u0, blk, units, NU, ub, ua);
       float res[2];
       const float* xs = smem + (size_t)sub * 8 * m.H;
-      const float* inv = g_inv + sub * 8;
-      if (wsm)
-        warp_tile<BF16, true, true, 8, 8, true>(wsm + (size_t)2 * (ua - tb.s0) * rb, rb, 7, m.H, xs, m.H, res, nw, inv);
-      else
-        warp_tile<BF16, false, true, 8, 8, true>(wg + (size_t)2 * ua * rb, rb, 7, m.H, xs, m.H, res, nw, inv);
-      const int u = ua + (lane & 3), gg = sub * 8 + (lane >> 2), b = b0 + gg;
-      if (u < ub || u >= u1 || !g_act[gg]) continue;
-      if (GU) bt.g[(size_t)b * m.FF + u] = gate_act_mul(m, res[0], res[1]);
-      else qkv_store(m, Ly, bt, l, u, b, g_pos[gg], res[0], res[1]);
+      if (wsm) warp_tile<BF16, true, true, 8, 8>(wsm + (size_t)2 * (ua - tb.s0) * rb, rb, 7, m.H, xs, m.H, res);
+      else warp_tile<BF16, false, true, 8, 8>(wg + (size_t)2 * ua * rb, rb, 7, m.H, xs, m.H, res);
+      epilogue(b0, ub, ua, sub, res);
     }
     DEFER_CTA_SYNC();
   }
@@ -1243,6 +1308,7 @@ __device__ void ph_head_wide_direct(const DModel& m, const DBatch& bt, const Par
   const unsigned char* wg = static_cast<const unsigned char*>(m.head);
   for (int b0 = pt.first; b0 < bt.B; b0 += pt.step) {
     stage_rows_inv<G>(m, bt, b0, bt.x, smem);
+    scale_rows<G>(m, m.norm, smem);
     for (int task = warp; task < (u1 - u0) * NSUB; task += kPW) {
       const int k = u0 + task / NSUB, sub = task % NSUB;
       const float* xs = smem + (size_t)sub * 8 * m.H;
@@ -1250,8 +1316,7 @@ __device__ void ph_head_wide_direct(const DModel& m, const DBatch& bt, const Par
       for (int t = 0; t < kSBlk / 8; t++) {
         const int r0 = min(k * kSBlk + 8 * t, m.V - 1);
         float res[2];
-        warp_tile<BF16, false, true, 8, 8, true>(wg + (size_t)r0 * rb, rb, m.V - 1 - r0, m.H, xs, m.H, res, m.norm,
-                                                 g_inv + sub * 8);
+        warp_tile<BF16, false, true, 8, 8>(wg + (size_t)r0 * rb, rb, m.V - 1 - r0, m.H, xs, m.H, res);
         const int s = lane >> 2, r = 8 * t + 2 * (lane & 3);
         tbuf[s * kSBlk + r] = res[0];
         tbuf[s * kSBlk + r + 1] = res[1];
@@ -1281,8 +1346,6 @@ __device__ __host__ __forceinline__ size_t head_staged_floats(int G, int H, bool
   return rows + 2 * ((size_t)(kSBlk / 2) * H * (bf16 ? 2 : 4) / 4);
 }
 
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_prior1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // The staged wide head: the CTA walks its vocabulary blocks in half blocks
 // of 16 rows, each copied into shared memory with cp.async while the
@@ -1314,6 +1377,7 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
   const int nh = 2 * (u1 - u0);  // half blocks of this CTA
   for (int b0 = pt.first; b0 < bt.B; b0 += pt.step) {
     stage_rows_inv<G>(m, bt, b0, bt.x, smem);
+    scale_rows<G>(m, m.norm, smem);
     auto issue = [&](int h) {
       if (h < nh) {
         const unsigned char* src = wg + ((size_t)u0 * kSBlk + (size_t)h * HALF) * rb;
@@ -1331,8 +1395,8 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
       for (int task = warp; task < TILES; task += kPW) {
         const int t = task / NSUB, sub = task % NSUB;
         float res[2];
-        warp_tile<BF16, true, true, 8, 8, true>(wh + (size_t)8 * t * rb, rb, 7, m.H, smem + (size_t)sub * 8 * m.H,
-                                                m.H, res, m.norm, g_inv + sub * 8);
+        warp_tile<BF16, true, true, 8, 8>(wh + (size_t)8 * t * rb, rb, 7, m.H, smem + (size_t)sub * 8 * m.H, m.H,
+                                          res);
         const int s = lane >> 2, r = (h & 1) * HALF + 8 * t + 2 * (lane & 3);
         float* row = sums + (size_t)(sub * 8 + s) * kSBlk;
         row[r] = res[0];
@@ -1461,10 +1525,48 @@ __device__ __forceinline__ void sum_range(const DBatch& bt, int cta, int ncta, i
   f1 = (int)(n * (cta + 1) / ncta);
 }
 
-// Block sums of e for slots sampling next (needs the max over all blocks).
-template <bool FIRST>
-__device__ void ph_sample1(const DModel& m, const DBatch& bt, int cta, int ncta) {
+// Sums of the blocks [ka, kb) of kSBlk values each, every sum sequential in
+// element order (the sums warp_seq_sum gives), written to out[k]. A warp
+// takes 32 blocks at a time: it computes val(i) for their 32 x 32 elements
+// with coalesced loads, stages them in buf (its own [32][33] floats) and
+// lane j then adds block j's values one after another.
+// `src` holds the raw values (a slot's logits, n of them); val(i, x) maps
+// raw value x of element i to the summand. All 32 loads of a lane are in
+// flight before any is used.
+template <class F>
+__device__ __forceinline__ void block_seq_sums(int ka, int kb, const float* src, int n, F val, float* buf,
+                                               float* out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  static_assert(kSBlk == 32, "one lane per block of 32 values");
+  for (int kc = ka + 32 * warp; kc < kb; kc += 32 * kPW) {
+    const int nk = min(32, kb - kc);
+    float x[32];
+#pragma unroll
+    for (int r = 0; r < 32; r++) {
+      const int i = (kc + r) * kSBlk + lane;
+      x[r] = (r < nk && i < n) ? ld_f(src + i) : 0.0f;
+    }
+#pragma unroll
+    for (int r = 0; r < 32; r++) {
+      const int i = (kc + r) * kSBlk + lane;
+      buf[r * 33 + lane] = (r < nk && i < n) ? val(x[r]) : 0.0f;
+    }
+    __syncwarp();
+    if (lane < nk) {
+      float sm = 0.0f;
+#pragma unroll
+      for (int t = 0; t < 32; t++) sm = __fadd_rn(sm, buf[lane * 33 + t]);
+      out[kc + lane] = sm;
+    }
+    __syncwarp();
+  }
+}
+
+// Block sums of e for slots sampling next (needs the max over all blocks).
+// smem: kPW * 32 * 33 floats.
+template <bool FIRST>
+__device__ void ph_sample1(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
+  const int warp = threadIdx.x >> 5;
   const int nb = bt.nblk;
   int f0, f1;
   sum_range(bt, cta, ncta, f0, f1);
@@ -1474,22 +1576,20 @@ __device__ void ph_sample1(const DModel& m, const DBatch& bt, int cta, int ncta)
     const float T = bt.sess[b].temperature;
     const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
     const float* lg = bt.logits + (size_t)b * m.V;
-    const int k1 = min(f1 - b * nb, nb);
-    for (int k = max(f0 - b * nb, 0) + warp; k < k1; k += kPW) {
-      const int i = k * kSBlk + lane;
-      const float e = i < m.V ? e_of(ld_f(lg + i), T, M) : 0.0f;
-      const float sm = warp_seq_sum(e);
-      if (lane == 0) bt.ss.esum[(size_t)b * nb + k] = sm;
-    }
+    block_seq_sums(max(f0 - b * nb, 0), min(f1 - b * nb, nb), lg, m.V,
+                   [T, M](float l) { return e_of(l, T, M); }, smem + (size_t)warp * 32 * 33,
+                   bt.ss.esum + (size_t)b * nb);
   }
 }
 
 // Block sums of p = e * (1/Z) for slots sampling next.
+// smem: the hierarchy's group sums, then kPW * 32 * 33 floats.
 template <bool FIRST>
 __device__ void ph_sample2(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int nb = bt.nblk;
   const int ng2 = (nb + 31) / 32;
+  const size_t tail = ((size_t)ng2 + (ng2 + 31) / 32 + 3) & ~(size_t)3;
   int f0, f1;
   sum_range(bt, cta, ncta, f0, f1);
   if (f0 >= f1) return;
@@ -1501,13 +1601,9 @@ __device__ void ph_sample2(const DModel& m, const DBatch& bt, int cta, int ncta,
     if (!(Z > 0.0f) || !isfinite(Z)) continue;  // SELECT falls back to argmax
     const float inv = __fdiv_rn(1.0f, Z);
     const float* lg = bt.logits + (size_t)b * m.V;
-    const int k1 = min(f1 - b * nb, nb);
-    for (int k = max(f0 - b * nb, 0) + warp; k < k1; k += kPW) {
-      const int i = k * kSBlk + lane;
-      const float p = i < m.V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
-      const float sm = warp_seq_sum(p);
-      if (lane == 0) bt.ss.psum[(size_t)b * nb + k] = sm;
-    }
+    block_seq_sums(max(f0 - b * nb, 0), min(f1 - b * nb, nb), lg, m.V,
+                   [T, M, inv](float l) { return __fmul_rn(e_of(l, T, M), inv); },
+                   smem + tail + (size_t)warp * 32 * 33, bt.ss.psum + (size_t)b * nb);
   }
 }
 
@@ -1536,11 +1632,17 @@ __host__ __device__ __forceinline__ size_t attn_buf_floats(int Gh, int HD) {
   return (size_t)Gh * HD + (size_t)kAttnChunk * (HD + 4) + (size_t)kAttnChunk * HD;
 }
 
-// Shared-memory floats of the chunk stage: slot state (2 B ints), scores
-// [Gh][kAttnChunk], chunk sums [Gh], two unit buffers.
-__host__ __device__ __forceinline__ size_t attn_smem_floats(int B, int Gh, int HD) {
-  return (((size_t)2 * B + 3) & ~(size_t)3) + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3) +
-         2 * attn_buf_floats(Gh, HD);
+// Shared-memory floats of the chunk stage with nbuf unit buffers: slot
+// state (2 B ints), scores [Gh][kAttnChunk], chunk sums [Gh], the buffers.
+constexpr int kAttnMaxBuf = 4;  // units in flight per CTA: up to kAttnMaxBuf - 1 ahead
+// Per-slot fields of the chunk stage cached in shared memory (read once per
+// stage instead of once per unit): K, V and mask pointers, active, pos, cap.
+constexpr int kAttnSlotFloats = 9;
+__host__ __device__ __forceinline__ size_t attn_head_floats(int B, int Gh) {
+  return (((size_t)kAttnSlotFloats * B + 3) & ~(size_t)3) + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3);
+}
+__host__ __device__ __forceinline__ size_t attn_smem_floats(int B, int Gh, int HD, int nbuf = 2) {
+  return attn_head_floats(B, Gh) + (size_t)nbuf * attn_buf_floats(Gh, HD);
 }
 
 static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
@@ -1553,15 +1655,28 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
   const int per_slot = m.NKV * maxc;
   const int units = bt.B * per_slot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int* s_act = reinterpret_cast<int*>(smem);
+  const float** s_kc = reinterpret_cast<const float**>(smem);  // 8-byte aligned: the dynamic area is
+  const float** s_vc = s_kc + bt.B;
+  const uint32_t** s_mask = reinterpret_cast<const uint32_t**>(s_vc + bt.B);
+  int* s_act = reinterpret_cast<int*>(s_mask + bt.B);
   int* s_pos = s_act + bt.B;
-  float* sc = smem + (((size_t)2 * bt.B + 3) & ~(size_t)3);  // [Gh][kAttnChunk]
+  int* s_cap = s_pos + bt.B;
+  float* sc = smem + (((size_t)kAttnSlotFloats * bt.B + 3) & ~(size_t)3);  // [Gh][kAttnChunk]
   float* lsum = sc + Gh * kAttnChunk;                          // [Gh]
   float* buf0 = sc + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3);
   const size_t bfl = attn_buf_floats(Gh, HD);
+  // as many unit buffers as the launch's shared memory holds (at least two)
+  const size_t have = bt.smem_bytes / sizeof(float), head = attn_head_floats(bt.B, Gh);
+  const size_t room = have > head ? have - head : 0;
+  const int NB = (int)max((size_t)2, min((size_t)kAttnMaxBuf, room / bfl));
   for (int b = tid; b < bt.B; b += kPT) {
     s_act[b] = ld_i(&bt.st[b].active);
     s_pos[b] = ld_i(&bt.st[b].pos);
+    const DSession& S = bt.sess[b];
+    s_kc[b] = S.kc;
+    s_vc[b] = S.vc;
+    s_mask[b] = S.mask;
+    s_cap[b] = S.cap;
   }
   DEFER_CTA_SYNC();
   auto live = [&](int u) {
@@ -1576,9 +1691,10 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
   auto issue = [&](int u, float* buf) {
     if (u >= 0) {
       const int b = u / per_slot, rem = u % per_slot, kvh = rem / maxc, c = rem % maxc;
-      const DSession& S = bt.sess[b];
+      const float* kc = s_kc[b];
+      const float* vc = s_vc[b];
       const int t0 = c * kAttnChunk, tn = min(kAttnChunk, s_pos[b] + 1 - t0);
-      const size_t base = ((size_t)l * m.NKV + kvh) * S.cap + t0;
+      const size_t base = ((size_t)l * m.NKV + kvh) * s_cap[b] + t0;
       const float* qsrc = bt.q + (size_t)b * m.QD + (size_t)kvh * Gh * HD;
       float* qs = buf;
       float* ks = qs + Gh * HD;
@@ -1587,31 +1703,41 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
       for (int f = tid; f < Gh * c4n; f += kPT) cp_async16_g2s(qs + 4 * f, qsrc + 4 * f);
       for (int f = tid; f < tn * c4n; f += kPT) {
         const int tt = f / c4n, c4 = f - tt * c4n;
-        cp_async16_g2s(ks + (size_t)tt * (HD + 4) + 4 * c4, S.kc + (base + tt) * HD + 4 * c4);
-        cp_async16_g2s(vs + (size_t)tt * HD + 4 * c4, S.vc + (base + tt) * HD + 4 * c4);
+        cp_async16_g2s(ks + (size_t)tt * (HD + 4) + 4 * c4, kc + (base + tt) * HD + 4 * c4);
+        cp_async16_g2s(vs + (size_t)tt * HD + 4 * c4, vc + (base + tt) * HD + 4 * c4);
       }
     }
     cp_async_commit();
   };
+  // The walk of this CTA's units is taken twice: u_iss, NB - 1 units ahead,
+  // issues the copies (group j holds the j-th unit, or nothing), u computes.
   int u = cta < units ? (live(cta) ? cta : next(cta)) : -1;
-  issue(u, buf0);
+  int u_iss = u, n_iss = 0;
+  auto issue_next = [&]() {
+    issue(u_iss, buf0 + (size_t)(n_iss % NB) * bfl);
+    n_iss++;
+    if (u_iss >= 0) u_iss = next(u_iss);
+  };
+  for (int j = 0; j < NB - 1; j++) issue_next();
   for (int it = 0; u >= 0; it++) {
-    const int un = next(u);
-    issue(un, buf0 + (size_t)((it + 1) & 1) * bfl);
-    cp_async_wait_prior1();
+    issue_next();  // into the buffer unit it - 1 used
+    // every group but the NB - 1 newest has landed: unit it's among them
+    if (NB == 2) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else if (NB == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
+    else asm volatile("cp.async.wait_group 3;" ::: "memory");
     DEFER_CTA_SYNC();
-    const float* qs = buf0 + (size_t)(it & 1) * bfl;
+    const float* qs = buf0 + (size_t)(it % NB) * bfl;
     const float* ks = qs + Gh * HD;
     const float* vs = ks + kAttnChunk * (HD + 4);
     const int b = u / per_slot, rem = u % per_slot, kvh = rem / maxc, c = rem % maxc;
-    const DSession& S = bt.sess[b];
+    const uint32_t* mask = s_mask[b];
     const int pos = s_pos[b], nch = pos / kAttnChunk + 1;
     const int t0 = c * kAttnChunk, tn = min(kAttnChunk, pos + 1 - t0);
     for (int idx = tid; idx < Gh * kAttnChunk; idx += kPT) {
       const int h = idx / kAttnChunk, tt = idx - h * kAttnChunk;
       float sv = -INFINITY;
       const int t = t0 + tt;
-      const bool masked = S.mask && t < pos && ((S.mask[t >> 5] >> (t & 31)) & 1u);
+      const bool masked = mask && t < pos && ((mask[t >> 5] >> (t & 31)) & 1u);
       if (tt < tn && !masked) {
         const float* kr = ks + (size_t)tt * (HD + 4);
         const float* qr = qs + h * HD;
@@ -1619,10 +1745,11 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
 #pragma unroll 4
         for (int d = 0; d < HD; d += 4) {
           const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
-          a0 = fmaf(qr[d], k4.x, a0);
-          a1 = fmaf(qr[d + 1], k4.y, a1);
-          a2 = fmaf(qr[d + 2], k4.z, a2);
-          a3 = fmaf(qr[d + 3], k4.w, a3);
+          const float4 q4 = *reinterpret_cast<const float4*>(qr + d);  // same address in the warp: broadcast
+          a0 = fmaf(q4.x, k4.x, a0);
+          a1 = fmaf(q4.y, k4.y, a1);
+          a2 = fmaf(q4.z, k4.z, a2);
+          a3 = fmaf(q4.w, k4.w, a3);
         }
         sv = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), m.scale);
       }
@@ -1651,15 +1778,21 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
     DEFER_CTA_SYNC();
     for (int idx = tid; idx < Gh * HD; idx += kPT) {
       const int h = idx / HD, d = idx - h * HD;
-      const float* e = sc + h * kAttnChunk;
+      const float* e = sc + h * kAttnChunk;  // e = 0 past tn
       float acc = 0.0f;
-#pragma unroll 8
-      for (int tt = 0; tt < tn; tt++) acc = fmaf(e[tt], vs[(size_t)tt * HD + d], acc);
+      for (int t4 = 0; t4 < tn; t4 += 4) {
+        const float4 e4 = *reinterpret_cast<const float4*>(e + t4);  // broadcast
+        const float* vr = vs + (size_t)t4 * HD + d;
+        acc = fmaf(e4.x, vr[0], acc);
+        if (t4 + 1 < tn) acc = fmaf(e4.y, vr[HD], acc);
+        if (t4 + 2 < tn) acc = fmaf(e4.z, vr[2 * HD], acc);
+        if (t4 + 3 < tn) acc = fmaf(e4.w, vr[3 * HD], acc);
+      }
       if (nch > 1) part_b[((size_t)(kvh * Gh + h) * maxc + c) * (HD + 2) + 2 + d] = acc;
       else bt.att[(size_t)b * m.QD + (size_t)(kvh * Gh + h) * HD + d] = __fdiv_rn(acc, lsum[h]);
     }
     DEFER_CTA_SYNC();  // the buffer, the scores and the sums are reused
-    u = un;
+    u = next(u);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
 }

@@ -126,19 +126,21 @@ def test_wide_slot_groups_agree_with_single_sessions(mdir):
     assert wide["barrier"] == wide["phased"] == alone
 
 
-def test_partitioned_slot_groups_agree_with_single_sessions(mdir):
-    """The 135M shape with 72 sessions in a 96-slot batch: three 32-slot
-    groups, each owned by its own CTA partition (every partition covers all
-    rows, with row blocks shifted back at the end of each matrix), give the
-    tokens each session gives alone."""
+@pytest.mark.parametrize("n,batch", [(72, 96), (200, 256)])
+def test_partitioned_slot_groups_agree_with_single_sessions(mdir, n, batch):
+    """The 135M shape with 72 sessions in a 96-slot batch (three 32-slot
+    groups, each owned by its own CTA partition; every partition covers all
+    rows, with row blocks shifted back at the end of each matrix) and 200
+    sessions in 256 slots (more rows per CTA than shared memory holds, so
+    the weights stream through it in double-buffered steps) give the tokens
+    each session gives alone."""
     gm = D.Model.load(model_file(mdir, "smollm2-135m"))
-    n = 72
     V = gm.config.vocab_size
     prompts = [_tokens(V, 2 + (5 * i) % 17, 500 + i) for i in range(n)]
     seeds = [D.seed_from_u64(700 + i) for i in range(n)]
     temps = [[0.0, 0.8, 1.1][i % 3] for i in range(n)]
     maxt = [3 + (7 * i) % 9 for i in range(n)]
-    wide = {p: _on_path(p, lambda: D.generate_batch(gm, prompts, seeds, temps, maxt, batch=96)[0])
+    wide = {p: _on_path(p, lambda: D.generate_batch(gm, prompts, seeds, temps, maxt, batch=batch)[0])
             for p in ("barrier", "phased")}
     alone = _on_path("flow", lambda: D.generate_batch(gm, prompts, seeds, temps, maxt, batch=1)[0])
     assert wide["barrier"] == wide["phased"] == alone
