@@ -207,9 +207,9 @@ static size_t step_smem_floats(const DModel& m, int B, int max_chunks) {
   (void)max_chunks;
   // attention chunks: slot state, scores and at least two unit buffers (more
   // when the other stages leave room, up to kAttnMaxBuf)
-  f = std::max(f, attn_smem_floats(B, Gh, m.HD, 2));
-  const size_t a4 = attn_smem_floats(B, Gh, m.HD, kAttnMaxBuf);
-  if (a4 * 4 <= 200 * 1024) f = std::max(f, a4);
+  f = std::max(f, attn_smem_floats(B, Gh, m.HD, 1, 2));
+  const size_t a2 = attn_smem_floats(B, Gh, m.HD, 2, 2);  // two CTA parts, when that fits
+  if (a2 * 4 <= 200 * 1024) f = std::max(f, a2);
   // the wide head: normalized rows plus one [8][kSBlk] tile buffer per warp
   if (G >= 8) {
     f = std::max(f, (((size_t)G * m.H + 3) & ~(size_t)3) + (size_t)kPW * 8 * kSBlk);

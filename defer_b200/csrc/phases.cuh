@@ -1632,19 +1632,37 @@ __host__ __device__ __forceinline__ size_t attn_buf_floats(int Gh, int HD) {
   return (size_t)Gh * HD + (size_t)kAttnChunk * (HD + 4) + (size_t)kAttnChunk * HD;
 }
 
-// Shared-memory floats of the chunk stage with nbuf unit buffers: slot
-// state (2 B ints), scores [Gh][kAttnChunk], chunk sums [Gh], the buffers.
-constexpr int kAttnMaxBuf = 4;  // units in flight per CTA: up to kAttnMaxBuf - 1 ahead
-// Per-slot fields of the chunk stage cached in shared memory (read once per
-// stage instead of once per unit): K, V and mask pointers, active, pos, cap.
+// The chunk stage's shared memory: per-slot fields cached once per stage
+// (K, V and mask pointers, active, pos, cap), then per CTA part its scores
+// [Gh][kAttnChunk], chunk sums [Gh] and nbuf unit buffers.
+constexpr int kAttnMaxBuf = 4;  // unit buffers per part: up to kAttnMaxBuf - 1 units in flight
 constexpr int kAttnSlotFloats = 9;
-__host__ __device__ __forceinline__ size_t attn_head_floats(int B, int Gh) {
-  return (((size_t)kAttnSlotFloats * B + 3) & ~(size_t)3) + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3);
+__host__ __device__ __forceinline__ size_t attn_slot_floats(int B) {
+  return ((size_t)kAttnSlotFloats * B + 3) & ~(size_t)3;
 }
-__host__ __device__ __forceinline__ size_t attn_smem_floats(int B, int Gh, int HD, int nbuf = 2) {
-  return attn_head_floats(B, Gh) + (size_t)nbuf * attn_buf_floats(Gh, HD);
+__host__ __device__ __forceinline__ size_t attn_part_floats(int Gh, int HD, int nbuf) {
+  return (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3) + (size_t)nbuf * attn_buf_floats(Gh, HD);
+}
+__host__ __device__ __forceinline__ size_t attn_smem_floats(int B, int Gh, int HD, int parts, int nbuf) {
+  return attn_slot_floats(B) + (size_t)parts * attn_part_floats(Gh, HD, nbuf);
 }
 
+// Barrier of one CTA part: the whole CTA, or (two parts) its own half
+// through named barrier 1 + part.
+__device__ __forceinline__ void attn_part_sync(int parts, int part) {
+  if (parts == 1) {
+    DEFER_CTA_SYNC();
+  } else {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + part), "r"(kPT / 2) : "memory");
+  }
+}
+
+// CHUNKS stage. The CTA splits into two independent parts of kPW / 2 warps
+// when two parts with two unit buffers each fit its shared memory (a unit's
+// work is a few short dependent chains, so two units in flight side by side
+// keep more warps busy than one unit at a time), else it works as one part.
+// Part p of CTA c takes units v, v + V, ... with v = c * parts + p and V =
+// ncta * parts, and walks them with the next units' copies in flight.
 static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, int cta, int ncta, float* smem) {
   {  // the gate/up projection comes after the O projection
     const DLayer& Ly = m.layers[l];
@@ -1654,22 +1672,13 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
   const int maxc = bt.max_chunks;
   const int per_slot = m.NKV * maxc;
   const int units = bt.B * per_slot;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float** s_kc = reinterpret_cast<const float**>(smem);  // 8-byte aligned: the dynamic area is
   const float** s_vc = s_kc + bt.B;
   const uint32_t** s_mask = reinterpret_cast<const uint32_t**>(s_vc + bt.B);
   int* s_act = reinterpret_cast<int*>(s_mask + bt.B);
   int* s_pos = s_act + bt.B;
   int* s_cap = s_pos + bt.B;
-  float* sc = smem + (((size_t)kAttnSlotFloats * bt.B + 3) & ~(size_t)3);  // [Gh][kAttnChunk]
-  float* lsum = sc + Gh * kAttnChunk;                          // [Gh]
-  float* buf0 = sc + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3);
-  const size_t bfl = attn_buf_floats(Gh, HD);
-  // as many unit buffers as the launch's shared memory holds (at least two)
-  const size_t have = bt.smem_bytes / sizeof(float), head = attn_head_floats(bt.B, Gh);
-  const size_t room = have > head ? have - head : 0;
-  const int NB = (int)max((size_t)2, min((size_t)kAttnMaxBuf, room / bfl));
-  for (int b = tid; b < bt.B; b += kPT) {
+  for (int b = threadIdx.x; b < bt.B; b += kPT) {
     s_act[b] = ld_i(&bt.st[b].active);
     s_pos[b] = ld_i(&bt.st[b].pos);
     const DSession& S = bt.sess[b];
@@ -1679,12 +1688,26 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
     s_cap[b] = S.cap;
   }
   DEFER_CTA_SYNC();
+  const size_t bfl = attn_buf_floats(Gh, HD);
+  const size_t have = bt.smem_bytes / sizeof(float), slots = attn_slot_floats(bt.B);
+  const size_t room = have > slots ? have - slots : 0;
+  const int parts = room >= 2 * attn_part_floats(Gh, HD, 2) ? 2 : 1;
+  const size_t per_part = room / parts;
+  int NB = 2;
+  while (NB < kAttnMaxBuf && attn_part_floats(Gh, HD, NB + 1) <= per_part) NB++;
+  const int nthr = kPT / parts;
+  const int part = threadIdx.x / nthr;
+  const int tid = threadIdx.x - part * nthr, warp = tid >> 5, lane = tid & 31, nw = nthr / 32;
+  float* sc = smem + slots + (size_t)part * attn_part_floats(Gh, HD, NB);  // [Gh][kAttnChunk]
+  float* lsum = sc + Gh * kAttnChunk;                                        // [Gh]
+  float* buf0 = sc + (((size_t)Gh * kAttnChunk + Gh + 3) & ~(size_t)3);
+  const int vstep = ncta * parts;
   auto live = [&](int u) {
     const int b = u / per_slot, c = u % maxc;
     return s_act[b] && c <= s_pos[b] / kAttnChunk;
   };
   auto next = [&](int u) {
-    for (u += ncta; u < units; u += ncta)
+    for (u += vstep; u < units; u += vstep)
       if (live(u)) return u;
     return -1;
   };
@@ -1700,8 +1723,8 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
       float* ks = qs + Gh * HD;
       float* vs = ks + kAttnChunk * (HD + 4);
       const int c4n = HD / 4;
-      for (int f = tid; f < Gh * c4n; f += kPT) cp_async16_g2s(qs + 4 * f, qsrc + 4 * f);
-      for (int f = tid; f < tn * c4n; f += kPT) {
+      for (int f = tid; f < Gh * c4n; f += nthr) cp_async16_g2s(qs + 4 * f, qsrc + 4 * f);
+      for (int f = tid; f < tn * c4n; f += nthr) {
         const int tt = f / c4n, c4 = f - tt * c4n;
         cp_async16_g2s(ks + (size_t)tt * (HD + 4) + 4 * c4, kc + (base + tt) * HD + 4 * c4);
         cp_async16_g2s(vs + (size_t)tt * HD + 4 * c4, vc + (base + tt) * HD + 4 * c4);
@@ -1709,9 +1732,10 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
     }
     cp_async_commit();
   };
-  // The walk of this CTA's units is taken twice: u_iss, NB - 1 units ahead,
-  // issues the copies (group j holds the j-th unit, or nothing), u computes.
-  int u = cta < units ? (live(cta) ? cta : next(cta)) : -1;
+  // The part's walk is taken twice: u_iss, NB - 1 units ahead, issues the
+  // copies (group j holds the j-th unit, or nothing), u computes.
+  const int v0 = cta * parts + part;
+  int u = v0 < units ? (live(v0) ? v0 : next(v0)) : -1;
   int u_iss = u, n_iss = 0;
   auto issue_next = [&]() {
     issue(u_iss, buf0 + (size_t)(n_iss % NB) * bfl);
@@ -1725,7 +1749,7 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
     if (NB == 2) asm volatile("cp.async.wait_group 1;" ::: "memory");
     else if (NB == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
     else asm volatile("cp.async.wait_group 3;" ::: "memory");
-    DEFER_CTA_SYNC();
+    attn_part_sync(parts, part);
     const float* qs = buf0 + (size_t)(it % NB) * bfl;
     const float* ks = qs + Gh * HD;
     const float* vs = ks + kAttnChunk * (HD + 4);
@@ -1733,7 +1757,7 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
     const uint32_t* mask = s_mask[b];
     const int pos = s_pos[b], nch = pos / kAttnChunk + 1;
     const int t0 = c * kAttnChunk, tn = min(kAttnChunk, pos + 1 - t0);
-    for (int idx = tid; idx < Gh * kAttnChunk; idx += kPT) {
+    for (int idx = tid; idx < Gh * kAttnChunk; idx += nthr) {
       const int h = idx / kAttnChunk, tt = idx - h * kAttnChunk;
       float sv = -INFINITY;
       const int t = t0 + tt;
@@ -1755,14 +1779,14 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
       }
       sc[idx] = sv;
     }
-    DEFER_CTA_SYNC();
+    attn_part_sync(parts, part);
     float* part_b = bt.part + (size_t)b * m.NH * maxc * (HD + 2);
-    for (int h = warp; h < Gh; h += kPW) {
+    for (int h = warp; h < Gh; h += nw) {
       float* row = sc + h * kAttnChunk;
-      const float v0 = row[lane], v1 = row[lane + 32];
-      const float mx = warp_max(fmaxf(v0, v1));
-      const float e0 = (v0 == -INFINITY) ? 0.0f : expf(__fsub_rn(v0, mx));
-      const float e1 = (v1 == -INFINITY) ? 0.0f : expf(__fsub_rn(v1, mx));
+      const float v0s = row[lane], v1s = row[lane + 32];
+      const float mx = warp_max(fmaxf(v0s, v1s));
+      const float e0 = (v0s == -INFINITY) ? 0.0f : expf(__fsub_rn(v0s, mx));
+      const float e1 = (v1s == -INFINITY) ? 0.0f : expf(__fsub_rn(v1s, mx));
       row[lane] = e0;
       row[lane + 32] = e1;
       const float ls = warp_sum_butterfly(__fadd_rn(e0, e1));
@@ -1775,8 +1799,8 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
         }
       }
     }
-    DEFER_CTA_SYNC();
-    for (int idx = tid; idx < Gh * HD; idx += kPT) {
+    attn_part_sync(parts, part);
+    for (int idx = tid; idx < Gh * HD; idx += nthr) {
       const int h = idx / HD, d = idx - h * HD;
       const float* e = sc + h * kAttnChunk;  // e = 0 past tn
       float acc = 0.0f;
@@ -1791,10 +1815,11 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
       if (nch > 1) part_b[((size_t)(kvh * Gh + h) * maxc + c) * (HD + 2) + 2 + d] = acc;
       else bt.att[(size_t)b * m.QD + (size_t)(kvh * Gh + h) * HD + d] = __fdiv_rn(acc, lsum[h]);
     }
-    DEFER_CTA_SYNC();  // the buffer, the scores and the sums are reused
+    attn_part_sync(parts, part);  // the buffer, the scores and the sums are reused
     u = next(u);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
+  DEFER_CTA_SYNC();  // both parts done before the CTA leaves the stage
 }
 
 // Merge of the chunk partials of every (slot, query head) with two or more
