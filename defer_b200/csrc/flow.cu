@@ -145,7 +145,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-// Global -> shared bulk copy (no multicast); 16-byte aligned, size % 16 == 0.
+// Global -> this CTA's shared memory bulk copy; 16-byte aligned, size % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),

@@ -1724,10 +1724,21 @@ static __device__ void ph_attn_chunks(const DModel& m, const DBatch& bt, int l, 
       float* vs = ks + kAttnChunk * (HD + 4);
       const int c4n = HD / 4;
       for (int f = tid; f < Gh * c4n; f += nthr) cp_async16_g2s(qs + 4 * f, qsrc + 4 * f);
-      for (int f = tid; f < tn * c4n; f += nthr) {
-        const int tt = f / c4n, c4 = f - tt * c4n;
-        cp_async16_g2s(ks + (size_t)tt * (HD + 4) + 4 * c4, kc + (base + tt) * HD + 4 * c4);
-        cp_async16_g2s(vs + (size_t)tt * HD + 4 * c4, vc + (base + tt) * HD + 4 * c4);
+      if (nthr % c4n == 0) {
+        // a thread's 16-byte column c4 stays fixed; its row advances by nthr / c4n
+        const int c4 = tid % c4n, dt = nthr / c4n;
+        const float* kg = kc + base * HD + 4 * c4;
+        const float* vg = vc + base * HD + 4 * c4;
+        for (int tt = tid / c4n; tt < tn; tt += dt) {
+          cp_async16_g2s(ks + (size_t)tt * (HD + 4) + 4 * c4, kg + (size_t)tt * HD);
+          cp_async16_g2s(vs + (size_t)tt * HD + 4 * c4, vg + (size_t)tt * HD);
+        }
+      } else {
+        for (int f = tid; f < tn * c4n; f += nthr) {
+          const int tt = f / c4n, c4 = f - tt * c4n;
+          cp_async16_g2s(ks + (size_t)tt * (HD + 4) + 4 * c4, kc + (base + tt) * HD + 4 * c4);
+          cp_async16_g2s(vs + (size_t)tt * HD + 4 * c4, vc + (base + tt) * HD + 4 * c4);
+        }
       }
     }
     cp_async_commit();
