@@ -431,12 +431,18 @@ def main(argv=None):
                     help="sessions of the batched replay measurement (config 3); 0 skips it")
     ap.add_argument("--replay-gen", type=int, default=512, help="generated tokens per replay session")
     ap.add_argument("--replay-batch", type=int, default=512, help="slots per GPU of the batched replay")
-    ap.add_argument("--profile-case", action="store_true",
-                    help="no measurement: the small case profiles are captured on (135M model, "
-                         "16-token prompt, then one launch of 32 sampled tokens)")
+    ap.add_argument("--profile-case", nargs="?", const="single", choices=["single", "batched"],
+                    help="no measurement: a small case for profiles. single: the 135M model, 16-token "
+                         "prompt, then one launch of 32 sampled tokens (dataflow kernel). batched: "
+                         "--profile-slots sessions with --profile-prompt prompts and 2 sampled tokens "
+                         "in one batch on the per-stage launch path (one kernel per stage)")
+    ap.add_argument("--profile-slots", type=int, default=512)
+    ap.add_argument("--profile-prompt", type=int, default=128)
     a = ap.parse_args(argv)
     if a.impl == "reference":
         return run_reference(a)
+    if a.profile_case == "batched":
+        return profile_case_batched(a.profile_slots, a.profile_prompt)
     if a.profile_case:
         return profile_case()
     return run_b200(a)
@@ -454,6 +460,23 @@ def profile_case():
     s.prompt([int(t) for t in np.random.default_rng(1).integers(0, m.config.vocab_size, 16)])
     s.generate(32)
     print(json.dumps({"profile_case": "ok", **m.timing()}))
+    return 0
+
+
+def profile_case_batched(n: int, plen: int):
+    """n sessions (plen-token uniform prompts, T=0.8, 2 sampled tokens) as one
+    batch on the per-stage launch path, so that ncu sees every stage of the
+    batched step as its own kernel."""
+    os.environ["DEFER_B200_PHASED"] = "1"
+    import numpy as np
+    import defer_b200 as D
+    from defer_b200 import synthetic
+    m = D.Model.load(synthetic.model_path(MODEL, model_dir(), 0))
+    rng = np.random.default_rng(3)
+    prompts = [[int(t) for t in rng.integers(0, m.config.vocab_size, plen)] for _ in range(n)]
+    seeds = [D.seed_from_u64(i) for i in range(n)]
+    _, ms = D.generate_batch(m, prompts, seeds, [0.8] * n, [2] * n, batch=n)
+    print(json.dumps({"profile_case": "batched", "slots": n, "steps": plen + 2, "device_ms": ms}))
     return 0
 
 
