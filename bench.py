@@ -282,7 +282,8 @@ def batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barr
     h2d = sum(len(c.to_bytes()) for c in cks)
     d2h = 12 * len(cks)
     return {"metric": "batched replay tok/s (verified checkout of many WALs)", "value": value, "unit": "tok/s",
-            "n_gpus": world, "sessions": n, "tokens": int(all_tokens), "divergences": int(all_fail),
+            "n_gpus": world, "scaling": "strong", "sessions": n, "tokens": int(all_tokens),
+            "divergences": int(all_fail),
             "batch_per_gpu": batch, "device_s": dev_s, "generate_tok_s": all_tokens / gen_s,
             "gpu_launches": launches,
             "config": {"workload": REPLAY_WORKLOAD.format(n=n, n1=n - 1, gen=gen),
@@ -308,7 +309,8 @@ def run_b200(args):
         import torch
         import torch.distributed as tdist
         torch.cuda.set_device(local)
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device(f"cuda:{local}"))
         dist = tdist
 
     # single-session runs use the dataflow token-loop kernel; fail loudly if it does not apply
