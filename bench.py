@@ -297,6 +297,44 @@ def batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barr
                     "d2h_bytes_per_step": d2h}}
 
 
+# ------------------------------------------------ ablation attribution (config 4)
+ABLATION_WORKLOAD = ("config4: SmolLM2-1.7B-shape fp32 Llama (synthetic N(0,0.02) seed 0); leave-one-out "
+                     "attribution over a 128-token uniform-random context: base run plus 127 ablated variants "
+                     "(every position but the query, attribution.rs:237), each replayed from its masked "
+                     "position with one masked cache per variant, variants batched in one token loop")
+
+
+def ablation_measure(D, rank, sms, clk_mhz):
+    """Config 4 on this rank: returns the JSON object (device time of the
+    ablation's token-loop launches)."""
+    import numpy as np
+    from defer_b200 import synthetic
+    m = D.Model.load(synthetic.model_path("smollm2-1.7b", model_dir(), 0))
+    ctx = [int(t) for t in np.random.default_rng(4 + rank).integers(0, m.config.vocab_size, 128)]
+    positions = list(range(len(ctx) - 1))
+    D.ablation_attribution(m, ctx[:16], ctx[16], list(range(15)))  # warm-up
+    m.timing(reset=True)
+    t0 = time.perf_counter()
+    base, rows = D.ablation_attribution(m, ctx, ctx[-1], positions)
+    wall = time.perf_counter() - t0
+    tm = m.timing(reset=True)
+    n = len(ctx)
+    forwards = n + sum(n - p - 1 for p in positions)  # base + every variant's replay from p + 1
+    c = m.config
+    H, FF, QD, KVD = c.hidden_size, c.intermediate_size, c.q_dim, c.kv_dim
+    mac = c.num_layers * (H * (QD + 2 * KVD) + QD * H + 3 * FF * H) + c.vocab_size * H
+    dev_s = tm["device_ms"] / 1e3
+    achieved = forwards * 2.0 * mac / dev_s / 1e12
+    peak = sms * FP32_FMA_PER_SM_CLK * 2 * clk_mhz * 1e6 / 1e12
+    return {"metric": "ablation forwards/s (leave-one-out attribution)", "value": forwards / dev_s,
+            "unit": "forwards/s", "variants": len(positions), "forwards": forwards, "device_s": dev_s,
+            "wall_s": wall, "gpu_launches": tm["launches"], "base_logprob": base,
+            "config": {"workload": ABLATION_WORKLOAD},
+            "roofline": {"bound": "fp32 simt", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_kind": f"nominal: {sms} SMs x {FP32_FMA_PER_SM_CLK} fp32 "
+                                                               f"FMA/clk x 2 x {clk_mhz:.0f} MHz"}}
+
+
 def run_b200(args):
     import numpy as np  # noqa: F401
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -374,14 +412,20 @@ def run_b200(args):
         barrier()
     tm = m.timing(reset=True)
     clocks = clk.summary()
+    os.environ.pop("DEFER_B200_LOOP", None)  # wide batches below take the grid-barrier token loop
     replay = None
     if args.replay_sessions > 0:
         import torch
         sms = torch.cuda.get_device_properties(local).multi_processor_count
         clk_mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
-        os.environ.pop("DEFER_B200_LOOP", None)  # wide batches take the grid-barrier token loop
         replay = batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barrier, sms, clk_mhz)
         m.timing(reset=True)
+    ablation = None
+    if args.ablation:
+        import torch
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        clk_mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
+        ablation = ablation_measure(D, rank, sms, clk_mhz)
     try:
         os.unlink(wal)
     except OSError:
@@ -413,6 +457,7 @@ def run_b200(args):
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d // max(args.steps, 1),
                         "d2h_bytes_per_step": d2h // max(args.steps, 1)},
                 "gpu_launches": tm["launches"], "clocks": clocks, "batched_replay": replay,
+                "ablation": ablation,
                 "device": {"tokens": tokens, "device_ms": tm["device_ms"], "runs": tm["runs"]}}
         print(json.dumps(line), flush=True)
     if dist:
@@ -433,6 +478,8 @@ def main(argv=None):
                     help="sessions of the batched replay measurement (config 3); 0 skips it")
     ap.add_argument("--replay-gen", type=int, default=512, help="generated tokens per replay session")
     ap.add_argument("--replay-batch", type=int, default=512, help="slots per GPU of the batched replay")
+    ap.add_argument("--ablation", action="store_true",
+                    help="also measure config 4 (1.7B-shape leave-one-out attribution, 127 variants)")
     ap.add_argument("--profile-case", nargs="?", const="single", choices=["single", "batched"],
                     help="no measurement: a small case for profiles. single: the 135M model, 16-token "
                          "prompt, then one launch of 32 sampled tokens (dataflow kernel). batched: "
