@@ -1114,15 +1114,21 @@ template <bool BF16, int G>
 __device__ void ph_residual_wide(const DModel& m, const DBatch& bt, const void* W, int K, const float* xin, int cta,
                                  int ncta, float* smem, size_t smem_floats) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int NU = 4, NSUB = G / 8;
+  constexpr int NSUB = G / 8;
   const int units = m.H;
   const Part pt = part_of<G>(bt, cta, ncta);
   int u0, u1;
   cta_range(units, pt.ci, pt.nci, u0, u1);
   if (u0 >= u1) return;
+  const bool staged = (size_t)G * K <= smem_floats;
+  // the down projection (inputs wider than the hidden state) on a CTA with
+  // 16 or more rows uses 8-row tiles (lane L: rows 2 (L % 4), +1 of slot
+  // L / 4): half the activation loads per FMA and half the tasks; fewer rows
+  // or short inputs keep 4-row tiles (measured faster there)
+  const bool rows8 = staged && K > m.H && u1 - u0 >= 16 && units >= 8;
+  const int NU = rows8 ? 8 : 4;
   const TileBlocks tb = tile_blocks(u0, u1, units, NU);
   const size_t rb = row_bytes(K, BF16);
-  const bool staged = (size_t)G * K <= smem_floats;
   const unsigned char* wsm =
       stage_weights(W, tb.s0, tb.s1 - tb.s0, rb, smem, staged ? (size_t)G * K : 0, bt.smem_bytes);
   const unsigned char* wg = static_cast<const unsigned char*>(W);
@@ -1137,8 +1143,24 @@ __device__ void ph_residual_wide(const DModel& m, const DBatch& bt, const void* 
       const int blk = task / NSUB, sub = task % NSUB;
       int ub, ua;
       tile_block(u0, blk, units, NU, ub, ua);
-      float res[1];
       const unsigned char* w0 = wsm ? wsm + (size_t)(ua - tb.s0) * rb : wg + (size_t)ua * rb;
+      if (rows8) {
+        float res2[2];
+        const float* xs = smem + (size_t)sub * 8 * K;
+        if (wsm) warp_tile<BF16, true, true, 8, 8>(w0, rb, 7, K, xs, K, res2);
+        else warp_tile<BF16, false, true, 8, 8>(w0, rb, 7, K, xs, K, res2);
+        const int gg = sub * 8 + (lane >> 2), b = b0 + gg;
+        if (!g_act[gg]) continue;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          const int r = ua + 2 * (lane & 3) + i;
+          if (r < ub || r >= u1) continue;
+          float* x = bt.x + (size_t)b * m.H + r;
+          *x = __fadd_rn(ld_f(x), res2[i]);
+        }
+        continue;
+      }
+      float res[1];
       if (staged) {
         const float* xs = smem + (size_t)sub * 8 * K;
         if (wsm) warp_tile<BF16, true, true, 4, 8>(w0, rb, 3, K, xs, K, res);
