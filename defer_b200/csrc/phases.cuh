@@ -348,10 +348,11 @@ __device__ __forceinline__ void prefetch_rows(const void* W, int rows_total, int
 
 // ------------------------------------------------------------ RMSNorm
 // Per-group slot state of the stage in flight (load_slot_state): whether
-// slot b0 + g feeds a token this step, and its position; g_live marks the
-// rows stage_rows copied.
+// slot b0 + g feeds a token this step, its position and its sampling
+// temperature; g_live marks the rows stage_rows copied.
 static __shared__ int g_act[kMaxGroupWide];
 static __shared__ int g_pos[kMaxGroupWide];
+static __shared__ float g_temp[kMaxGroupWide];
 static __shared__ int g_live[kMaxGroupWide];
 
 template <int G>
@@ -360,6 +361,7 @@ __device__ void load_slot_state(const DBatch& bt, int b0) {
     const int b = b0 + threadIdx.x;
     g_act[threadIdx.x] = b < bt.B ? ld_i(&bt.st[b].active) : 0;
     g_pos[threadIdx.x] = b < bt.B ? ld_i(&bt.st[b].pos) : 0;
+    g_temp[threadIdx.x] = b < bt.B ? bt.sess[b].temperature : 0.0f;
   }
   DEFER_CTA_SYNC();
 }
@@ -1426,15 +1428,43 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
       }
       DEFER_CTA_SYNC();  // the half's buffer is free again; after an odd half the block's sums are complete
       if (h & 1) {
+        // logits and block statistics of the block: a warp's slots warp,
+        // warp + kPW, ... with their reductions interleaved (max and
+        // lowest-index argmax do not depend on the order of combination)
         const int k = u0 + h / 2;
         const int i = k * kSBlk + lane;
-        for (int gg = warp; gg < G; gg += kPW) {
-          if (!g_act[gg]) continue;
-          const int b = b0 + gg;
-          const float v = sums[(size_t)gg * kSBlk + lane];
-          bt.logits[(size_t)b * m.V + i] = v;
-          const size_t o = (size_t)b * nb + k;
-          block_stats(v, i, true, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+        constexpr int Q = (G + kPW - 1) / kPW;
+        ValIdx best[Q];
+        float smx[Q];
+#pragma unroll
+        for (int q = 0; q < Q; q++) {
+          const int gg = warp + q * kPW;
+          const bool on = gg < G && g_act[gg];
+          const float v = on ? sums[(size_t)gg * kSBlk + lane] : 0.0f;
+          if (on) bt.logits[(size_t)(b0 + gg) * m.V + i] = v;
+          const float T = on ? g_temp[gg] : 0.0f;
+          best[q] = ValIdx{v, !isnan(v) ? i : INT_MAX};
+          smx[q] = (on && T != 0.0f) ? __fdiv_rn(v, T) : -INFINITY;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+          for (int q = 0; q < Q; q++) {
+            const ValIdx o{__shfl_xor_sync(0xffffffffu, best[q].v, off), __shfl_xor_sync(0xffffffffu, best[q].i, off)};
+            if (vi_better(o, best[q])) best[q] = o;
+            smx[q] = fmaxf(smx[q], __shfl_xor_sync(0xffffffffu, smx[q], off));
+          }
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int q = 0; q < Q; q++) {
+            const int gg = warp + q * kPW;
+            if (gg >= G || !g_act[gg]) continue;
+            const size_t o = (size_t)(b0 + gg) * nb + k;
+            bt.ss.lmax[o] = best[q].v;
+            bt.ss.larg[o] = best[q].i;
+            bt.ss.smax[o] = smx[q];
+          }
         }
         // the sums are rewritten from the next half on, after its barrier
       }
