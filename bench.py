@@ -487,9 +487,14 @@ def main(argv=None):
                          "in one batch on the per-stage launch path (one kernel per stage)")
     ap.add_argument("--profile-slots", type=int, default=512)
     ap.add_argument("--profile-prompt", type=int, default=128)
+    ap.add_argument("--trace", action="store_true",
+                    help="no measurement: per-stage critical-path breakdown of the dataflow kernel from "
+                         "globaltimer stamps of one traced step (--profile-prompt tokens of context)")
     a = ap.parse_args(argv)
     if a.impl == "reference":
         return run_reference(a)
+    if a.trace:
+        return profile_trace(a.profile_prompt)
     if a.profile_case == "batched":
         return profile_case_batched(a.profile_slots, a.profile_prompt)
     if a.profile_case:
@@ -509,6 +514,91 @@ def profile_case():
     s.prompt([int(t) for t in np.random.default_rng(1).integers(0, m.config.vocab_size, 16)])
     s.generate(32)
     print(json.dumps({"profile_case": "ok", **m.timing()}))
+    return 0
+
+
+STAGE_KINDS = ("qkv", "attn", "o", "gateup", "down")
+
+
+def stage_names(L: int):
+    names = ["select"]
+    for l in range(L):
+        names += [f"{k}{l}" for k in STAGE_KINDS]
+    return names + ["head", "sum1", "sum2"]
+
+
+def trace_summary(tr, L: int):
+    """Critical path of one traced step of the dataflow kernel. tr[c, k, :]
+    holds globaltimer ns of CTA c in stage k: entry, inputs received, then
+    each phase warp's finish. For stage k with producer stage p: end(k) =
+    last finish over CTAs; span = end(k) - end(p) (its share of the step);
+    handoff = a CTA's receipt minus end(p) (last producer store to the
+    consumer holding every input); compute = a CTA's last warp finish minus
+    its receipt; tail = end(k) minus the median CTA's finish."""
+    import numpy as np
+    tr = np.asarray(tr, dtype=np.int64)
+    names = stage_names(L)
+    done = tr[:, :, 2:].max(axis=2)
+    recv = tr[:, :, 1]
+    ends = done.max(axis=0)
+    prod = {0: None}
+    for l in range(L):
+        q = 1 + 5 * l
+        prod[q] = 0 if l == 0 else q - 1
+        for j in range(1, 5):
+            prod[q + j] = q + j - 1
+    prod[1 + 5 * L] = 5 * L
+    prod[2 + 5 * L] = 1 + 5 * L
+    prod[3 + 5 * L] = 2 + 5 * L
+    rows = {}
+    for k, name in enumerate(names):
+        p = prod.get(k)
+        if p is None or ends[k] == 0 or ends[p] == 0:
+            continue
+        part = (done[:, k] > 0) & (recv[:, k] > 0)
+        if not part.any():
+            continue
+        ho = (recv[part, k] - ends[p]) / 1e3
+        cp = (done[part, k] - recv[part, k]) / 1e3
+        kind = name.rstrip("0123456789")
+        r = rows.setdefault(kind, {"n": 0, "span": [], "handoff_med": [], "handoff_max": [], "compute_med": [],
+                                   "compute_max": [], "tail": [], "ctas": []})
+        r["n"] += 1
+        r["span"].append((ends[k] - ends[p]) / 1e3)
+        r["handoff_med"].append(float(np.median(ho)))
+        r["handoff_max"].append(float(ho.max()))
+        r["compute_med"].append(float(np.median(cp)))
+        r["compute_max"].append(float(cp.max()))
+        r["tail"].append((ends[k] - np.median(done[part, k])) / 1e3)
+        r["ctas"].append(int(part.sum()))
+    out = {}
+    for kind, r in rows.items():
+        out[kind] = {"stages": r["n"], **{key: round(float(np.mean(v)), 3) for key, v in r.items()
+                                          if key != "n"}}
+    t0 = tr[:, 0, 0][tr[:, 0, 0] > 0].min() if (tr[:, 0, 0] > 0).any() else 0
+    last = int(max(i for i in range(len(names)) if ends[i] > 0))
+    return {"step_us": round((ends[last] - t0) / 1e3, 3), "last_stage": names[last], "per_kind_us": out}
+
+
+def profile_trace(context: int):
+    """Traces one generated step of the benchmark session (dataflow
+    kernel) at about `context` positions and prints the per-stage
+    breakdown (trace_summary) as JSON."""
+    os.environ.setdefault("DEFER_B200_LOOP", "flow")
+    import numpy as np
+    import defer_b200 as D
+    from defer_b200 import synthetic
+    m = D.Model.load(synthetic.model_path(MODEL, model_dir(), 0))
+    s = D.Session(m, D.seed_from_u64(1), TEMPERATURE)
+    s.prompt([int(t) for t in np.random.default_rng(1).integers(0, m.config.vocab_size, context)])
+    s.generate(8)  # warm-up launch
+    m.timing(reset=True)
+    m.trace_next_run(16)
+    s.generate(32)
+    tm = m.timing(reset=True)
+    res = trace_summary(m.trace(), m.config.num_layers)
+    res.update({"profile": "trace", "context": context + 8 + 16, "launch_us_per_token": 1e3 * tm["device_ms"] / 32})
+    print(json.dumps(res), flush=True)
     return 0
 
 

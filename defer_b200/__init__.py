@@ -204,6 +204,27 @@ class Model:
         return {"device_ms": ms.value, "runs": r.value, "launches": l.value, "tokens": t.value,
                 "hbm_bytes": b.value}
 
+    def trace_next_run(self, step: int):
+        """Instrumentation: the next dataflow token-loop run records a
+        per-stage time trace of its step `step` (see trace())."""
+        _check(_L().defer_debug_trace_arm(self._h, int(step)))
+
+    def trace(self) -> np.ndarray:
+        """The last trace as uint64 [ctas, stages, 10] globaltimer ns: slot 0
+        stage entry, 1 inputs received, 2 + w warp w done (0 = not reached)."""
+        n = ctypes.c_size_t(0)
+        c, st = ctypes.c_int32(0), ctypes.c_int32(0)
+        _check(_L().defer_debug_trace_read(self._h, None, 0, ctypes.byref(n), ctypes.byref(c), ctypes.byref(st)))
+        out = np.zeros(max(n.value, 1), np.uint64)
+        _check(_L().defer_debug_trace_read(self._h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), out.size,
+                                           ctypes.byref(n), ctypes.byref(c), ctypes.byref(st)))
+        return out[:n.value].reshape(c.value, st.value, -1) if n.value else out[:0]
+
+    def stall_next_run(self, wait_us: int = 1000):
+        """Fault drill: the next token-loop run withholds one hand-off with
+        its bounded waits cut to wait_us, and raises DeviceTimeoutError."""
+        _check(_L().defer_debug_stall(self._h, int(wait_us)))
+
 
 class KvCache:
     """KvCache (src/model.rs:184-243) in HBM."""

@@ -103,6 +103,9 @@ SIGNATURES = [
     ("defer_model_timing", ctypes.c_int, [vp, c_f64p, ctypes.POINTER(ctypes.c_uint64),
                                           ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), c_f64p,
                                           ctypes.c_int]),
+    ("defer_debug_trace_arm", ctypes.c_int, [vp, ctypes.c_int32]),
+    ("defer_debug_trace_read", ctypes.c_int, [vp, ctypes.POINTER(ctypes.c_uint64), sz, c_szp, c_i32p, c_i32p]),
+    ("defer_debug_stall", ctypes.c_int, [vp, ctypes.c_uint32]),
     ("defer_log_softmax_at", ctypes.c_double, [c_f32p, sz, sz]),
 ]
 

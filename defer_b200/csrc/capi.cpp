@@ -573,6 +573,38 @@ int defer_model_timing(defer_model* m, double* device_ms, uint64_t* runs, uint64
   });
 }
 
+int defer_debug_trace_arm(defer_model* m, int32_t step) {
+  return guard([&] {
+    need(m, "model");
+    m->m->dbg_trace_step = step < 0 ? -1 : step;
+    m->m->dbg_trace.clear();
+  });
+}
+
+int defer_debug_trace_read(const defer_model* m, uint64_t* out, size_t cap, size_t* n, int32_t* ctas,
+                           int32_t* stages) {
+  return guard([&] {
+    need(m, "model");
+    const defer::Model& M = *m->m;
+    if (n) *n = M.dbg_trace.size();
+    if (ctas) *ctas = M.dbg_trace_ctas;
+    if (stages) *stages = M.dbg_trace_stages;
+    if (out) {
+      if (cap < M.dbg_trace.size()) defer::fail(defer::kInvalidArgument, "trace buffer too small");
+      std::copy(M.dbg_trace.begin(), M.dbg_trace.end(), out);
+    }
+  });
+}
+
+int defer_debug_stall(defer_model* m, uint32_t wait_us) {
+  return guard([&] {
+    need(m, "model");
+    if (wait_us == 0 || wait_us > 10000000u) defer::fail(defer::kInvalidArgument, "wait_us must be in 1..10^7");
+    m->m->dbg_stall = 1;
+    m->m->dbg_wait_ns = (unsigned long long)wait_us * 1000ull;
+  });
+}
+
 double defer_log_softmax_at(const float* logits, size_t n, size_t idx) {
   return defer::log_softmax_at(logits, n, idx);
 }

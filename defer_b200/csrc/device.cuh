@@ -138,6 +138,15 @@ struct DBatch {
                           // their weight rows into what their inputs leave free)
   int parts;              // wide projections: CTA partitions, each owning every
                           // parts-th slot group and all rows of the matrix
+  // Instrumentation and fault drills; all zero in normal runs.
+  unsigned long long* trace;  // [ncta][stages][kTraceSlots] globaltimer stamps of step
+  int trace_step;             //   trace_step (dataflow kernel), or null
+  int stall;                  // 1: CTA 0 withholds its first hand-off of step 0
+  unsigned long long wait_ns; // limit of every bounded wait (0: the kernel's default)
 };
+
+// Trace record of one stage of one CTA (dataflow kernel): slot 0 = stage
+// entry, 1 = inputs received (after the poll), 2 + w = warp w done.
+constexpr int kTraceSlots = 10;
 
 }  // namespace defer

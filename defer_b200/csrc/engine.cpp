@@ -149,7 +149,7 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   DEFER_CUDA(cudaMemsetAsync(d_ctrl_, 0, 8 * sizeof(int), st));
   DEFER_CUDA(cudaMemsetAsync(tickets_, 0, (size_t)n * m_->dm.NKV * sizeof(int), st));
 
-  DBatch bt;
+  DBatch bt{};
   bt.B = n;
   bt.sess = d_sess_;
   bt.st = d_state_;
@@ -175,6 +175,12 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   bt.bar = reinterpret_cast<unsigned*>(d_ctrl_ + 3);
   bt.smem_bytes = 0;  // set by the launchers
   bt.parts = 1;
+  bt.trace = nullptr;
+  bt.trace_step = -1;
+  bt.stall = m_->dbg_stall;  // fault drill: one run only
+  bt.wait_ns = m_->dbg_wait_ns;
+  m_->dbg_stall = 0;
+  m_->dbg_wait_ns = 0;
   last_steps_ = nsteps;
   const bool persistent = use_persistent();
   FlowPlan plan;
@@ -195,6 +201,16 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
     fb.epoch = (uint32_t)flow_epoch_;
     flow_epoch_ += need;
   }
+  unsigned long long* d_trace = nullptr;
+  size_t trace_words = 0;
+  if (plan.ok && m_->dbg_trace_step >= 0) {
+    // per-stage trace of one step (instrumentation, armed through the C ABI)
+    trace_words = (size_t)plan.geo.grid * flow_stages_per_step(m_->dm) * kTraceSlots;
+    DEFER_CUDA(cudaMalloc(&d_trace, trace_words * sizeof(uint64_t)));
+    DEFER_CUDA(cudaMemsetAsync(d_trace, 0, trace_words * sizeof(uint64_t), st));
+    bt.trace = d_trace;
+    bt.trace_step = m_->dbg_trace_step;
+  }
   DEFER_CUDA(cudaEventRecord(ev_start_, st));
   if (plan.ok) launch_steps_flow(m_->dm, bt, fb, plan, nsteps, st);
   else if (persistent) launch_steps_persistent(m_->dm, bt, nsteps, m_->sms, st);
@@ -207,6 +223,14 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   DEFER_CUDA(cudaMemcpyAsync(ctrl, d_ctrl_, sizeof(ctrl), cudaMemcpyDeviceToHost, st));
   DEFER_CUDA(cudaMemcpyAsync(hs.data(), d_scratch_, total * 4, cudaMemcpyDeviceToHost, st));
   DEFER_CUDA(cudaStreamSynchronize(st));
+  if (d_trace) {
+    m_->dbg_trace.resize(trace_words);
+    DEFER_CUDA(cudaMemcpy(m_->dbg_trace.data(), d_trace, trace_words * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+    DEFER_CUDA(cudaFree(d_trace));
+    m_->dbg_trace_ctas = plan.geo.grid;
+    m_->dbg_trace_stages = flow_stages_per_step(m_->dm);
+    m_->dbg_trace_step = -1;
+  }
   for (int b = 0; b < n; b++) {
     SlotProgram& p = progs[b];
     const int ngen = (int)p.tokens.size() - p.n_prompt;

@@ -170,6 +170,7 @@ struct FlowShared {
   int pfail;  // the producer gave up (ends the phase threads' ring waits)
   int go, step, sampn;
   uint32_t tok;
+  unsigned long long wait_ns;  // limit of the phase threads' bounded waits
   int act[kMaxGroup], pos[kMaxGroup], samp[kMaxGroup];
   float inv[kMaxGroup], M[kMaxGroup], Z[kMaxGroup];
   float wv[kPW][kMaxGroup];
@@ -217,7 +218,7 @@ __device__ __forceinline__ Seg seg1(const uint64_t* src, float* dst, int n, uint
 // Every phase thread polls its share of the region, kPollBatch words at a
 // time (word f = tid + k * kPT of the batch), until each tag equals
 // `want`, storing the values to shared memory; a word is re-read only while
-// its tag is stale. Bounded: past kWaitNs, or when another CTA has failed,
+// its tag is stale. Bounded: past sh.wait_ns, or when another CTA has failed,
 // the CTA is marked failed (the caller checks after its next barrier). With
 // `acquire`, a fence after the last observation orders this thread's later
 // loads after the writers' release fences.
@@ -263,7 +264,7 @@ __device__ __forceinline__ void poll(const Seg& s, bool acquire, FlowShared& sh,
           ok = false;
           break;
         }
-        if (now_ns() - t0 > kWaitNs) {
+        if (now_ns() - t0 > sh.wait_ns) {
           flag_fail(sh, status, kStTimeout);
           ok = false;
           break;
@@ -296,7 +297,7 @@ __device__ __forceinline__ const unsigned char* ring_wait(Ring& rg, FlowShared& 
           flag_fail(sh, status, kStOk);
           break;
         }
-        if (now_ns() - t0 > kWaitNs) {
+        if (now_ns() - t0 > sh.wait_ns) {
           flag_fail(sh, status, kStTimeout);
           break;
         }
@@ -515,6 +516,22 @@ struct Flow {
   bool has_kv;   // this CTA's QKV rows include K/V rows (it appends to the cache)
 
   __device__ uint32_t tag(int s, int id) const { return fb.epoch + (uint32_t)((s + 1) * KS + id); }
+
+  // Trace stamps of step bt.trace_step (instrumentation; off when bt.trace
+  // is null): stage entry and inputs received by thread 0, done per warp.
+  __device__ void tr_at(int s, int sid, int slot) const {
+    if (bt.trace && s == bt.trace_step && sid < KS)
+      bt.trace[((size_t)cta * KS + sid) * kTraceSlots + slot] = now_ns();
+  }
+  __device__ void tr_entry(int s, int sid) const {
+    if (threadIdx.x == 0) tr_at(s, sid, 0);
+  }
+  __device__ void tr_recv(int s, int sid) const {
+    if (threadIdx.x == 0) tr_at(s, sid, 1);
+  }
+  __device__ void tr_done(int s, int sid) const {
+    if ((threadIdx.x & 31) == 0) tr_at(s, sid, 2 + (threadIdx.x >> 5));
+  }
   __device__ bool fail() const { return failed(sh); }
   __device__ unsigned act_mask() const {
     unsigned mk = 0;
@@ -621,6 +638,10 @@ struct Flow {
   __device__ bool select(int s) {
     const int tid = threadIdx.x;
     const uint32_t tg = tag(s, 0);
+    tr_entry(s, 0);
+    // Fault drill (bt.stall): CTA 0 withholds the step header of step 0, so
+    // every other CTA's first poll runs into its bounded wait.
+    const bool withhold = bt.stall && s == 0 && cta == 0;
     for (int b = cta; b < bt.B; b += ncta) {
       DSlotState* st = sh.st + b;
       const DSession& S = sh.sess[b];
@@ -733,27 +754,31 @@ struct Flow {
         rc = m.rope_cos[(size_t)pos * m.HALF + tid];
         rs = m.rope_sin[(size_t)pos * m.HALF + tid];
       }
+      if (!withhold) {
 #pragma unroll
-      for (int k = 0; k < kNormRegs; k++) {
-        const int i = tid + k * kPT;
-        if (i < m.H) st_f(xrow + i, ev[k], tg);
-      }
-      if (tid < m.HALF) {
-        st_f(xrow + m.H + 2 + tid, rc, tg);
-        st_f(xrow + m.H + 2 + m.HALF + tid, rs, tg);
-      }
-      if (tid == 0) {
-        st_word(xrow + m.H, (uint32_t)pos, tg);
-        st_word(xrow + m.H + 1, (live ? (t & 0x7FFFFFFFu) : 0u) | (sh.sampn ? 0x80000000u : 0u), tg);
+        for (int k = 0; k < kNormRegs; k++) {
+          const int i = tid + k * kPT;
+          if (i < m.H) st_f(xrow + i, ev[k], tg);
+        }
+        if (tid < m.HALF) {
+          st_f(xrow + m.H + 2 + tid, rc, tg);
+          st_f(xrow + m.H + 2 + m.HALF + tid, rs, tg);
+        }
+        if (tid == 0) {
+          st_word(xrow + m.H, (uint32_t)pos, tg);
+          st_word(xrow + m.H + 1, (live ? (t & 0x7FFFFFFFu) : 0u) | (sh.sampn ? 0x80000000u : 0u), tg);
+        }
       }
       csync_();
     }
+    tr_done(s, 0);
     return true;
   }
 
   // --------------------------------------------------------------- QKV
   // Returns false when the run ends (no active slot) or on failure.
   __device__ bool qkv(int s, int l) {
+    tr_entry(s, sid_qkv(l));
     const Slice sl = slice_of(m, ly, nblk, 0, l, cta, ncta, geo.slot_bytes);
     const DLayer& Ly = ly[l];
     if (sl.nrows > 0) load_norm(Ly.attn_norm);
@@ -776,6 +801,7 @@ struct Flow {
       fence_acquire_gpu();  // as acquire_cache (the positions are known below)
       csync_();
       if (fail()) return false;
+      tr_recv(s, sid_qkv(l));
       if (threadIdx.x < G) {
         const int g = threadIdx.x;
         int p = -1, smp = 0;
@@ -809,6 +835,7 @@ struct Flow {
       acquire_cache(l);
       csync_();
       if (fail()) return false;
+      tr_recv(s, sid_qkv(l));
       // own residual rows (the O projection adds to them; read after barriers)
 #pragma unroll
       for (int g = 0; g < G; g++) {
@@ -818,7 +845,10 @@ struct Flow {
       }
       xstride = H;
     }
-    if (sl.nrows == 0) return true;
+    if (sl.nrows == 0) {
+      tr_done(s, sid_qkv(l));
+      return true;
+    }
     const int HD = m.HD, HALF = m.HALF, Gh = m.NH / m.NKV;
     const int qh = m.QD / 2, kh = m.KVD / 2, grp = (Gh + 2) * HD;
     const int qkvd = m.QD + 2 * m.KVD;
@@ -872,6 +902,7 @@ struct Flow {
         }
       }
     });
+    tr_done(s, sid_qkv(l));
     return true;
   }
 
@@ -914,6 +945,7 @@ struct Flow {
   // bit); otherwise the partials of each (slot, query head) are combined, in
   // chunk order, by one CTA placed after the unit CTAs.
   __device__ bool attn(int s, int l) {
+    tr_entry(s, sid_att(l));
     csync_();  // the QKV warps are done with the staging area
     const int Gh = m.NH / m.NKV, HD = m.HD, maxc = bt.max_chunks;
     const int grp = (Gh + 2) * HD;
@@ -979,6 +1011,7 @@ struct Flow {
       }
       csync_();
       if (fail()) return false;
+      if (u == cta) tr_recv(s, sid_att(l));
       // scores; the row of position pos (t == pos, last of the last chunk) is the new k
       for (int idx = tid; idx < Gh * kAttnChunk; idx += kPT) {
         const int h = idx / kAttnChunk, tt = idx - h * kAttnChunk;
@@ -1065,6 +1098,7 @@ struct Flow {
       }
       csync_();
     }
+    tr_done(s, sid_att(l));
     return true;
   }
 
@@ -1074,6 +1108,7 @@ struct Flow {
     // of an appending CTA orders this layer's cache appends before any later
     // tagged word of the CTA; readers acquire them at their next attention
     // stage of this layer.
+    tr_entry(s, sid_o(l));
     if (has_kv) fence_release_gpu();
     const Slice sl = slice_of(m, ly, nblk, 1, l, cta, ncta, geo.slot_bytes);
     if (sl.nrows == 0) return true;
@@ -1081,15 +1116,18 @@ struct Flow {
     do_poll(Seg{fb.at, stage, m.QD, G, m.QD, m.QD, act_mask(), tag(s, sid_att(l))}, false);
     csync_();
     if (fail()) return false;
+    tr_recv(s, sid_o(l));
     const uint32_t tg = tag(s, sid_o(l));
     gemv<false>(sl, stage, m.QD, m.QD, [&](int row, const float* a0, bool has1, const float* a1) {
       resid(row, a0, tg);
       if (has1) resid(row + 1, a1, tg);
     });
+    tr_done(s, sid_o(l));
     return true;
   }
 
   __device__ bool gateup(int s, int l) {
+    tr_entry(s, sid_gu(l));
     const Slice sl = slice_of(m, ly, nblk, 2, l, cta, ncta, geo.slot_bytes);
     if (sl.nrows == 0) return true;
     load_norm(ly[l].ffn_norm);
@@ -1098,6 +1136,7 @@ struct Flow {
     norm_ready();
     csync_();
     if (fail()) return false;
+    tr_recv(s, sid_gu(l));
     const uint32_t tg = tag(s, sid_gu(l));
     const bool gelu = m.gelu != 0;
     gemv<true>(sl, stage, m.H, m.H, [&](int row, const float* a0, bool, const float* a1) {
@@ -1118,21 +1157,25 @@ struct Flow {
         st_f(fb.gt + (size_t)g * m.FF + j, __fmul_rn(act, up), tg);
       }
     });
+    tr_done(s, sid_gu(l));
     return true;
   }
 
   __device__ bool down(int s, int l) {
+    tr_entry(s, sid_dn(l));
     const Slice sl = slice_of(m, ly, nblk, 3, l, cta, ncta, geo.slot_bytes);
     if (sl.nrows == 0) return true;
     csync_();
     do_poll(Seg{fb.gt, stage, m.FF, G, m.FF, m.FF, act_mask(), tag(s, sid_gu(l))}, false);
     csync_();
     if (fail()) return false;
+    tr_recv(s, sid_dn(l));
     const uint32_t tg = tag(s, sid_dn(l));
     gemv<false>(sl, stage, m.FF, m.FF, [&](int row, const float* a0, bool has1, const float* a1) {
       resid(row, a0, tg);
       if (has1) resid(row + 1, a1, tg);
     });
+    tr_done(s, sid_dn(l));
     return true;
   }
 
@@ -1194,6 +1237,7 @@ struct Flow {
   }
 
   __device__ bool head(int s) {
+    tr_entry(s, sid_head(m.L));
     const Slice sl = slice_of(m, ly, nblk, 4, 0, cta, ncta, geo.slot_bytes);
     load_norm(m.norm);
     const unsigned act = act_mask();
@@ -1202,6 +1246,7 @@ struct Flow {
     norm_ready();
     csync_();
     if (fail()) return false;
+    tr_recv(s, sid_head(m.L));
     gemv<true>(sl, stage, m.H, m.H, [&](int row, const float* a0, bool has1, const float* a1) {
       const int lane = threadIdx.x & 31;
 #pragma unroll
@@ -1212,6 +1257,7 @@ struct Flow {
       }
     });
     emit_stats(act, tag(s, sid_head(m.L)), true);
+    tr_done(s, sid_head(m.L));
     return true;
   }
 
@@ -1237,9 +1283,11 @@ struct Flow {
   __device__ bool sums(int s, unsigned slots) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* cm = stage;  // [G][ncta]
+    tr_entry(s, sid_s1(m.L));
     do_poll(Seg{fb.csm, cm, ncta, G, fb.cta_cap, ncta, slots, tag(s, sid_head(m.L))}, false);
     csync_();
     if (fail()) return false;
+    tr_recv(s, sid_s1(m.L));
     if (threadIdx.x < G && ((slots >> threadIdx.x) & 1u)) {
       float M = -INFINITY;
       for (int j = 0; j < ncta; j++) M = fmaxf(M, cm[(size_t)threadIdx.x * ncta + j]);
@@ -1258,14 +1306,17 @@ struct Flow {
         if (lane == 0) st_f(fb.esum + (size_t)g * nblk + k, sum, t1);
       }
     }
+    tr_done(s, sid_s1(m.L));
     float* es = stage;  // [G][nblk], then group sums
     const int ng2 = (nblk + 31) / 32;
     float* g2 = es + (size_t)G * nblk;
     float* g3 = g2 + ng2;
     csync_();
+    tr_entry(s, sid_s2(m.L));
     do_poll(Seg{fb.esum, es, nblk, G, nblk, nblk, slots, t1}, false);
     csync_();
     if (fail()) return false;
+    tr_recv(s, sid_s2(m.L));
 #pragma unroll
     for (int g = 0; g < G; g++) {
       if (!((slots >> g) & 1u)) continue;
@@ -1290,6 +1341,7 @@ struct Flow {
         if (lane == 0) st_f(fb.psum + (size_t)g * nblk + k, sum, t2);
       }
     }
+    tr_done(s, sid_s2(m.L));
     csync_();
     return true;
   }
@@ -1361,6 +1413,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1)
     sh.stop = 0;
     sh.fail = 0;
     sh.pfail = 0;
+    sh.wait_ns = bt.wait_ns ? bt.wait_ns : kWaitNs;
     for (int g = 0; g < kMaxGroup; g++) {
       sh.M[g] = 0.0f;
       sh.Z[g] = 0.0f;  // no sums yet: a select falls back to the greedy path
@@ -1506,6 +1559,8 @@ FlowBufs flow_bufs(const DModel& m, int B, int max_chunks, int sms, uint64_t* w)
   f.epoch = 1;
   return f;
 }
+
+int flow_stages_per_step(const DModel& m) { return stages_per_step(m.L); }
 
 uint64_t flow_tags_per_run(const DModel& m, int nsteps) {
   return (uint64_t)(nsteps + 1) * (uint64_t)stages_per_step(m.L);

@@ -51,6 +51,9 @@ FlowPlan flow_plan(const DModel& m, int B, int max_chunks, int sms);
 // 64-bit words of every tagged buffer for B slots.
 size_t flow_tagged_words(const DModel& m, int B, int max_chunks, int sms);
 
+// Stages of one token step (the trace's second dimension).
+int flow_stages_per_step(const DModel& m);
+
 // Tags one run of nsteps steps consumes.
 uint64_t flow_tags_per_run(const DModel& m, int nsteps);
 

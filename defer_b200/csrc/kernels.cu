@@ -34,15 +34,20 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 // status word and leaves, so a lost CTA can never hang the GPU.
 constexpr unsigned long long kBarrierTimeoutNs = 2000000000ull;
 
-__device__ __forceinline__ void grid_barrier(unsigned* bar, unsigned& target, int* status) {
+// `limit_ns` replaces the limit when non-zero; `withhold` (a fault drill set
+// from the host) makes this CTA skip its arrival, so every CTA's wait runs
+// out.
+__device__ __forceinline__ void grid_barrier(unsigned* bar, unsigned& target, int* status,
+                                             unsigned long long limit_ns = 0, bool withhold = false) {
   __syncthreads();
   if (threadIdx.x == 0) {
     target += gridDim.x;
-    red_release_add(bar, 1u);
+    if (!withhold) red_release_add(bar, 1u);
+    const unsigned long long lim = limit_ns ? limit_ns : kBarrierTimeoutNs;
     const unsigned long long t0 = globaltimer_ns();
     unsigned spins = 0;
     while ((int)(ld_acquire_u32(bar) - target) < 0) {
-      if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kBarrierTimeoutNs) {
+      if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > lim) {
         atomicExch(status, kStTimeout);
         break;
       }
@@ -136,34 +141,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
   unsigned target = 0;
   if (any_first(bt, false)) {  // the first step samples from the previous run's logits
     ph_restat(m, bt, cta, ncta);
-    grid_barrier(bt.bar, target, bt.status);
+    grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
     if (any_first(bt, true)) {
       ph_sample1<true>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       ph_sample2<true>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
     }
   }
   for (int s = 0; s < nsteps; s++) {
     ph_select<BF16>(m, bt, s, cta, ncta, dyn_smem);
-    grid_barrier(bt.bar, target, bt.status);
+    grid_barrier(bt.bar, target, bt.status, bt.wait_ns, bt.stall && s == 0 && cta == 0);
     if (ld_status(bt.status) != kStOk) return;
     if (!ld_status(bt.any_active + (s & 1))) break;
     for (int l = 0; l < m.L; l++) {
       const DLayer& Ly = m.layers[l];
       ph_qkv<BF16, G>(m, bt, l, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       ph_attn_chunks(m, bt, l, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       ph_attn_combine(m, bt, cta, ncta);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       ph_residual_gemv<BF16, G>(m, bt, Ly.wo, m.QD, bt.att, cta, ncta, dyn_smem, smem_floats);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       ph_gateup<BF16, G>(m, bt, l, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       if (l + 1 < m.L) prefetch_rows(m.layers[l + 1].wqkv, m.QKVR, m.H, BF16, m.QKVR / 2, 2, cta, ncta);
       ph_residual_gemv<BF16, G>(m, bt, Ly.wdown, m.FF, bt.g, cta, ncta, dyn_smem, smem_floats);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       if (ld_status(bt.status) != kStOk) return;
     }
     ph_head<BF16, G>(m, bt, cta, ncta, dyn_smem);
@@ -171,12 +176,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
     // step's SELECT may already be changing the slot state this reads, and
     // every CTA must take the same number of barriers.
     const bool sampling = any_sampling(bt);
-    grid_barrier(bt.bar, target, bt.status);
+    grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
     if (sampling) {
       ph_sample1<false>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
       ph_sample2<false>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status);
+      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
     }
     if (ld_status(bt.status) != kStOk) return;
   }
@@ -353,6 +358,19 @@ static void persistent_impl(const DModel& m, const DBatch& bt, int nsteps, int s
   unsigned sfl = (unsigned)sf;
   void* args[] = {&mm, &bb, &ns, &sfl};
   DEFER_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(kThreads), args, smem, st));
+}
+
+template <bool BF16, int G>
+static void preload_impl() {
+  cudaFuncAttributes fa;
+  DEFER_CUDA(cudaFuncGetAttributes(&fa, k_persistent<BF16, G>));
+}
+
+void persistent_preload(const DModel& m, int B) {
+  const int G = group_for(m, B);
+  if (G != 1) fail(kInvalidArgument, "persistent_preload covers single-slot batches");
+  if (m.bf16) preload_impl<true, 1>();
+  else preload_impl<false, 1>();
 }
 
 void launch_steps_persistent(const DModel& m, const DBatch& bt, int nsteps, int sms, cudaStream_t st) {

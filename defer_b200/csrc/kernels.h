@@ -18,6 +18,10 @@ int launches_per_step_phased(const DModel& m);
 // All phases of up to `nsteps` steps in one cooperative persistent launch
 // (one CTA per SM, bounded grid barriers between phases).
 void launch_steps_persistent(const DModel& m, const DBatch& bt, int nsteps, int sms, cudaStream_t st);
+// Loads the device code of the persistent kernel that a batch of B slots of
+// model m launches on the current device (CUDA loads modules lazily, and a
+// module load allocates device memory), without launching it.
+void persistent_preload(const DModel& m, int B);
 
 // The device sampler (argmax / temperature + CDF) on one logits vector.
 void launch_sample_one(const float* logits, int V, float T, uint32_t word, uint32_t* out_tok, float* out_margin,

@@ -48,6 +48,13 @@ struct Model {
   mutable double t_device_ms = 0.0;
   mutable uint64_t t_runs = 0, t_launches = 0, t_tokens = 0;
   mutable double t_bytes = 0.0;
+  // Instrumentation and fault drills armed through the C ABI, each consumed
+  // by the next token-loop run on this model.
+  mutable int dbg_trace_step = -1;              // trace this step of the next dataflow run
+  mutable std::vector<uint64_t> dbg_trace;      // last trace: [ctas][stages][kTraceSlots]
+  mutable int dbg_trace_ctas = 0, dbg_trace_stages = 0;
+  mutable int dbg_stall = 0;                    // withhold CTA 0's first hand-off
+  mutable unsigned long long dbg_wait_ns = 0;   // bounded-wait limit of that run
   ~Model();
 };
 

@@ -52,16 +52,22 @@ namespace {
 std::mutex g_addr_mu;
 void* g_addr[64] = {nullptr};
 
-// Device address of the scratch on `device` (the current device). Resolved
-// once per device; host code must never hand the array's own name to a
-// kernel (in host code it is only a host-side stand-in).
-void* scratch_address(int device) {
+// Set-up of `device` (the current device) on its first call: the device
+// address of the scratch, looked up once (host code must never hand the
+// array's own name to a kernel: in host code it is only a host-side
+// stand-in), and the device code of this step loaded. CUDA loads modules
+// lazily and a module load allocates device memory, so doing both here
+// keeps every later call free of allocations.
+void* scratch_address(const DModel& d, int device) {
   std::lock_guard<std::mutex> lk(g_addr_mu);
   if (device < 0 || device >= 64) fail(kInvalidArgument, "device id out of range");
   if (!g_addr[device]) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) fail(kCuda, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    cudaFuncAttributes fa;
+    DEFER_CUDA(cudaFuncGetAttributes(&fa, k_noalloc_init));
+    persistent_preload(d, 1);
     g_addr[device] = p;
   }
   return g_addr[device];
@@ -105,7 +111,7 @@ void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uin
                                std::to_string(kNoAllocScratchBytes) + " bytes");
 
   DEFER_CUDA(cudaSetDevice(m->device));
-  char* base = static_cast<char*>(scratch_address(m->device));
+  char* base = static_cast<char*>(scratch_address(d, m->device));
   int* ctrl = reinterpret_cast<int*>(base + o_ctrl);
   DSlotState* state = reinterpret_cast<DSlotState*>(base + o_state);
   DSession* sess = reinterpret_cast<DSession*>(base + o_sess);
@@ -130,7 +136,7 @@ void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uin
   k_noalloc_init<<<1, 32, 0, st>>>(s, token, sess, state, tok, ctrl, tickets, d.NKV);
   DEFER_CUDA(cudaGetLastError());
 
-  DBatch bt;
+  DBatch bt{};
   bt.B = 1;
   bt.sess = sess;
   bt.st = state;

@@ -80,10 +80,15 @@ DEFER_API int defer_forward(defer_model* m, defer_cache* c, uint32_t token, cons
  * Limits: the step's scratch lives in one 4 MiB array inside this library
  * (held by every GPU that loads it until the process exits); a model/cap
  * whose scratch would exceed it is rejected with InvalidArgument. The first
- * call on a device looks up that array's device address, so make that first
- * call before any stream capture. All calls share the array and each call
- * reinitialises it, so calls must not overlap on the GPU (different
- * streams or threads racing each other corrupt each other's scratch). */
+ * call on a device is its set-up: it looks up that array's device address
+ * and loads this step's device code (CUDA loads code lazily, and loading it
+ * takes device memory), so make that first call before a memory pool
+ * reserves the free HBM and before any stream capture; later calls
+ * allocate nothing. The address is kept for the life of the process: after
+ * a cudaDeviceReset of that device do not call this entry point again.
+ * All calls share the array and each call reinitialises it, so calls must
+ * not overlap on the GPU (different streams or threads racing each other
+ * corrupt each other's scratch). */
 DEFER_API int defer_forward_noalloc(defer_model* m, float* k_cache, float* v_cache, uint32_t cap, uint32_t pos,
                                     uint32_t token, float* logits_out, void* stream);
 
@@ -217,6 +222,24 @@ DEFER_API int defer_ablation(defer_model* m, const uint32_t* context, size_t n, 
  * reading them. */
 DEFER_API int defer_model_timing(defer_model* m, double* device_ms, uint64_t* runs, uint64_t* launches,
                                  uint64_t* tokens, double* hbm_bytes, int reset);
+/* Instrumentation (no counterpart in the reference): arms a per-stage time
+ * trace of step `step` (< 0 disarms) of the next dataflow token-loop run on
+ * this model. For every CTA and stage of that step the kernel records
+ * globaltimer nanoseconds in 10 slots: 0 stage entry, 1 inputs received
+ * (after the poll), 2 + w warp w finished its share. Stages: 0 select, then
+ * per layer l: 1 + 5l QKV, 2 + 5l attention, 3 + 5l O, 4 + 5l gate/up,
+ * 5 + 5l down; then head, sampler sums 1 and 2. */
+DEFER_API int defer_debug_trace_arm(defer_model* m, int32_t step);
+/* The last trace: n = ctas * stages * 10 stamps (0 = not reached). */
+DEFER_API int defer_debug_trace_read(const defer_model* m, uint64_t* out, size_t cap, size_t* n, int32_t* ctas,
+                                     int32_t* stages);
+/* Fault drill (no counterpart in the reference; the test of the device
+ * failure detection): the next token-loop run on this model has CTA 0
+ * withhold its first hand-off of step 0 (the dataflow kernel's step header,
+ * the grid-barrier kernel's first arrival) and limits every bounded wait to
+ * wait_us microseconds, so the run ends with DeviceTimeout (9) and no GPU
+ * fault; later runs are unaffected. */
+DEFER_API int defer_debug_stall(defer_model* m, uint32_t wait_us);
 /* attribution::log_softmax_at (src/attribution.rs:71-85). */
 DEFER_API double defer_log_softmax_at(const float* logits, size_t n, size_t idx);
 
