@@ -1,11 +1,11 @@
 #!/usr/bin/env python
 """Benchmark of the B200 token loop on the reference's headline workload.
 
-Workload: SmolLM2-135M-shape Llama, random-init
-fp32 weights N(0, 0.02) from seed 0; one session per GPU at temperature
-0.7 with ChaCha8 seed 42 (+ rank); a 32-token uniform-random prompt; decode
-to a 2048-token context while appending every token to a WAL on the host;
-then a verified checkout (replay with Divergence checks) of that WAL.
+Workload (config 2): SmolLM2-135M-shape Llama, random-init fp32 weights
+N(0, 0.02) from seed 0; one session per GPU at temperature 0.7 with ChaCha8
+seed 42 (+ rank); a 32-token uniform-random prompt; decode to a 2048-token
+context while appending every token to a WAL on the host; then a verified
+checkout (replay with Divergence checks) of that WAL.
 
 One step = that whole session loop: 32 prompt + 2016 generated + 2048
 replayed = 4096 single-token forward passes (each with its sampler step).
@@ -16,12 +16,18 @@ replayed = 4096 single-token forward passes (each with its sampler step).
   e2e   : the same tokens per wall-clock second through the public API with
           host buffers (prompt / WAL / checkpoint bytes in, tokens out),
           including every host<->device copy and the WAL file writes.
-  batched_replay : BASELINE configs[2] (512 sessions, prompts 16-256 tokens,
-          seeds 0..511, T=0.8, 512 generated tokens each) on the same ranks:
-          each rank generates the checkpoints of its contiguous token-balanced
+  config1 : 5-token prompt, 64 greedy tokens, one session per GPU, with its
+          HBM roofline (the single-session decode target).
+  batched_replay : config 3 (512 sessions, prompts 16-256 tokens, seeds
+          0..511, T=0.8, 512 generated tokens each) on the same ranks: each
+          rank generates the checkpoints of its contiguous token-balanced
           block with the batched token loop, then the timed batched verified
-          replay; aggregate tokens / max-over-ranks device time, with the fp32
-          SIMT roofline of the batched projections.
+          replay; aggregate tokens / max-over-ranks device time, with both
+          roofline bounds (HBM bytes, fp32 SIMT flops) and the binding one.
+  ablation : config 4 (1.7B shape, leave-one-out attribution over a
+          128-token context, 127 variants batched).
+  cpu_baseline / --impl reference : the single-threaded CPU oracle of the
+          reference's path on bounded samples of the same workload.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 """
@@ -130,25 +136,55 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ----------------------------------------------------------- CPU baseline
-def _cpu_session_worker(args):
-    """Oracle session (the reference's CPU path restated in C) on one core:
-    32-token prompt, then `gen` sampled tokens; returns (forwards, seconds)."""
-    path, gen, seed, core = args
+# ------------------------------------------------------------ CPU legs
+SAMPLE_FORWARDS = 16  # forwards per CPU sample step
+
+
+def workload_positions(n: int):
+    """Positions of a stratified sample of n forwards of the workload. It
+    feeds positions 0..2047 twice (the generation, then the verified replay),
+    so its position mix is uniform over 0..2047; forward k of the sample
+    runs at the middle of the k-th of n equal position ranges."""
+    return [int((k + 0.5) * CONTEXT / n) for k in range(n)]
+
+
+def _cpu_sample_worker(args):
+    """The oracle (the reference's CPU path restated in C, single-threaded
+    like the reference) on one core: `steps` timed sample steps after `warm`
+    untimed ones, each SAMPLE_FORWARDS forwards at workload_positions (the
+    cache length is set per forward: the CPU cost of a forward at position p
+    does not depend on the cached values), each followed by the sampler
+    (T = 0.7) where the workload samples from those logits. Returns
+    (forwards, seconds)."""
+    path, steps, warm, seed, core = args
     if core is not None:
         try:
             os.sched_setaffinity(0, {core})
         except OSError:
             pass
     sys.path.insert(0, ROOT)
+    import numpy as np
     from oracle import oracle as O
     m = O.Model.load(path)
-    prompt = prompt_tokens(m.config.vocab_size)
+    rng = np.random.default_rng(seed)
+    toks = [int(t) for t in rng.integers(0, m.config.vocab_size, SAMPLE_FORWARDS)]
+    words = [int(w) for w in rng.integers(0, 2 ** 32, SAMPLE_FORWARDS, dtype=np.uint64)]
+    c = m.new_cache(CONTEXT + 1)
+    pos = workload_positions(SAMPLE_FORWARDS)
+
+    def one_step():
+        for k, p in enumerate(pos):
+            c.set_len(p)
+            lo = m.forward(toks[k], c)
+            if PROMPT_LEN - 1 <= p < CONTEXT - 1:  # these logits are sampled (generation and replay)
+                O.sample_token_word(lo, TEMPERATURE, words[k])
+
+    for _ in range(warm):
+        one_step()
     t0 = time.perf_counter()
-    s = O.Session(m, O.seed_from_u64(seed), TEMPERATURE, cache_cap=PROMPT_LEN + gen + 1)
-    s.prompt(prompt)
-    s.generate(gen)
-    return PROMPT_LEN + gen, time.perf_counter() - t0
+    for _ in range(steps):
+        one_step()
+    return steps * SAMPLE_FORWARDS, time.perf_counter() - t0
 
 
 def cpu_model_name():
@@ -161,44 +197,55 @@ def cpu_model_name():
     return "unknown"
 
 
-def cpu_baseline(path: str, gen: int, workers: int):
+def cpu_sample(path: str, steps: int, warm: int, sessions: int):
+    """`sessions` independent single-threaded oracle sessions, one per core
+    (spawned processes); returns (forwards per second, cores, forwards,
+    seconds)."""
     ctx = mp.get_context("spawn")
-    cores = sorted(os.sched_getaffinity(0))[:workers]
+    cores = sorted(os.sched_getaffinity(0))[:max(1, sessions)]
     with ctx.Pool(len(cores)) as pool:
-        res = pool.map(_cpu_session_worker, [(path, gen, SEED + i, c) for i, c in enumerate(cores)])
-    toks = sum(r[0] for r in res)
+        res = pool.map(_cpu_sample_worker, [(path, steps, warm, SEED + i, c) for i, c in enumerate(cores)])
+    fw = sum(r[0] for r in res)
     secs = max(r[1] for r in res)
-    return toks / secs, len(cores), toks, secs
+    return fw / secs, len(cores), fw, secs
+
+
+def cpu_sample_text(steps: int, sessions: int) -> str:
+    return (f"{sessions} session(s), one single-threaded oracle process pinned per core (the reference is "
+            f"single-threaded); per step {SAMPLE_FORWARDS} forwards at positions stratified over 0..{CONTEXT - 1} "
+            f"(the workload's position mix: generation and replay each feed 0..{CONTEXT - 1}), each followed by "
+            f"the T=0.7 sampler where the workload samples; {steps} timed step(s); the workload's mean cost per "
+            f"forward is extrapolated from the sample; CPU: {cpu_model_name()}")
+
+
+def bench_config(world: int) -> dict:
+    """The workload description both arms print (the same dict)."""
+    return {"workload": WORKLOAD, "tokens_per_step_per_gpu": 2 * CONTEXT,
+            "l2": "weights 538 MB per token > 126 MB L2: inputs larger than L2, no flush",
+            "parallelism": f"{world} independent session(s), one per GPU, no collective"}
+
+
+METRIC = "decode tok/s (single-session token loop)"
 
 
 # ------------------------------------------------------------------- arms
 def run_reference(args):
     """The reference's CPU implementation of the path (the oracle port; the
-    Rust crate cannot be built here) timed on the host cores."""
+    Rust crate cannot be built here) on the host cores: one single-threaded
+    session per GPU of the other arm, each timed on a bounded sample of the
+    config-2 workload per step. Under torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
     from defer_b200 import synthetic
     path = synthetic.model_path(MODEL, model_dir(), 0)
-    workers = min(8, len(os.sched_getaffinity(0)))
-    gen = args.ref_gen
-    for _ in range(args.warmup):
-        cpu_baseline(path, 4, workers)
-    vals, toks, secs = [], 0, 0.0
-    for _ in range(args.steps):
-        v, cores, t, s = cpu_baseline(path, gen, workers)
-        vals.append(v)
-        toks += t
-        secs += s
-    value = toks / secs
-    sample = (f"per step: {cores} independent oracle sessions (one per core, single-threaded like the reference), "
-              f"each the first {PROMPT_LEN}+{gen} forwards of the workload (prompt + sampled decode); "
-              f"CPU: {cpu_model_name()}")
-    line = {"impl": "reference", "metric": "decode tok/s (single-session token loop)", "value": value,
-            "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * secs / max(args.steps, 1), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": value / 17.0, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "cpu_sample": sample},
+    value, cores, fw, secs = cpu_sample(path, args.steps, args.warmup, world)
+    sample = cpu_sample_text(args.steps, world)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * secs / max(args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": value / world / 17.0, "dtype": "fp32",
+            "data": "synthetic", "config": bench_config(world),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -224,6 +271,50 @@ def session_step(D, m, prompt, seed_bytes, wal_path):
     h2d = 4 * (len(prompt) + 2 * gen + CONTEXT + gen)
     d2h = 4 * (len(prompt) + 2 * gen + CONTEXT + 2 * gen)
     return tokens, h2d, d2h
+
+
+# ------------------------------------------------ single-session greedy (config 1)
+CONFIG1_WORKLOAD = ("config1: the same 135M-shape model; 5-token uniform-random prompt (seed 1), greedy decode of "
+                    "64 tokens, one session per GPU (dataflow token-loop kernel)")
+
+
+def config1_measure(D, m, reps, world, max_over_ranks, sum_over_ranks):
+    """Config 1 on every rank: `reps` timed sessions after 2 untimed ones.
+    value = tokens fed (5 + 64 per session) per second of device time; the
+    roofline is the algorithmic bytes of those steps (weights once per token
+    plus the KV read and written) over the same time."""
+    import numpy as np
+    prompt = [int(t) for t in np.random.default_rng(1).integers(0, m.config.vocab_size, 5)]
+
+    def one():
+        s = D.Session(m, D.seed_from_u64(0), 0.0)
+        s.prompt(prompt)
+        out = s.generate(64)
+        assert len(out) == 64
+        return out
+
+    ref = one()
+    one()
+    m.timing(reset=True)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        assert one() == ref  # bit-reproducible run to run
+    wall = time.perf_counter() - t0
+    tm = m.timing(reset=True)
+    dev_s = max_over_ranks(tm["device_ms"] / 1e3)
+    tokens = sum_over_ranks(tm["tokens"])
+    peak, peak_kind = peaks()
+    achieved = sum_over_ranks(tm["hbm_bytes"]) / dev_s / 1e9
+    return {"metric": "decode tok/s (config 1, single-session greedy)", "value": tokens / dev_s, "unit": "tok/s",
+            "us_per_token": 1e6 * dev_s / (69 * reps),
+            "sessions": reps, "tokens": int(tokens), "device_s": dev_s,
+            "config": {"workload": CONFIG1_WORKLOAD},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / world / peak,
+                         "peak_kind": peak_kind, "target_frac": 0.70,
+                         "kernel": "k_flow (dataflow token loop: one launch for the prompt, one for the 64 tokens)"},
+            "e2e": {"value": tokens / max_over_ranks(wall), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * (5 + 64), "d2h_bytes_per_step": 4 * 2 * 64}}
 
 
 # -------------------------------------------------- batched replay (config 3)
@@ -264,7 +355,8 @@ def batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barr
     res, ms = D.replay_batch(m, cks, batch=batch) if cks else ([], 0.0)
     wall = time.perf_counter() - t0
     barrier()
-    launches = m.timing(reset=True)["launches"]
+    tmr = m.timing(reset=True)
+    launches = tmr["launches"]
     failures = sum(1 for r in res if r.status != 0)
     dev_s = max_over_ranks(ms / 1e3)
     wall_s = max_over_ranks(wall)
@@ -275,9 +367,25 @@ def batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barr
     c = m.config
     H, FF, QD, KVD = c.hidden_size, c.intermediate_size, c.q_dim, c.kv_dim
     mac = c.num_layers * (H * (QD + 2 * KVD) + QD * H + 3 * FF * H) + c.vocab_size * H  # projections + head
-    flops_tok = 2.0 * mac  # attention (O(pos)) not counted
+    # attention at position p: scores and the weighted value sum, 2 * 2 * L * NH * HD * (p + 1) flops
+    att = sum(len(ck.history_tokens) * (len(ck.history_tokens) + 1) // 2 for ck in cks)
+    flops = 2.0 * mac * tokens + 4.0 * c.num_layers * c.num_heads * c.head_dim * att
+    all_flops = sum_over_ranks(flops)
     peak_tf = world * sms * FP32_FMA_PER_SM_CLK * 2 * clk_mhz * 1e6 / 1e12
-    achieved_tf = value * flops_tok / 1e12
+    achieved_tf = all_flops / dev_s / 1e12
+    # HBM: weights once per batched step plus every slot's KV read and written (the engine's algorithmic bytes)
+    hbm_peak, hbm_kind = peaks()
+    achieved_gbs = sum_over_ranks(tmr["hbm_bytes"]) / dev_s / 1e9
+    simt = {"bound": "fp32 simt", "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
+            "frac": achieved_tf / peak_tf, "peak_kind": f"nominal: {sms} SMs x {FP32_FMA_PER_SM_CLK} fp32 FMA/clk "
+                                                        f"x 2 x {clk_mhz:.0f} MHz per GPU",
+            "flops": all_flops, "note": "projections, lm_head and attention; the batched GEMMs keep the "
+                                        "reference's fp32 arithmetic"}
+    hbm = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak * world, "unit": "GB/s",
+           "frac": achieved_gbs / (hbm_peak * world), "peak_kind": hbm_kind,
+           "bytes": sum_over_ranks(tmr["hbm_bytes"]), "note": "weights once per batched step plus the KV read "
+                                                                "and written by every slot"}
+    binding = simt if simt["frac"] >= hbm["frac"] else hbm
     # host->device: the checkpoint bytes; device->host: status, step, token per session
     h2d = sum(len(c.to_bytes()) for c in cks)
     d2h = 12 * len(cks)
@@ -285,14 +393,10 @@ def batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barr
             "n_gpus": world, "scaling": "strong", "sessions": n, "tokens": int(all_tokens),
             "divergences": int(all_fail),
             "batch_per_gpu": batch, "device_s": dev_s, "generate_tok_s": all_tokens / gen_s,
-            "gpu_launches": launches,
+            "gpu_launches": launches, "rank_tokens": tokens, "rank_device_s": ms / 1e3,
             "config": {"workload": REPLAY_WORKLOAD.format(n=n, n1=n - 1, gen=gen),
                        "parallelism": f"{world} GPU(s), contiguous token-balanced session blocks"},
-            "roofline": {"bound": "fp32 simt (batched GEMMs keep the reference's fp32 arithmetic)",
-                         "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved_tf / peak_tf,
-                         "peak_kind": f"nominal: {sms} SMs x {FP32_FMA_PER_SM_CLK} fp32 FMA/clk x 2 x "
-                                      f"{clk_mhz:.0f} MHz per GPU",
-                         "flops_per_token": flops_tok, "sm_count": sms},
+            "roofline": dict(binding, other=hbm if binding is simt else simt),
             "e2e": {"value": all_tokens / wall_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h}}
 
@@ -384,11 +488,9 @@ def run_b200(args):
     # CPU baseline first (spawned pool, before this process touches the GPU)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        v, cores, toks, secs = cpu_baseline(path, args.cpu_gen, 1)
+        v, cores, fw, secs = cpu_sample(path, args.cpu_steps, 1, 1)
         cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
-               "sample": f"{toks} forwards of the workload's first steps ({PROMPT_LEN}-token prompt + "
-                         f"{args.cpu_gen} sampled tokens) by the single-threaded oracle port pinned to one core, "
-                         f"{secs:.1f} s; CPU: {cpu_model_name()}"}
+               "sample": cpu_sample_text(args.cpu_steps, 1) + f" ({fw} forwards in {secs:.1f} s)"}
 
     m = D.Model.load(path, device=local)
     prompt = prompt_tokens(m.config.vocab_size)
@@ -412,6 +514,8 @@ def run_b200(args):
         barrier()
     tm = m.timing(reset=True)
     clocks = clk.summary()
+    c1 = config1_measure(D, m, args.config1_reps, world, max_over_ranks, sum_over_ranks)
+    m.timing(reset=True)
     os.environ.pop("DEFER_B200_LOOP", None)  # wide batches below take the grid-barrier token loop
     replay = None
     if args.replay_sessions > 0:
@@ -421,7 +525,7 @@ def run_b200(args):
         replay = batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barrier, sms, clk_mhz)
         m.timing(reset=True)
     ablation = None
-    if args.ablation:
+    if not args.no_ablation:
         import torch
         sms = torch.cuda.get_device_properties(local).multi_processor_count
         clk_mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
@@ -446,14 +550,13 @@ def run_b200(args):
                 "traffic": (tpt * tokens / runs) if tpt else None,
                 "launch_ms": tm["device_ms"] / runs}
     if rank == 0:
-        line = {"metric": "decode tok/s (single-session token loop)", "value": value, "unit": "tok/s",
+        assert tokens == 2 * CONTEXT * args.steps
+        line = {"metric": METRIC, "value": value, "unit": "tok/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": 1000.0 * dev_s / args.steps, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": value / world / 17.0, "dtype": "fp32", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "tokens_per_step_per_gpu": tokens // max(args.steps, 1),
-                           "l2": "weights 538 MB per token > 126 MB L2: inputs larger than L2, no flush",
-                           "parallelism": f"{world} independent sessions (one per GPU), no collective"},
-                "roofline": roofline, "cpu_baseline": cpu,
+                "config": bench_config(world),
+                "roofline": roofline, "cpu_baseline": cpu, "config1": c1,
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d // max(args.steps, 1),
                         "d2h_bytes_per_step": d2h // max(args.steps, 1)},
                 "gpu_launches": tm["launches"], "clocks": clocks, "batched_replay": replay,
@@ -471,15 +574,16 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-gen", type=int, default=150, help="sampled tokens of the CPU baseline sample")
-    ap.add_argument("--ref-gen", type=int, default=48, help="sampled tokens per reference-arm step")
+    ap.add_argument("--cpu-steps", type=int, default=8,
+                    help=f"sample steps ({SAMPLE_FORWARDS} forwards each) of the CPU baseline")
+    ap.add_argument("--config1-reps", type=int, default=10, help="timed repetitions of config 1")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--replay-sessions", type=int, default=512,
                     help="sessions of the batched replay measurement (config 3); 0 skips it")
     ap.add_argument("--replay-gen", type=int, default=512, help="generated tokens per replay session")
     ap.add_argument("--replay-batch", type=int, default=512, help="slots per GPU of the batched replay")
-    ap.add_argument("--ablation", action="store_true",
-                    help="also measure config 4 (1.7B-shape leave-one-out attribution, 127 variants)")
+    ap.add_argument("--no-ablation", action="store_true",
+                    help="skip config 4 (1.7B-shape leave-one-out attribution, 127 variants)")
     ap.add_argument("--profile-case", nargs="?", const="single", choices=["single", "batched"],
                     help="no measurement: a small case for profiles. single: the 135M model, 16-token "
                          "prompt, then one launch of 32 sampled tokens (dataflow kernel). batched: "
@@ -490,11 +594,12 @@ def main(argv=None):
     ap.add_argument("--trace", action="store_true",
                     help="no measurement: per-stage critical-path breakdown of the dataflow kernel from "
                          "globaltimer stamps of one traced step (--profile-prompt tokens of context)")
+    ap.add_argument("--trace-out", default=None, help="with --trace: also save the raw stamps (.npy)")
     a = ap.parse_args(argv)
     if a.impl == "reference":
         return run_reference(a)
     if a.trace:
-        return profile_trace(a.profile_prompt)
+        return profile_trace(a.profile_prompt, a.trace_out)
     if a.profile_case == "batched":
         return profile_case_batched(a.profile_slots, a.profile_prompt)
     if a.profile_case:
@@ -538,7 +643,7 @@ def trace_summary(tr, L: int):
     import numpy as np
     tr = np.asarray(tr, dtype=np.int64)
     names = stage_names(L)
-    done = tr[:, :, 2:].max(axis=2)
+    done = tr[:, :, 2:9].max(axis=2)  # the 7 phase warps
     recv = tr[:, :, 1]
     ends = done.max(axis=0)
     prod = {0: None}
@@ -562,7 +667,12 @@ def trace_summary(tr, L: int):
         cp = (done[part, k] - recv[part, k]) / 1e3
         kind = name.rstrip("0123456789")
         r = rows.setdefault(kind, {"n": 0, "span": [], "handoff_med": [], "handoff_max": [], "compute_med": [],
-                                   "compute_max": [], "tail": [], "ctas": []})
+                                   "compute_max": [], "tail": [], "ctas": [], "mark10": [], "mark11": [],
+                                   "mark12": [], "mark13": []})
+        for mk in (10, 11, 12, 13):  # warp 0's sub-stage marks, from the receipt
+            ok = part & (tr[:, k, mk] > 0)
+            if ok.any():
+                r[f"mark{mk}"].append(float(np.median((tr[ok, k, mk] - recv[ok, k]) / 1e3)))
         r["n"] += 1
         r["span"].append((ends[k] - ends[p]) / 1e3)
         r["handoff_med"].append(float(np.median(ho)))
@@ -574,13 +684,13 @@ def trace_summary(tr, L: int):
     out = {}
     for kind, r in rows.items():
         out[kind] = {"stages": r["n"], **{key: round(float(np.mean(v)), 3) for key, v in r.items()
-                                          if key != "n"}}
+                                          if key != "n" and len(v)}}
     t0 = tr[:, 0, 0][tr[:, 0, 0] > 0].min() if (tr[:, 0, 0] > 0).any() else 0
     last = int(max(i for i in range(len(names)) if ends[i] > 0))
     return {"step_us": round((ends[last] - t0) / 1e3, 3), "last_stage": names[last], "per_kind_us": out}
 
 
-def profile_trace(context: int):
+def profile_trace(context: int, out: str = None):
     """Traces one generated step of the benchmark session (dataflow
     kernel) at about `context` positions and prints the per-stage
     breakdown (trace_summary) as JSON."""
@@ -596,7 +706,10 @@ def profile_trace(context: int):
     m.trace_next_run(16)
     s.generate(32)
     tm = m.timing(reset=True)
-    res = trace_summary(m.trace(), m.config.num_layers)
+    tr = m.trace()
+    if out:
+        np.save(out, tr)
+    res = trace_summary(tr, m.config.num_layers)
     res.update({"profile": "trace", "context": context + 8 + 16, "launch_us_per_token": 1e3 * tm["device_ms"] / 32})
     print(json.dumps(res), flush=True)
     return 0

@@ -94,6 +94,11 @@ struct DSession {
   int n_prompt, n_total;
   float temperature;
   int verify;             // 1: replay/checkout, 0: generate
+  // Position-parallel replay (verify mode): `lanes` slots share one cache
+  // and program; the slot whose first step index is j feeds the indices
+  // j, j + lanes, j + 2 lanes, ..., and from the logits of index i it
+  // verifies the token of index i + 1 in its next step. 1 otherwise.
+  int lanes;
 };
 
 // Mutable per-slot state written by the kernels.
@@ -146,7 +151,10 @@ struct DBatch {
 };
 
 // Trace record of one stage of one CTA (dataflow kernel): slot 0 = stage
-// entry, 1 = inputs received (after the poll), 2 + w = warp w done.
-constexpr int kTraceSlots = 10;
+// entry, 1 = inputs received (after the poll), 2 + w = warp w done; warp 0
+// also marks 10 = RMS statistic ready / attention rows staged, 11 = first
+// weight piece in shared memory / attention scores done, 12 = attention
+// softmax done, 13 = attention weighted sum done.
+constexpr int kTraceSlots = 16;
 
 }  // namespace defer

@@ -23,7 +23,27 @@ int loop_mode() {
   return 1;
 }
 
+int replay_lanes(size_t n) {
+  const char* e = getenv("DEFER_B200_REPLAY_LANES");
+  long lanes = 256;
+  if (e && *e) lanes = strtol(e, nullptr, 10);
+  if (lanes < 1) lanes = 1;
+  // short histories are cheaper one position per step (dataflow kernel)
+  if (n < 64) return 1;
+  return (int)std::min<long>(lanes, (long)n);
+}
+
 static uint64_t words_per_sample(float t) { return t == 0.0f ? 0 : 1; }
+
+// Steps a lane program needs: its feeds, plus one step that only verifies
+// the index after its last feed when that index is still in the program.
+static int lane_steps(int n_total, int lanes, int lane) {
+  if (lanes <= 1) return n_total;
+  if (lane >= n_total) return 0;
+  const int feeds = (n_total - lane + lanes - 1) / lanes;
+  const int last = lane + (feeds - 1) * lanes;
+  return feeds + (last + 1 < n_total ? 1 : 0);
+}
 
 // ------------------------------------------------------------------ Runner
 Runner::Runner(const Model* m, int B, int max_cap) : m_(m), B_(B), max_cap_(max_cap) {
@@ -76,6 +96,12 @@ Runner::~Runner() {
 
 const float* Runner::logits(int b) const { return logits_ + (size_t)b * m_->dm.V; }
 
+void Runner::copy_logits_to(int b, Runner& dst, int db) const {
+  if (dst.m_ != m_) fail(kInvalidArgument, "runners of different models");
+  DEFER_CUDA(cudaMemcpyAsync(dst.logits_ + (size_t)db * m_->dm.V, logits(b), (size_t)m_->dm.V * 4,
+                             cudaMemcpyDeviceToDevice, m_->stream));
+}
+
 void Runner::download_logits(int b, float* out) const {
   DEFER_CUDA(cudaMemcpy(out, logits(b), (size_t)m_->dm.V * 4, cudaMemcpyDeviceToHost));
 }
@@ -89,12 +115,29 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   cudaStream_t st = m_->stream;
   // Pack tokens / words / stop lists / margins into one device scratch.
   std::vector<size_t> o_tok(n), o_words(n), o_stop(n), o_marg(n);
+  std::vector<int> head(n);  // the program holding slot b's tokens / words / margins (its lane 0)
   size_t total = 0;
   int nsteps = 0;
+  bool any_lanes = false;
   for (int b = 0; b < n; b++) {
     SlotProgram& p = progs[b];
     if (!p.cache || p.cache->model != m_) fail(kInvalidArgument, "program without a cache of this model");
     if (p.cache->cap > max_cap_) fail(kInvalidArgument, "cache larger than the runner supports");
+    head[b] = b;
+    if (p.lanes > 1) {
+      any_lanes = true;
+      if (!p.verify || p.masked || p.lane < 0 || p.lane >= p.lanes)
+        fail(kInvalidArgument, "position-parallel lanes are for unmasked verified replays");
+      if (p.lane > 0) {
+        const SlotProgram& h = progs[b - 1];
+        if (h.lanes != p.lanes || h.lane != p.lane - 1 || h.cache != p.cache)
+          fail(kInvalidArgument, "lanes of one replay must be consecutive and share its cache");
+        head[b] = head[b - 1];
+        nsteps = std::max(nsteps, lane_steps((int)progs[head[b]].tokens.size(), p.lanes, p.lane));
+        continue;  // tokens, words and margins live in the lane-0 program
+      }
+      if (p.n_prompt < 1) fail(kInvalidArgument, "a position-parallel replay needs a prompt");
+    }
     const int ngen = (int)p.tokens.size() - p.n_prompt;
     if (ngen < 0) fail(kInvalidArgument, "n_prompt exceeds program length");
     if (p.temperature != 0.0f && (int)p.words.size() < ngen) fail(kInvalidArgument, "missing PRNG words");
@@ -106,7 +149,7 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
     total += p.stop.size();
     o_marg[b] = total;
     total += p.want_margins ? (size_t)ngen : 0;
-    nsteps = std::max(nsteps, (int)p.tokens.size());
+    nsteps = std::max(nsteps, lane_steps((int)p.tokens.size(), p.lanes, p.lane));
   }
   if (total > scratch_words_ || !d_scratch_) {
     if (d_scratch_) cudaFree(d_scratch_);
@@ -117,19 +160,23 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   std::vector<DSession> sess(n);
   std::vector<DSlotState> state(n);
   for (int b = 0; b < n; b++) {
-    SlotProgram& p = progs[b];
+    const int h = head[b];
+    SlotProgram& p = progs[h];  // the program's data (the lane-0 program of a lane group)
+    const int lane = progs[b].lane, lanes = progs[b].lanes;
     const int ngen = (int)p.tokens.size() - p.n_prompt;
-    std::copy(p.tokens.begin(), p.tokens.end(), hs.begin() + o_tok[b]);
-    if (p.temperature != 0.0f) std::copy(p.words.begin(), p.words.begin() + ngen, hs.begin() + o_words[b]);
-    std::copy(p.stop.begin(), p.stop.end(), hs.begin() + o_stop[b]);
+    if (h == b) {
+      std::copy(p.tokens.begin(), p.tokens.end(), hs.begin() + o_tok[b]);
+      if (p.temperature != 0.0f) std::copy(p.words.begin(), p.words.begin() + ngen, hs.begin() + o_words[b]);
+      std::copy(p.stop.begin(), p.stop.end(), hs.begin() + o_stop[b]);
+    }
     DSession& s = sess[b];
     s.kc = p.cache->k;
     s.vc = p.cache->v;
     s.mask = p.masked ? p.cache->mask : nullptr;
-    s.tokens = d_scratch_ + o_tok[b];
-    s.words = d_scratch_ + o_words[b];
-    s.margins = p.want_margins ? reinterpret_cast<float*>(d_scratch_ + o_marg[b]) : nullptr;
-    s.stop = d_scratch_ + o_stop[b];
+    s.tokens = d_scratch_ + o_tok[h];
+    s.words = d_scratch_ + o_words[h];
+    s.margins = p.want_margins ? reinterpret_cast<float*>(d_scratch_ + o_marg[h]) : nullptr;
+    s.stop = d_scratch_ + o_stop[h];
     s.n_stop = (int)p.stop.size();
     s.cap = p.cache->cap;
     s.pos = (int)p.cache->len;
@@ -137,10 +184,12 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
     s.n_total = (int)p.tokens.size();
     s.temperature = p.temperature;
     s.verify = p.verify ? 1 : 0;
+    s.lanes = lanes;
     DSlotState& z = state[b];
     memset(&z, 0, sizeof(z));
-    z.pos = (int)p.cache->len;
-    z.done = p.tokens.empty() ? 1 : 0;
+    z.pos = (int)p.cache->len + lane;
+    z.step = lane;
+    z.done = lane >= (int)p.tokens.size() ? 1 : 0;
     z.div_step = -1;
   }
   DEFER_CUDA(cudaMemcpyAsync(d_scratch_, hs.data(), total * 4, cudaMemcpyHostToDevice, st));
@@ -185,7 +234,10 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   const bool persistent = use_persistent();
   FlowPlan plan;
   const int mode = persistent ? loop_mode() : 0;
-  if (mode && flow_words_) plan = flow_plan(m_->dm, n, max_chunks_, m_->sms);
+  // the dataflow kernel reads a step's cached rows before that step's
+  // appends are known to be visible, so lanes (which read rows other lanes
+  // append in the same step) take the grid-barrier kernel
+  if (mode && flow_words_ && !any_lanes) plan = flow_plan(m_->dm, n, max_chunks_, m_->sms);
   if (mode == 2 && !plan.ok)
     fail(kInvalidArgument, std::string("the dataflow token loop does not apply: ") +
                                (flow_words_ ? plan.why : "batch wider than its slot group"));
@@ -231,20 +283,8 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
     m_->dbg_trace_stages = flow_stages_per_step(m_->dm);
     m_->dbg_trace_step = -1;
   }
-  for (int b = 0; b < n; b++) {
-    SlotProgram& p = progs[b];
-    const int ngen = (int)p.tokens.size() - p.n_prompt;
-    SlotResult& r = results[b];
-    r.steps = state[b].step;
-    r.div_step = state[b].div_step;
-    r.div_token = state[b].div_token;
-    r.tokens.assign(hs.begin() + o_tok[b], hs.begin() + o_tok[b] + p.tokens.size());
-    if (p.want_margins)
-      r.margins.assign(reinterpret_cast<float*>(hs.data() + o_marg[b]),
-                       reinterpret_cast<float*>(hs.data() + o_marg[b]) + ngen);
-    p.cache->len = (size_t)state[b].pos;
-  }
-  // Timing and algorithmic traffic of this run.
+  // Timing and algorithmic traffic of this run: weights once per step run,
+  // and per token fed at position p the KV rows 0..p read and row p written.
   float ms = 0.0f;
   DEFER_CUDA(cudaEventElapsedTime(&ms, ev_start_, ev_stop_));
   const DModel& d = m_->dm;
@@ -253,12 +293,38 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   double bytes = 0.0;
   uint64_t tokens = 0;
   for (int b = 0; b < n; b++) {
-    const int k = results[b].steps;
+    const int h = head[b];
+    SlotProgram& p = progs[h];
+    const int ngen = (int)p.tokens.size() - p.n_prompt;
+    const int lanes = progs[b].lanes, lane = progs[b].lane;
+    SlotResult& r = results[b];
+    r.div_step = state[b].div_step;
+    r.div_token = state[b].div_token;
+    int fed;  // tokens this slot fed
+    if (lanes > 1) {
+      fed = state[b].step > lane ? (state[b].step - lane + lanes - 1) / lanes : 0;
+      fed = std::min(fed, lane < (int)p.tokens.size() ? ((int)p.tokens.size() - lane + lanes - 1) / lanes : 0);
+    } else {
+      fed = state[b].step;
+    }
+    r.steps = fed;
+    if (h == b) {
+      r.tokens.assign(hs.begin() + o_tok[b], hs.begin() + o_tok[b] + p.tokens.size());
+      if (p.want_margins)
+        r.margins.assign(reinterpret_cast<float*>(hs.data() + o_marg[b]),
+                         reinterpret_cast<float*>(hs.data() + o_marg[b]) + ngen);
+    }
     const double p0 = (double)sess[b].pos;
-    steps_run = std::max(steps_run, k);
-    tokens += (uint64_t)k;
-    // step i reads positions 0..p0+i and writes position p0+i
-    bytes += kv_row * ((double)k * (p0 + 1.0) + (double)k * (k - 1) / 2.0 + (double)k);
+    steps_run = std::max(steps_run, fed);
+    tokens += (uint64_t)fed;
+    for (int j = 0; j < fed; j++) bytes += kv_row * (p0 + lane + (double)j * lanes + 2.0);
+    if (lanes > 1) {
+      // the lanes fed interleaved positions of one cache: its length is the
+      // last position fed + 1 over every lane
+      if (fed > 0) p.cache->len = std::max(p.cache->len, (size_t)(p0 + lane + (double)(fed - 1) * lanes + 1));
+    } else {
+      p.cache->len = (size_t)state[b].pos;
+    }
   }
   bytes += (double)steps_run * (double)m_->weight_bytes;
   m_->t_device_ms += ms;
@@ -437,6 +503,24 @@ static SlotProgram replay_program(const Checkpoint& ck, KvCache* cache) {
   return p;
 }
 
+static void free_runner(void* p) { delete static_cast<Runner*>(p); }
+
+// The model's wide runner for position-parallel checkouts (created on first
+// use, regrown when a wider or longer replay needs it).
+static Runner* replay_runner_for(const Model* m, int lanes, int cap) {
+  if (!m->replay_runner || m->replay_runner_B < lanes || m->replay_runner_cap < cap) {
+    const int B = std::max(lanes, m->replay_runner_B);
+    const int c = std::max(cap, m->replay_runner_cap);
+    if (m->replay_runner) m->replay_runner_free(m->replay_runner);
+    m->replay_runner = nullptr;
+    m->replay_runner = new Runner(m, B, c);
+    m->replay_runner_free = free_runner;
+    m->replay_runner_B = B;
+    m->replay_runner_cap = c;
+  }
+  return static_cast<Runner*>(m->replay_runner);
+}
+
 Session* Session::checkout(const Model* m, const Checkpoint& ck, int cache_cap) {
   validate_checkpoint(m, ck);
   std::unique_ptr<Session> s(new Session(m, ck.base_seed, ck.temperature, cache_cap));
@@ -445,10 +529,34 @@ Session* Session::checkout(const Model* m, const Checkpoint& ck, int cache_cap) 
     if (ck.history_tokens[i] >= m->cfg.vocab_size) s->feed_tokens(ck.history_tokens.data(), i + 1);  // raises
   if (n > std::min<size_t>(m->cfg.max_seq_len, s->cache->cap)) s->feed_tokens(ck.history_tokens.data(), n);  // raises
   if (n) {
-    std::vector<SlotProgram> progs(1, replay_program(ck, s->cache));
-    progs[0].want_margins = true;
+    SlotProgram base = replay_program(ck, s->cache);
+    base.want_margins = true;
     std::vector<SlotResult> res;
-    s->runner_->run(progs, res);
+    const int lanes = ck.prompt_len >= 1 ? replay_lanes(n) : 1;
+    if (lanes <= 1) {
+      std::vector<SlotProgram> progs(1, std::move(base));
+      s->runner_->run(progs, res);
+    } else {
+      Runner* wide = replay_runner_for(m, lanes, s->cache->cap);
+      std::vector<SlotProgram> progs(lanes);
+      for (int j = 0; j < lanes; j++) {
+        SlotProgram& p = progs[j];
+        if (j == 0) p = std::move(base);
+        p.cache = s->cache;
+        p.verify = true;
+        p.lanes = lanes;
+        p.lane = j;
+      }
+      wide->run(progs, res);
+      // the first divergence in position order over the lanes
+      for (int j = 1; j < lanes; j++)
+        if (res[j].div_step >= 0 && (res[0].div_step < 0 || res[j].div_step < res[0].div_step)) {
+          res[0].div_step = res[j].div_step;
+          res[0].div_token = res[j].div_token;
+        }
+      // the logits of the last position become the session's
+      wide->copy_logits_to((int)((n - 1) % (size_t)lanes), *s->runner_, 0);
+    }
     s->last_margins = res[0].margins;
     const SlotResult& r = res[0];
     if (r.div_step >= 0)

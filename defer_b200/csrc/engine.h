@@ -25,6 +25,10 @@ struct SlotProgram {
   std::vector<uint32_t> stop;
   bool want_margins = false;
   bool masked = false;  // the cache's mask bitmap applies to this run
+  // Position-parallel replay (verify mode): programs lane = 0..lanes-1 of one
+  // replay are consecutive in the run, share the cache, the tokens and the
+  // words (given in the lane-0 program only) and one margins array.
+  int lanes = 1, lane = 0;
 };
 
 struct SlotResult {
@@ -46,6 +50,8 @@ class Runner {
   void run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& results);
   const float* logits(int b) const;  // device pointer of slot b's logits
   void download_logits(int b, float* out) const;
+  // Slot b's logits into slot db of `dst` (same model), on the model's stream.
+  void copy_logits_to(int b, Runner& dst, int db) const;
   int last_steps() const { return last_steps_; }
 
  private:
@@ -69,6 +75,9 @@ class Runner {
 // Whether runs use a persistent kernel (default) or one launch per phase
 // (DEFER_B200_PHASED=1).
 bool use_persistent();
+// Lanes of a position-parallel checkout of n tokens (1 = one position per
+// step); DEFER_B200_REPLAY_LANES overrides the default.
+int replay_lanes(size_t n);
 // Among the persistent kernels: 1 = the dataflow kernel where it applies,
 // else the grid-barrier kernel (default); 0 = always the grid-barrier
 // kernel (DEFER_B200_LOOP=barrier); 2 = the dataflow kernel or an error
@@ -84,7 +93,11 @@ class Session {
   // engine.rs:121-137. on_token(token, rng_word_pos) -> status (0 = continue)
   std::vector<uint32_t> generate(size_t max_tokens, const std::vector<uint32_t>& stop,
                                  const std::function<int(uint32_t, uint64_t)>& on_token);
-  static Session* checkout(const Model* m, const Checkpoint& ck, int cache_cap);  // engine.rs:241-274
+  // engine.rs:241-274. Long histories are replayed position-parallel: up to
+  // replay_lanes() lanes feed interleaved positions of the one cache, each
+  // verifying the token after the position it fed (same arithmetic per
+  // position, so the same tokens, logits and KV bits as one at a time).
+  static Session* checkout(const Model* m, const Checkpoint& ck, int cache_cap);
   Checkpoint checkpoint() const;                                                   // engine.rs:223-232
   bool has_logits() const { return has_logits_; }
   void last_logits(float* out) const;

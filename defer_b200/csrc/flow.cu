@@ -514,6 +514,7 @@ struct Flow {
   int k0, k1;    // this CTA's logits blocks
   int r0, r1;    // this CTA's residual rows
   bool has_kv;   // this CTA's QKV rows include K/V rows (it appends to the cache)
+  int cur_s = -1, cur_sid = 0;  // the stage being traced (instrumentation)
 
   __device__ uint32_t tag(int s, int id) const { return fb.epoch + (uint32_t)((s + 1) * KS + id); }
 
@@ -523,8 +524,14 @@ struct Flow {
     if (bt.trace && s == bt.trace_step && sid < KS)
       bt.trace[((size_t)cta * KS + sid) * kTraceSlots + slot] = now_ns();
   }
-  __device__ void tr_entry(int s, int sid) const {
+  __device__ void tr_entry(int s, int sid) {
+    cur_s = s;
+    cur_sid = sid;
     if (threadIdx.x == 0) tr_at(s, sid, 0);
+  }
+  // A sub-stage mark of the current stage by warp 0.
+  __device__ void tr_mark(int slot) const {
+    if (threadIdx.x == 0) tr_at(cur_s, cur_sid, slot);
   }
   __device__ void tr_recv(int s, int sid) const {
     if (threadIdx.x == 0) tr_at(s, sid, 1);
@@ -585,6 +592,7 @@ struct Flow {
     float inv[G];
     if (NORM && G == 1) {
       inv[0] = sh.act[0] ? inv_rms(xs, xstride, 0) : 0.0f;  // every warp, no barrier
+      tr_mark(10);
     } else if (NORM) {
       // slot g's statistic once for the CTA, by warp g mod 7 (same rule)
       for (int g = warp; g < G; g += kPW) {
@@ -602,6 +610,7 @@ struct Flow {
     for (int done = 0; done < sl.nrows;) {
       const int n = min(sl.per, sl.nrows - done);
       const unsigned char* base = ring_wait(rg, sh, bt.status);
+      if (done == 0) tr_mark(11);
       for (int pr = warp; NR * pr < n; pr += kPW) {
         const int i0 = NR * pr;
         const void* rows[NR];
@@ -1009,9 +1018,10 @@ struct Flow {
           }
         }
       }
+      if (u == cta) tr_recv(s, sid_att(l));
       csync_();
       if (fail()) return false;
-      if (u == cta) tr_recv(s, sid_att(l));
+      if (u == cta) tr_mark(10);
       // scores; the row of position pos (t == pos, last of the last chunk) is the new k
       for (int idx = tid; idx < Gh * kAttnChunk; idx += kPT) {
         const int h = idx / kAttnChunk, tt = idx - h * kAttnChunk;
@@ -1035,6 +1045,7 @@ struct Flow {
         sc[idx] = sv;
       }
       csync_();
+      if (u == cta) tr_mark(11);
       const bool single = nch == 1;
       uint64_t* part = fb.pt + (((size_t)b * m.NH + (size_t)kvh * Gh) * maxc + c) * (HD + 2);
       const size_t hstride = (size_t)maxc * (HD + 2);
@@ -1056,6 +1067,7 @@ struct Flow {
         }
       }
       csync_();
+      if (u == cta) tr_mark(12);
       const int tv = tn - (tc < tn ? 1 : 0);  // rows taken from vs (the new row, if any, comes last)
       for (int idx = tid; idx < Gh * HD; idx += kPT) {
         const int h = idx / HD, d = idx - h * HD;
@@ -1070,6 +1082,7 @@ struct Flow {
           st_f(part + h * hstride + 2 + d, acc, tp);
       }
       csync_();
+      if (u == cta) tr_mark(13);
     }
     // Combine per (slot, query head), chunks in order.
     for (int bh = 0; bh < bt.B * m.NH; bh++) {

@@ -41,6 +41,10 @@ struct Model {
   void* fwd_runner = nullptr;
   void (*fwd_runner_free)(void*) = nullptr;
   int fwd_runner_cap = 0;
+  // Wide runner of position-parallel checkouts (owned, created on demand).
+  mutable void* replay_runner = nullptr;
+  mutable void (*replay_runner_free)(void*) = nullptr;
+  mutable int replay_runner_B = 0, replay_runner_cap = 0;
   // Accumulated by every token-loop run on this model (see defer_model_timing):
   // device time between events recorded on `stream` around the launch, runs,
   // kernel launches, tokens fed, and algorithmic HBM bytes (weights once per

@@ -132,6 +132,7 @@ void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uin
   s.n_total = 1;
   s.temperature = 0.0f;
   s.verify = 0;
+  s.lanes = 1;
   int* tickets = reinterpret_cast<int*>(base + o_tickets);
   k_noalloc_init<<<1, 32, 0, st>>>(s, token, sess, state, tok, ctrl, tickets, d.NKV);
   DEFER_CUDA(cudaGetLastError());

@@ -813,12 +813,16 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
     // travel through shared memory (never re-read from global memory).
     if (tid == 0) {
       if (st->was_active) {
-        st->pos += 1;
-        st->step += 1;
+        st->pos += S.lanes;
+        st->step += S.lanes;
       }
       st->was_active = 0;
       st->active = 0;
-      if (st->step >= S.n_total) st->done = 1;
+      // a lane of a position-parallel replay still verifies the index after
+      // the last one it fed
+      const int vi = st->step - S.lanes + 1;
+      const bool verify_left = S.lanes > 1 && st->step >= S.lanes && vi < S.n_total;
+      if (st->step >= S.n_total && !verify_left) st->done = 1;
       s_go = !st->done;
       s_step = st->step;
     }
@@ -827,12 +831,12 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
       DEFER_CTA_SYNC();
       continue;
     }
-    const int s = s_step;
-    uint32_t tok;
-    if (s < S.n_prompt) {
-      tok = S.tokens[s];
-    } else {
-      const int k = s - S.n_prompt;
+    const int s = s_step;        // index fed in this step (none when >= n_total)
+    const int vi = s - S.lanes + 1;  // index chosen from this slot's previous logits (= s for one lane)
+    const bool feed = s < S.n_total;
+    uint32_t tok = feed ? S.tokens[s] : 0u;
+    if ((S.lanes == 1 || s >= S.lanes) && vi >= S.n_prompt && vi < S.n_total) {
+      const int k = vi - S.n_prompt;
       const float T = S.temperature;
       const int nb = bt.nblk;
       const float* lmax = bt.ss.lmax + (size_t)b * nb;
@@ -855,13 +859,12 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
         }
       }
       if (S.verify) {
-        tok = S.tokens[s];
-        if (tid == 0 && smp != tok) {
-          st->div_step = s;
+        if (tid == 0 && smp != S.tokens[vi]) {
+          st->div_step = vi;
           st->div_token = smp;
           st->done = 1;
         }
-      } else {
+      } else {  // generate mode has one lane: vi == s
         tok = smp;
         if (tid == 0) S.tokens[s] = smp;
       }
@@ -869,6 +872,7 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
     }
     if (tid == 0) {
       s_tok = 0xFFFFFFFFu;
+      if (!feed) st->done = 1;  // a lane's last verification: nothing to feed
       if (!st->done) {
         if (tok >= (uint32_t)m.V) {
           atomicExch(bt.status, kStBadToken);
@@ -911,8 +915,8 @@ static __device__ void ph_finalize(const DBatch& bt, int cta, int ncta) {
   for (int b = cta; b < bt.B; b += ncta) {
     DSlotState* st = bt.st + b;
     if (st->was_active) {
-      st->pos += 1;
-      st->step += 1;
+      st->pos += bt.sess[b].lanes;
+      st->step += bt.sess[b].lanes;
     }
     st->was_active = 0;
     st->active = 0;

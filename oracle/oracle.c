@@ -431,6 +431,15 @@ OR_EXPORT void or_cache_truncate(or_cache *c, size_t n) {
     if (n < c->len) c->len = n;
 }
 
+/* Timing samples only (bench.py's CPU legs): sets the length to n <= cap
+ * without computing the rows in between, which keep what they hold (zeros
+ * in a new cache). The CPU cost of a forward at position p does not depend
+ * on the cached values, so a forward at any position of a workload can be
+ * timed without first running every position before it. */
+OR_EXPORT void or_cache_set_len(or_cache *c, size_t n) {
+    if (n <= c->cap) c->len = n;
+}
+
 /* KvCache::clone (attribution.rs:254). */
 OR_EXPORT void or_cache_copy(or_cache *dst, const or_cache *src) {
     size_t n = src->len < dst->cap ? src->len : dst->cap;

@@ -102,6 +102,7 @@ def lib():
         L.or_cache_len.argtypes = [vp]
         L.or_cache_len.restype = sz
         L.or_cache_truncate.argtypes = [vp, sz]
+        L.or_cache_set_len.argtypes = [vp, sz]
         L.or_cache_copy.argtypes = [vp, vp]
         L.or_cache_keys.argtypes = [vp, sz]
         L.or_cache_keys.restype = f32p
@@ -550,6 +551,11 @@ class KvCache:
 
     def truncate(self, n: int):
         lib().or_cache_truncate(self.ptr, n)
+
+    def set_len(self, n: int):
+        """Timing samples only: length n <= cap without computing the rows
+        in between (see or_cache_set_len)."""
+        lib().or_cache_set_len(self.ptr, n)
 
     def clone(self) -> "KvCache":
         c = KvCache(self.model, self.cap)

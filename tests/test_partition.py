@@ -1,4 +1,4 @@
-"""Session-level data parallelism (SURVEY-style row e): the deterministic
+"""Session-level data parallelism across GPUs: the deterministic
 partition of sessions over ranks, and the sharded verified replay run as
 two gloo ranks on the CPU (the oracle's checkout as the per-rank worker, so
 no GPU is needed). The GPU worker is the batched replay the GPU tests cover."""
