@@ -620,6 +620,18 @@ def generate_batch(model: Model, prompts: Sequence[Sequence[int]], seeds: Sequen
     return [[int(t) for t in outs[i][:no[i]]] for i in range(n)], ms.value
 
 
+def tc_gemm(x: np.ndarray, w: np.ndarray, w_bf16: bool = False, device: int = 0) -> np.ndarray:
+    """The tensor-core contraction of the batched attribution step on its
+    own: x [m, k] . w [n, k]^T (m <= 128) as split-bf16 tcgen05 MMAs."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    m, k = x.shape
+    n = w.shape[0]
+    y = np.empty((m, n), np.float32)
+    _check(_L().defer_debug_tc_gemm(device, _f32p(x), m, _f32p(w), n, k, 1 if w_bf16 else 0, _f32p(y)))
+    return y
+
+
 def ablation_attribution(model: Model, context: Sequence[int], target: int, positions: Sequence[int],
                          batch: int = 128):
     """attribution::ablation_attribution (src/attribution.rs:224-264):

@@ -106,6 +106,8 @@ SIGNATURES = [
     ("defer_debug_trace_arm", ctypes.c_int, [vp, ctypes.c_int32]),
     ("defer_debug_trace_read", ctypes.c_int, [vp, ctypes.POINTER(ctypes.c_uint64), sz, c_szp, c_i32p, c_i32p]),
     ("defer_debug_stall", ctypes.c_int, [vp, ctypes.c_uint32]),
+    ("defer_debug_tc_gemm", ctypes.c_int, [ctypes.c_int, c_f32p, ctypes.c_uint32, c_f32p, ctypes.c_uint32,
+                                           ctypes.c_uint32, ctypes.c_int32, c_f32p]),
     ("defer_log_softmax_at", ctypes.c_double, [c_f32p, sz, sz]),
 ]
 

@@ -9,6 +9,7 @@
 
 #include "common.h"
 #include "engine.h"
+#include "tc.h"
 #include "formats.h"
 #include "hostutil.h"
 #include "kernels.h"
@@ -593,6 +594,14 @@ int defer_debug_trace_read(const defer_model* m, uint64_t* out, size_t cap, size
       if (cap < M.dbg_trace.size()) defer::fail(defer::kInvalidArgument, "trace buffer too small");
       std::copy(M.dbg_trace.begin(), M.dbg_trace.end(), out);
     }
+  });
+}
+
+int defer_debug_tc_gemm(int device, const float* x, uint32_t m, const float* w, uint32_t n, uint32_t k,
+                        int32_t w_bf16, float* y) {
+  return guard([&] {
+    if (!x || !w || !y) defer::fail(defer::kInvalidArgument, "null buffer");
+    defer::tc_gemm_check(device, x, (int)m, w, (int)n, (int)k, w_bf16 != 0, y);
   });
 }
 

@@ -8,6 +8,7 @@
 #include "common.h"
 #include "flow.h"
 #include "kernels.h"
+#include "tc.h"
 
 namespace defer {
 
@@ -263,8 +264,18 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
     bt.trace = d_trace;
     bt.trace_step = m_->dbg_trace_step;
   }
+  bool tc = false;
+  if (use_tc && n <= kTcM && !any_lanes) {
+    // DEFER_B200_TC: 0 never, 1 whenever the run qualifies, default when the
+    // hidden size makes the tensor cores pay off
+    const char* e = getenv("DEFER_B200_TC");
+    tc = (e && e[0] == '1') || (!(e && e[0] == '0') && m_->dm.H >= 1024);
+    for (int b = 0; b < n && tc; b++) tc = progs[head[b]].n_prompt == (int)progs[head[b]].tokens.size();
+  }
+  if (tc && !m_->tc) m_->tc = tc_model_build(m_->dm, m_->host_layers, m_->sms, st);
   DEFER_CUDA(cudaEventRecord(ev_start_, st));
-  if (plan.ok) launch_steps_flow(m_->dm, bt, fb, plan, nsteps, st);
+  if (tc) launch_steps_tc(m_->dm, *m_->tc, bt, nsteps, m_->sms, m_->tc->work, st);
+  else if (plan.ok) launch_steps_flow(m_->dm, bt, fb, plan, nsteps, st);
   else if (persistent) launch_steps_persistent(m_->dm, bt, nsteps, m_->sms, st);
   else launch_steps_phased(m_->dm, m_->host_layers.data(), bt, 0, nsteps, m_->sms, st);
   DEFER_CUDA(cudaGetLastError());
@@ -329,7 +340,8 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   bytes += (double)steps_run * (double)m_->weight_bytes;
   m_->t_device_ms += ms;
   m_->t_runs += 1;
-  m_->t_launches += persistent ? 1 : (uint64_t)nsteps * (uint64_t)launches_per_step_phased(d) + 1;
+  m_->t_launches += tc ? (uint64_t)nsteps * (uint64_t)launches_per_step_tc(d) + 1
+                       : persistent ? 1 : (uint64_t)nsteps * (uint64_t)launches_per_step_phased(d) + 1;
   m_->t_tokens += tokens;
   m_->t_bytes += bytes;
   if (ctrl[0] == kStTimeout) fail(kDeviceTimeout, "a bounded wait of the token loop timed out");
@@ -771,6 +783,7 @@ void ablation_batch(Model* m, const uint32_t* context, size_t n, uint32_t target
   std::vector<float> logits(m->cfg.vocab_size);
   {
     Runner r1(m, 1, cap);
+    r1.use_tc = true;  // the variants reuse this prefix: same arithmetic as theirs
     std::vector<SlotProgram> progs(1);
     progs[0].cache = full.get();
     progs[0].tokens.assign(context, context + n);
@@ -784,6 +797,7 @@ void ablation_batch(Model* m, const uint32_t* context, size_t n, uint32_t target
   if (batch <= 0) batch = 1;
   batch = std::min<int>(batch, (int)n_pos);
   Runner runner(m, batch, cap);
+  runner.use_tc = true;
   std::vector<std::unique_ptr<KvCache>> caches;
   for (int b = 0; b < batch; b++) caches.emplace_back(cache_new(m, cap));
   const size_t words = (size_t)cap / 32 + 1;

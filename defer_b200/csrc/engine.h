@@ -53,6 +53,9 @@ class Runner {
   // Slot b's logits into slot db of `dst` (same model), on the model's stream.
   void copy_logits_to(int b, Runner& dst, int db) const;
   int last_steps() const { return last_steps_; }
+  // Runs whose programs never sample and fit one 128-slot MMA tile take the
+  // tensor-core step (DEFER_B200_TC=0 keeps them on the CUDA cores).
+  bool use_tc = false;
 
  private:
   const Model* m_;

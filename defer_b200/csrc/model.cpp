@@ -187,6 +187,7 @@ size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 Model::~Model() {
   if (fwd_runner && fwd_runner_free) fwd_runner_free(fwd_runner);
   if (replay_runner && replay_runner_free) replay_runner_free(replay_runner);
+  delete tc;
   if (arena) cudaFree(arena);
   if (d_layers) cudaFree(d_layers);
   if (stream) cudaStreamDestroy(stream);

@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "device.cuh"
+#include "tc.h"
 
 namespace defer {
 
@@ -45,6 +46,8 @@ struct Model {
   mutable void* replay_runner = nullptr;
   mutable void (*replay_runner_free)(void*) = nullptr;
   mutable int replay_runner_B = 0, replay_runner_cap = 0;
+  // Projections packed for the tensor-core step (built on first use).
+  mutable TcModel* tc = nullptr;
   // Accumulated by every token-loop run on this model (see defer_model_timing):
   // device time between events recorded on `stream` around the launch, runs,
   // kernel launches, tokens fed, and algorithmic HBM bytes (weights once per

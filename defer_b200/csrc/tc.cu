@@ -1,0 +1,631 @@
+// Tensor-core (tcgen05) contraction of wide batched steps that never sample
+// (the leave-one-out attribution batch, attribution.rs:224-264): every
+// projection of the step is one GEMM Y[slot][row] = A[slot][k] . W[row][k]
+// over up to 128 slots, on the 5th-generation tensor cores with the
+// accumulator in tensor memory.
+//
+// Precision. The weights and activations are fp32; each is split into two
+// bf16 terms, x = x_hi + x_lo with x_hi = bf16(x) and x_lo = bf16(x - x_hi)
+// (|x - x_hi - x_lo| <= 2^-18 |x|), and the product is accumulated in fp32
+// as x_hi.w_hi + x_hi.w_lo + x_lo.w_hi (the dropped x_lo.w_lo term is below
+// 2^-18 of the product). Weights stored as bf16 are exact in one term
+// (w_lo = 0, two products). Results are checked against the CPU oracle at
+// the parity tolerance; they are deterministic run to run (fixed K-block
+// order, split-K partial sums added in split order), but not bit-identical
+// to the CUDA-core path of the other token loops.
+//
+// Operand layout. Both operands are K-major bf16 in the canonical layout
+// without swizzle: 8 x 8 core matrices (8 rows of 16 bytes, 128 contiguous
+// bytes), a 64-wide K block of R rows stored as (row group g, k chunk c) at
+// (g * 8 + c) * 128 bytes, so the leading byte offset (next k chunk) is 128
+// and the stride byte offset (next row group) is 1024. Activations of one
+// K block: [hi: 128 rows][lo: 128 rows] (32 KB); weights are packed once
+// into tiles of 64 rows x 64 k, [hi][lo] per tile (16 KB, 8 KB when bf16),
+// ordered row tile major, K block minor, so a CTA's K range is contiguous.
+//
+// GEMM kernel (k_tc_gemm): one CTA per (64-row tile, K split); 4 warps.
+// Thread 0 streams A and W blocks with bulk copies into a 4-stage ring
+// (mbarrier complete_tx); thread 32 issues the MMAs (M = 128, N = 64,
+// K = 16 per instruction, 2-3 products per k step) and commits each stage
+// back to the producer; after the last block all 128 threads read their
+// TMEM lane (slot) with tcgen05.ld and store the 64 partial sums. Every
+// wait is bounded; a wait that runs out sets the status word, the CTA
+// drains its copies in flight and frees its tensor memory.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "common.h"
+#include "kernels.h"
+#include "phases.cuh"
+#include "tc.h"
+
+namespace defer {
+namespace {
+
+constexpr int kTcBN = 64;                        // weight rows per tile (MMA N)
+constexpr int kTcBK = 64;                        // K per block
+constexpr int kTcStages = 4;
+constexpr int kTcABytes = kTcM * kTcBK * 2;      // one bf16 term of an activation block
+constexpr int kTcWBytes = kTcBN * kTcBK * 2;     // one bf16 term of a weight tile
+constexpr int kTcStageBytes = 2 * kTcABytes + 2 * kTcWBytes;
+constexpr int kTcThreads = 128;
+constexpr unsigned long long kTcWaitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mb_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mb_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mb_try(uint64_t* b, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity` to complete; false when it ran out.
+__device__ __forceinline__ bool mb_wait(uint64_t* b, unsigned parity) {
+  if (mb_try(b, parity)) return true;
+  const unsigned long long t0 = gtime();
+  unsigned spins = 0;
+  while (!mb_try(b, parity)) {
+    if ((++spins & 63u) == 0 && gtime() - t0 > kTcWaitNs) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   saddr(dst)),
+               "l"(src), "r"(bytes), "r"(saddr(bar))
+               : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, no swizzle, Blackwell version.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version 1; base offset 0, layout SWIZZLE_NONE
+  return d;
+}
+// Instruction descriptor of kind::f16: bf16 A and B (both K-major), fp32 D.
+constexpr uint32_t kIdesc = (1u << 4)                       // D format f32
+                            | (1u << 7) | (1u << 10)        // A, B format bf16
+                            | ((uint32_t)(kTcBN >> 3) << 17)  // N
+                            | ((uint32_t)(kTcM >> 4) << 24);  // M
+
+__device__ __forceinline__ void umma(uint32_t dtm, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(dtm), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+               : "memory");
+}
+
+struct TcGemmArgs {
+  const unsigned char* A;  // [nkb][2][kTcM * kTcBK] bf16
+  const unsigned char* W;  // [ntile][nkb][wterms][kTcBN * kTcBK] bf16
+  float* Y;                // [splits][kTcM][n_pad] partial sums
+  int nkb, splits, n_pad, wterms;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ TcGemmArgs g) {
+  extern __shared__ __align__(1024) unsigned char tsm[];
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int failed;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x / g.splits, sp = blockIdx.x % g.splits;
+  const int kb0 = sp * g.nkb / g.splits, kb1 = (sp + 1) * g.nkb / g.splits;
+  const int nk = kb1 - kb0;
+  unsigned char* ring = tsm;
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; s++) {
+      mb_init(&full[s], 1);
+      mb_init(&empty[s], 1);
+    }
+    mb_init(&done, 1);
+    failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  if (warp == 0) {  // 64 columns of tensor memory: the 128 x 64 fp32 accumulator
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base)),
+                 "r"(kTcBN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tm = tmem_base;
+  const size_t wtile = (size_t)g.wterms * kTcWBytes;
+  const unsigned stage_bytes = 2u * kTcABytes + (unsigned)wtile;
+
+  if (tid == 0) {
+    // producer: this CTA's K blocks of A and of its weight tile
+    int issued = 0;
+    for (int i = 0; i < nk; i++) {
+      const int s = i % kTcStages;
+      if (i >= kTcStages && !mb_wait(&empty[s], (unsigned)((i / kTcStages - 1) & 1))) {
+        atomicCAS(g.status, kStOk, kStTimeout);
+        *(volatile int*)&failed = 1;
+        break;
+      }
+      if (*(volatile int*)&failed) break;
+      unsigned char* st = ring + (size_t)s * kTcStageBytes;
+      mb_expect_tx(&full[s], stage_bytes);
+      bulk_copy(st, g.A + (size_t)(kb0 + i) * 2 * kTcABytes, 2u * kTcABytes, &full[s]);
+      bulk_copy(st + 2 * kTcABytes, g.W + ((size_t)tile * g.nkb + kb0 + i) * wtile, (unsigned)wtile, &full[s]);
+      issued = i + 1;
+    }
+    // copies still in flight land before the CTA leaves: the last one of each stage
+    for (int i = max(0, issued - kTcStages); i < issued; i++)
+      if (!mb_wait(&full[i % kTcStages], (unsigned)((i / kTcStages) & 1))) atomicCAS(g.status, kStOk, kStTimeout);
+  } else if (tid == 32) {
+    // MMA issuer
+    int i = 0;
+    for (; i < nk; i++) {
+      const int s = i % kTcStages;
+      if (!mb_wait(&full[s], (unsigned)((i / kTcStages) & 1))) {
+        atomicCAS(g.status, kStOk, kStTimeout);
+        *(volatile int*)&failed = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t st = saddr(ring + (size_t)s * kTcStageBytes);
+      const uint32_t a_hi = st, a_lo = st + kTcABytes, w_hi = st + 2 * kTcABytes, w_lo = w_hi + kTcWBytes;
+#pragma unroll
+      for (int ks = 0; ks < kTcBK / 16; ks++) {
+        const uint32_t o = (uint32_t)ks * 256u;  // two 8-wide k chunks of 128 bytes each
+        const uint64_t ah = smem_desc(a_hi + o, 128, 1024), al = smem_desc(a_lo + o, 128, 1024);
+        const uint64_t wh = smem_desc(w_hi + o, 128, 1024);
+        umma(tm, ah, wh, (i > 0 || ks > 0) ? 1u : 0u);
+        umma(tm, al, wh, 1u);
+        if (g.wterms == 2) umma(tm, ah, smem_desc(w_lo + o, 128, 1024), 1u);
+      }
+      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+    }
+    umma_commit(&done);
+  }
+  __syncwarp();
+  // epilogue: lane r of TMEM = slot r; 64 columns = this tile's rows
+  const bool ok = mb_wait(&done, 0u);
+  if (!ok) atomicCAS(g.status, kStOk, kStTimeout);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (ok && nk > 0) {
+    const int r = warp * 32 + lane;
+    float* y = g.Y + ((size_t)sp * kTcM + r) * g.n_pad + (size_t)tile * kTcBN;
+#pragma unroll
+    for (int c0 = 0; c0 < kTcBN; c0 += 16) {
+      uint32_t v[16];
+      const uint32_t ta = tm + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          : "r"(ta));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        *reinterpret_cast<float4*>(y + c0 + 4 * q) =
+            make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                        __uint_as_float(v[4 * q + 3]));
+    }
+  } else if (ok) {
+    const int r = warp * 32 + lane;  // an empty K range contributes zeros
+    float* y = g.Y + ((size_t)sp * kTcM + r) * g.n_pad + (size_t)tile * kTcBN;
+    for (int c = 0; c < kTcBN; c += 4) *reinterpret_cast<float4*>(y + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kTcBN) : "memory");
+  }
+}
+
+// Offset (elements) of (row r, k) inside one 64-wide K block of R rows.
+__host__ __device__ __forceinline__ size_t core_off(int r, int kk) {
+  return ((size_t)((r >> 3) * 8 + (kk >> 3)) << 6) + (size_t)((r & 7) << 3) + (size_t)(kk & 7);
+}
+
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(x);
+  lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+}
+
+// Weight packing: W [N][K] (fp32, or bf16 when `bf16`) -> tiles; one thread
+// per 8-wide k chunk of one row. Rows >= N and k >= K are zero.
+__global__ void k_tc_pack_w(const void* W, int N, int K, int bf16, int nkb, int wterms, unsigned char* out,
+                            size_t chunks) {
+  for (size_t c = blockIdx.x * (size_t)blockDim.x + threadIdx.x; c < chunks; c += (size_t)gridDim.x * blockDim.x) {
+    const int kc = (int)(c % (size_t)(nkb * 8));
+    const int n = (int)(c / (size_t)(nkb * 8));
+    const int k0 = kc * 8;
+    __align__(16) __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int k = k0 + e;
+      float x = 0.0f;
+      if (n < N && k < K) {
+        if (bf16)
+          x = __uint_as_float((uint32_t)(reinterpret_cast<const uint16_t*>(W)[(size_t)n * K + k]) << 16);
+        else
+          x = reinterpret_cast<const float*>(W)[(size_t)n * K + k];
+      }
+      split_bf16(x, hi[e], lo[e]);
+    }
+    const int tile = n / kTcBN, r = n % kTcBN, kb = k0 / kTcBK, kk = k0 % kTcBK;
+    unsigned char* t = out + ((size_t)tile * nkb + kb) * (size_t)wterms * kTcWBytes;
+    *reinterpret_cast<uint4*>(t + core_off(r, kk) * 2) = *reinterpret_cast<const uint4*>(hi);
+    if (wterms == 2) *reinterpret_cast<uint4*>(t + kTcWBytes + core_off(r, kk) * 2) = *reinterpret_cast<const uint4*>(lo);
+  }
+}
+
+// Activations -> A blocks: slot row b (one CTA each, 128 of them) of `x`
+// ([B][K], row stride K), RMS-normalised with weight `nw` when nw != null
+// ((x * inv) * w, inv = 1 / sqrt(ss / K + eps) with ss a fixed-tree sum),
+// split into bf16 terms. Rows of slots >= B or not active are zero.
+__global__ void __launch_bounds__(256) k_tc_prep(const float* x, const float* nw, float eps, int K, int nkb, int B,
+                                                 const DSlotState* st, unsigned char* A) {
+  const int b = blockIdx.x, tid = threadIdx.x;
+  __shared__ float red[8];
+  __shared__ float s_inv;
+  const bool live = b < B && __ldcg(&st[b].active) != 0;
+  const float* xr = x + (size_t)b * K;
+  if (nw && live) {
+    float acc = 0.0f;
+    for (int k = tid; k < K; k += 256) {
+      const float v = __ldcg(xr + k);
+      acc = fmaf(v, v, acc);
+    }
+    acc = warp_sum_butterfly(acc);
+    if ((tid & 31) == 0) red[tid >> 5] = acc;
+    __syncthreads();
+    if (tid == 0) {
+      float ss = 0.0f;
+      for (int w = 0; w < 8; w++) ss = __fadd_rn(ss, red[w]);
+      s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+    }
+    __syncthreads();
+  }
+  const float inv = (nw && live) ? s_inv : 1.0f;
+  const int kpad = nkb * kTcBK;
+  for (int k0 = tid * 8; k0 < kpad; k0 += 256 * 8) {
+    __align__(16) __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int k = k0 + e;
+      float v = 0.0f;
+      if (live && k < K) {
+        v = __ldcg(xr + k);
+        if (nw) v = __fmul_rn(__fmul_rn(v, inv), nw[k]);
+      }
+      split_bf16(v, hi[e], lo[e]);
+    }
+    const int kb = k0 / kTcBK, kk = k0 % kTcBK;
+    unsigned char* blk = A + (size_t)kb * 2 * kTcABytes;
+    *reinterpret_cast<uint4*>(blk + core_off(b, kk) * 2) = *reinterpret_cast<const uint4*>(hi);
+    *reinterpret_cast<uint4*>(blk + kTcABytes + core_off(b, kk) * 2) = *reinterpret_cast<const uint4*>(lo);
+  }
+}
+
+// Sum of the split-K partials of (slot b, column n), in split order.
+__device__ __forceinline__ float ysum(const float* Y, int splits, int n_pad, int b, int n) {
+  float v = Y[(size_t)b * n_pad + n];
+  for (int s = 1; s < splits; s++) v = __fadd_rn(v, Y[((size_t)s * kTcM + b) * n_pad + n]);
+  return v;
+}
+
+__device__ __forceinline__ bool live_slot(const DBatch& bt, int b) { return ld_i(&bt.st[b].active) != 0; }
+
+// QKV epilogue: pair u (rows 2u, 2u+1) of slot b -> bias, RoPE, q / KV append.
+__global__ void k_tc_qkv_epi(DModel m, DBatch bt, int l, const float* Y, int splits, int n_pad) {
+  const DLayer& Ly = m.layers[l];
+  const int pairs = m.QKVR / 2;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < bt.B * pairs; i += gridDim.x * blockDim.x) {
+    const int b = i / pairs, u = i - b * pairs;
+    if (!live_slot(bt, b)) continue;
+    const float a = ysum(Y, splits, n_pad, b, 2 * u), c = ysum(Y, splits, n_pad, b, 2 * u + 1);
+    qkv_store(m, Ly, bt, l, u, b, ld_i(&bt.st[b].pos), a, c);
+  }
+}
+
+// x[b][n] += Y (O and down projections).
+__global__ void k_tc_resid(DModel m, DBatch bt, const float* Y, int splits, int n_pad) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < bt.B * m.H; i += gridDim.x * blockDim.x) {
+    const int b = i / m.H, n = i - b * m.H;
+    if (!live_slot(bt, b)) continue;
+    float* x = bt.x + (size_t)b * m.H + n;
+    *x = __fadd_rn(*x, ysum(Y, splits, n_pad, b, n));
+  }
+}
+
+// g = act(gate) * up (gate/up rows interleaved).
+__global__ void k_tc_gu_epi(DModel m, DBatch bt, const float* Y, int splits, int n_pad) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < bt.B * m.FF; i += gridDim.x * blockDim.x) {
+    const int b = i / m.FF, j = i - b * m.FF;
+    if (!live_slot(bt, b)) continue;
+    bt.g[(size_t)b * m.FF + j] =
+        gate_act_mul(m, ysum(Y, splits, n_pad, b, 2 * j), ysum(Y, splits, n_pad, b, 2 * j + 1));
+  }
+}
+
+__global__ void k_tc_head_epi(DModel m, DBatch bt, const float* Y, int splits, int n_pad) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)bt.B * m.V;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / m.V), n = (int)(i - (size_t)b * m.V);
+    if (!live_slot(bt, b)) continue;
+    bt.logits[(size_t)b * m.V + n] = ysum(Y, splits, n_pad, b, n);
+  }
+}
+
+// The step's phases that stay on the CUDA cores.
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads) k_tc_select(DModel m, DBatch bt, int run_step) {
+  extern __shared__ __align__(16) float tsel[];
+  ph_select<BF16>(m, bt, run_step, blockIdx.x, gridDim.x, tsel);
+}
+__global__ void __launch_bounds__(kThreads) k_tc_attn(DModel m, DBatch bt, int l) {
+  extern __shared__ __align__(16) float tat[];
+  ph_attn_chunks(m, bt, l, blockIdx.x, gridDim.x, tat);
+}
+__global__ void __launch_bounds__(kThreads) k_tc_combine(DModel m, DBatch bt) {
+  ph_attn_combine(m, bt, blockIdx.x, gridDim.x);
+}
+__global__ void __launch_bounds__(kThreads) k_tc_finalize(DBatch bt) { ph_finalize(bt, blockIdx.x, gridDim.x); }
+
+int div_up(long a, long b) { return (int)((a + b - 1) / b); }
+
+}  // namespace
+
+// ----------------------------------------------------------------- host
+size_t tc_packed_bytes(int N, int K, bool bf16) {
+  const size_t nt = (size_t)div_up(N, kTcBN), nkb = (size_t)div_up(K, kTcBK);
+  return nt * nkb * (bf16 ? 1 : 2) * (size_t)kTcWBytes;
+}
+
+TcMatrix tc_pack(const void* W, int N, int K, bool bf16, unsigned char* out, cudaStream_t st) {
+  TcMatrix t;
+  t.N = N;
+  t.K = K;
+  t.nkb = div_up(K, kTcBK);
+  t.ntile = div_up(N, kTcBN);
+  t.wterms = bf16 ? 1 : 2;
+  t.data = out;
+  const size_t chunks = (size_t)t.ntile * kTcBN * t.nkb * 8;
+  k_tc_pack_w<<<std::min<size_t>((chunks + 255) / 256, 148 * 16), 256, 0, st>>>(W, N, K, bf16 ? 1 : 0, t.nkb,
+                                                                               t.wterms, out, chunks);
+  DEFER_CUDA(cudaGetLastError());
+  return t;
+}
+
+size_t tc_act_bytes(int K) { return (size_t)div_up(K, kTcBK) * 2 * kTcABytes; }
+
+void tc_prep(const float* x, const float* nw, float eps, int K, int B, const DSlotState* st, unsigned char* A,
+             cudaStream_t s) {
+  k_tc_prep<<<kTcM, 256, 0, s>>>(x, nw, eps, K, div_up(K, kTcBK), B, st, A);
+  DEFER_CUDA(cudaGetLastError());
+}
+
+int tc_splits(const TcMatrix& w, int sms) {
+  // enough CTAs to stream the weights from every SM, at least 4 K blocks each
+  int s = 1;
+  while (w.ntile * s < sms && w.nkb / (2 * s) >= 4) s *= 2;
+  return s;
+}
+
+// Kernel attributes are set once per device.
+static bool first_on_device(unsigned long long& mask) {
+  int dev = 0;
+  DEFER_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (mask & bit) return false;
+  mask |= bit;
+  return true;
+}
+
+void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s) {
+  static unsigned long long attr = 0;
+  const int smem = kTcStages * kTcStageBytes;
+  if (first_on_device(attr))
+    DEFER_CUDA(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  TcGemmArgs g;
+  g.A = A;
+  g.W = w.data;
+  g.Y = Y;
+  g.nkb = w.nkb;
+  g.splits = splits;
+  g.n_pad = w.ntile * kTcBN;
+  g.wterms = w.wterms;
+  g.status = status;
+  k_tc_gemm<<<w.ntile * splits, kTcThreads, smem, s>>>(g);
+  DEFER_CUDA(cudaGetLastError());
+}
+
+size_t tc_y_floats(const TcMatrix& w, int splits) { return (size_t)splits * kTcM * w.ntile * kTcBN; }
+
+void launch_steps_tc(const DModel& m, const TcModel& tm, const DBatch& bt0, int nsteps, int sms, TcWork& wk,
+                     cudaStream_t st) {
+  if (bt0.B > kTcM) fail(kInvalidArgument, "tensor-core step: more than 128 slots");
+  DBatch bt = bt0;
+  const size_t smem = step_smem_bytes(m, bt.B, bt.max_chunks);
+  bt.smem_bytes = (unsigned)smem;
+  bt.parts = 1;
+  static unsigned long long attr = 0;
+  if (first_on_device(attr)) {
+    DEFER_CUDA(cudaFuncSetAttribute(k_tc_select<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    DEFER_CUDA(cudaFuncSetAttribute(k_tc_select<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    DEFER_CUDA(cudaFuncSetAttribute(k_tc_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  }
+  if (smem > 200 * 1024) fail(kInvalidArgument, "tensor-core step: phase shared memory too large");
+  const int attn_units = bt.B * m.NKV * bt.max_chunks;
+  const int ew = std::min(sms * 8, 4096);  // epilogue grid
+  for (int s = 0; s < nsteps; s++) {
+    if (m.bf16) k_tc_select<true><<<bt.B, kThreads, smem, st>>>(m, bt, s);
+    else k_tc_select<false><<<bt.B, kThreads, smem, st>>>(m, bt, s);
+    for (int l = 0; l < m.L; l++) {
+      const TcLayer& T = tm.layers[l];
+      tc_prep(bt.x, T.attn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st);
+      tc_gemm(wk.A, T.qkv, wk.Y, T.s_qkv, bt.status, st);
+      k_tc_qkv_epi<<<ew, 256, 0, st>>>(m, bt, l, wk.Y, T.s_qkv, T.qkv.ntile * kTcBN);
+      k_tc_attn<<<std::min(attn_units, sms * 8), kThreads, smem, st>>>(m, bt, l);
+      k_tc_combine<<<sms, kThreads, 0, st>>>(m, bt);
+      tc_prep(bt.att, nullptr, 0.0f, m.QD, bt.B, bt.st, wk.A, st);
+      tc_gemm(wk.A, T.o, wk.Y, T.s_o, bt.status, st);
+      k_tc_resid<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_o, T.o.ntile * kTcBN);
+      tc_prep(bt.x, T.ffn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st);
+      tc_gemm(wk.A, T.gu, wk.Y, T.s_gu, bt.status, st);
+      k_tc_gu_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_gu, T.gu.ntile * kTcBN);
+      tc_prep(bt.g, nullptr, 0.0f, m.FF, bt.B, bt.st, wk.A, st);
+      tc_gemm(wk.A, T.down, wk.Y, T.s_down, bt.status, st);
+      k_tc_resid<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_down, T.down.ntile * kTcBN);
+    }
+    tc_prep(bt.x, m.norm, m.eps, m.H, bt.B, bt.st, wk.A, st);
+    tc_gemm(wk.A, tm.head, wk.Y, tm.s_head, bt.status, st);
+    k_tc_head_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, tm.s_head, tm.head.ntile * kTcBN);
+  }
+  k_tc_finalize<<<bt.B, kThreads, 0, st>>>(bt);
+  DEFER_CUDA(cudaGetLastError());
+}
+
+int launches_per_step_tc(const DModel& m) { return 3 + 12 * m.L; }
+
+void tc_gemm_check(int device, const float* X, int M, const float* W, int N, int K, bool w_bf16, float* Y) {
+  if (M < 1 || M > kTcM || N < 1 || K < 1) fail(kInvalidArgument, "tensor-core GEMM check: bad shape");
+  DEFER_CUDA(cudaSetDevice(device));
+  int sms = 0;
+  DEFER_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  cudaStream_t st;
+  DEFER_CUDA(cudaStreamCreate(&st));
+  const size_t wbytes = (size_t)N * K * (w_bf16 ? 2 : 4);
+  void *dW = nullptr, *dX = nullptr, *dP = nullptr, *dA = nullptr, *dY = nullptr, *dS = nullptr;
+  DEFER_CUDA(cudaMalloc(&dW, wbytes));
+  DEFER_CUDA(cudaMalloc(&dX, (size_t)M * K * 4));
+  DEFER_CUDA(cudaMalloc(&dP, tc_packed_bytes(N, K, w_bf16)));
+  DEFER_CUDA(cudaMalloc(&dA, tc_act_bytes(K)));
+  DEFER_CUDA(cudaMalloc(&dS, sizeof(DSlotState) * M + 16));
+  std::vector<DSlotState> sts(M);
+  for (auto& z : sts) {
+    memset(&z, 0, sizeof(z));
+    z.active = 1;
+  }
+  if (w_bf16) {
+    std::vector<uint16_t> wb((size_t)N * K);
+    for (size_t i = 0; i < wb.size(); i++) {
+      uint32_t u;
+      memcpy(&u, &W[i], 4);
+      wb[i] = (uint16_t)(u >> 16);  // the caller passes bf16-exact values
+    }
+    DEFER_CUDA(cudaMemcpy(dW, wb.data(), wbytes, cudaMemcpyHostToDevice));
+  } else {
+    DEFER_CUDA(cudaMemcpy(dW, W, wbytes, cudaMemcpyHostToDevice));
+  }
+  DEFER_CUDA(cudaMemcpy(dX, X, (size_t)M * K * 4, cudaMemcpyHostToDevice));
+  DEFER_CUDA(cudaMemcpy(dS, sts.data(), sizeof(DSlotState) * M, cudaMemcpyHostToDevice));
+  int* status = reinterpret_cast<int*>(static_cast<char*>(dS) + sizeof(DSlotState) * M);
+  DEFER_CUDA(cudaMemset(status, 0, sizeof(int)));
+  TcMatrix w = tc_pack(dW, N, K, w_bf16, static_cast<unsigned char*>(dP), st);
+  const int splits = tc_splits(w, sms);
+  DEFER_CUDA(cudaMalloc(&dY, tc_y_floats(w, splits) * sizeof(float)));
+  tc_prep(static_cast<float*>(dX), nullptr, 0.0f, K, M, static_cast<DSlotState*>(dS), static_cast<unsigned char*>(dA),
+          st);
+  tc_gemm(static_cast<unsigned char*>(dA), w, static_cast<float*>(dY), splits, status, st);
+  std::vector<float> part(tc_y_floats(w, splits));
+  int stat = 0;
+  DEFER_CUDA(cudaMemcpyAsync(part.data(), dY, part.size() * 4, cudaMemcpyDeviceToHost, st));
+  DEFER_CUDA(cudaMemcpyAsync(&stat, status, sizeof(int), cudaMemcpyDeviceToHost, st));
+  DEFER_CUDA(cudaStreamSynchronize(st));
+  const size_t n_pad = (size_t)w.ntile * kTcBN;
+  for (int r = 0; r < M; r++)
+    for (int n = 0; n < N; n++) {
+      float v = part[(size_t)r * n_pad + n];
+      for (int sp = 1; sp < splits; sp++) v += part[((size_t)sp * kTcM + r) * n_pad + n];
+      Y[(size_t)r * N + n] = v;
+    }
+  cudaFree(dW);
+  cudaFree(dX);
+  cudaFree(dP);
+  cudaFree(dA);
+  cudaFree(dY);
+  cudaFree(dS);
+  cudaStreamDestroy(st);
+  if (stat == kStTimeout) fail(kDeviceTimeout, "a bounded wait of the tensor-core GEMM timed out");
+}
+
+TcModel::~TcModel() {
+  if (arena) cudaFree(arena);
+  if (y_buf) cudaFree(y_buf);
+}
+
+TcModel* tc_model_build(const DModel& m, const std::vector<DLayer>& layers, int sms, cudaStream_t st) {
+  const bool bf = m.bf16 != 0;
+  std::unique_ptr<TcModel> t(new TcModel());
+  size_t bytes = 0;
+  for (int l = 0; l < m.L; l++)
+    bytes += tc_packed_bytes(m.QKVR, m.H, bf) + tc_packed_bytes(m.H, m.QD, bf) + tc_packed_bytes(2 * m.FF, m.H, bf) +
+             tc_packed_bytes(m.H, m.FF, bf);
+  bytes += tc_packed_bytes(m.V, m.H, bf);
+  const size_t act = tc_act_bytes(std::max({m.H, m.QD, m.FF}));
+  DEFER_CUDA(cudaMalloc(&t->arena, bytes + act));
+  t->bytes = bytes;
+  t->max_act = act;
+  unsigned char* p = static_cast<unsigned char*>(t->arena);
+  auto pack = [&](const void* W, int N, int K) {
+    TcMatrix w = tc_pack(W, N, K, bf, p, st);
+    p += tc_packed_bytes(N, K, bf);
+    return w;
+  };
+  t->layers.resize(m.L);
+  for (int l = 0; l < m.L; l++) {
+    TcLayer& T = t->layers[l];
+    T.attn_norm = layers[l].attn_norm;
+    T.ffn_norm = layers[l].ffn_norm;
+    T.qkv = pack(layers[l].wqkv, m.QKVR, m.H);
+    T.o = pack(layers[l].wo, m.H, m.QD);
+    T.gu = pack(layers[l].wgu, 2 * m.FF, m.H);
+    T.down = pack(layers[l].wdown, m.H, m.FF);
+    T.s_qkv = tc_splits(T.qkv, sms);
+    T.s_o = tc_splits(T.o, sms);
+    T.s_gu = tc_splits(T.gu, sms);
+    T.s_down = tc_splits(T.down, sms);
+    t->max_y = std::max({t->max_y, tc_y_floats(T.qkv, T.s_qkv), tc_y_floats(T.o, T.s_o), tc_y_floats(T.gu, T.s_gu),
+                         tc_y_floats(T.down, T.s_down)});
+  }
+  t->head = pack(m.head, m.V, m.H);
+  t->s_head = tc_splits(t->head, sms);
+  t->max_y = std::max(t->max_y, tc_y_floats(t->head, t->s_head));
+  t->work.A = p;
+  DEFER_CUDA(cudaMemsetAsync(t->work.A, 0, act, st));
+  DEFER_CUDA(cudaMalloc(&t->y_buf, t->max_y * sizeof(float)));
+  t->work.Y = t->y_buf;
+  DEFER_CUDA(cudaStreamSynchronize(st));
+  return t.release();
+}
+
+}  // namespace defer

@@ -243,6 +243,13 @@ DEFER_API int defer_debug_trace_read(const defer_model* m, uint64_t* out, size_t
  * wait_us microseconds, so the run ends with DeviceTimeout (9) and no GPU
  * fault; later runs are unaffected. */
 DEFER_API int defer_debug_stall(defer_model* m, uint32_t wait_us);
+/* The tensor-core contraction of the batched attribution step on its own
+ * (no counterpart in the reference; its check): y [m][n] = x [m][k] .
+ * w [n][k]^T with fp32 host buffers, m <= 128, computed as split-bf16
+ * products accumulated in fp32 by tcgen05 MMAs on `device`; with w_bf16
+ * the weights are bf16-exact values stored as bf16. */
+DEFER_API int defer_debug_tc_gemm(int device, const float* x, uint32_t m, const float* w, uint32_t n, uint32_t k,
+                                  int32_t w_bf16, float* y);
 /* attribution::log_softmax_at (src/attribution.rs:71-85). */
 DEFER_API double defer_log_softmax_at(const float* logits, size_t n, size_t idx);
 
