@@ -239,7 +239,10 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   // appends are known to be visible, so lanes (which read rows other lanes
   // append in the same step) take the grid-barrier kernel
   if (mode && flow_words_ && !any_lanes) plan = flow_plan(m_->dm, n, max_chunks_, m_->sms);
-  if (mode == 2 && !plan.ok)
+  // DEFER_B200_LOOP=flow requires the dataflow kernel for the runs it can
+  // take at all (position-parallel lanes and the tensor-core step are
+  // other kernels by design)
+  if (mode == 2 && !plan.ok && !any_lanes && !(use_tc && n <= kTcM))
     fail(kInvalidArgument, std::string("the dataflow token loop does not apply: ") +
                                (flow_words_ ? plan.why : "batch wider than its slot group"));
   FlowBufs fb{};

@@ -32,12 +32,13 @@
 //
 // The two plain (untagged) buffers read across CTAs:
 //  * KV cache: after its QKV stage appended K/V rows, every thread of an
-//    appending CTA executes fence.release.gpu at the start of its O stage
-//    (after the attention stage's CTA barriers), so every later tagged word
-//    of that CTA releases the appends. Every CTA owns gate/up rows, whose
-//    words every CTA polls in its down stage; a fence.acquire.gpu after the
-//    next QKV poll then acquires all appends of earlier steps, and attention
-//    loads the cached rows before (and while) the new q/k/v are polled.
+//    appending CTA executes fence.release.gpu at the start of its down stage
+//    of that layer (after the stage barriers in between), so its
+//    down-projection words, and every later tagged word, release the
+//    appends. Every CTA owns down rows, whose words every CTA polls in its
+//    next QKV stage; a fence.acquire.gpu after that poll acquires all
+//    appends of earlier steps, and attention loads the cached rows before
+//    (and while) the new q/k/v are polled.
 //  * logits: every p-sum writer executes fence.release.gpu (after CTA
 //    barriers that follow the logits stores) before storing its p-sums; the
 //    select phase polls the p-sums, fences (acquire) and then reads the
@@ -113,6 +114,11 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
   uint64_t w;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
+}
+// Two adjacent words (16-byte aligned) in one load; each word is still a
+// single-copy-atomic 8-byte access.
+__device__ __forceinline__ void ld_word2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 // One-directional gpu-scope fences: an acquire fence after relaxed reads
@@ -222,8 +228,83 @@ __device__ __forceinline__ Seg seg1(const uint64_t* src, float* dst, int n, uint
 // the CTA is marked failed (the caller checks after its next barrier). With
 // `acquire`, a fence after the last observation orders this thread's later
 // loads after the writers' release fences.
+// Paired form of the poll: rows of even length and stride starting on a
+// 16-byte boundary are read two words per load, PB pairs per thread per
+// round, so a 1536-word region takes one round trip.
+template <int PB>
+__device__ __forceinline__ bool poll_pairs(const Seg& s, FlowShared& sh, int* status) {
+  const int tid = threadIdx.x;
+  const int np = s.n >> 1;
+  const int total = s.rows * np;
+  const unsigned long long t0 = now_ns();
+  for (int base = 0; base < total; base += kPT * PB) {
+    uint32_t so[PB], dof[PB];
+    unsigned pend = 0;  // bits 2k and 2k + 1: the two words of pair k
+#pragma unroll
+    for (int k = 0; k < PB; k++) {
+      const int f = base + tid + k * kPT;
+      so[k] = 0;
+      dof[k] = 0;
+      if (f < total) {
+        const int r = f / np, c = f - r * np;
+        if ((s.mask >> r) & 1u) {
+          so[k] = (uint32_t)(r * s.sstride + 2 * c);
+          dof[k] = (uint32_t)(r * s.dstride + 2 * c);
+          pend |= 3u << (2 * k);
+        }
+      }
+    }
+    unsigned spins = 0;
+    while (pend) {
+      uint64_t w[2 * PB];
+#pragma unroll
+      for (int k = 0; k < PB; k++)
+        if ((pend >> (2 * k)) & 3u) ld_word2(s.src + so[k], w[2 * k], w[2 * k + 1]);
+#pragma unroll
+      for (int k = 0; k < PB; k++) {
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const unsigned bit = 1u << (2 * k + e);
+          if ((pend & bit) && (uint32_t)(w[2 * k + e] >> 32) == s.want) {
+            s.dst[dof[k] + e] = __uint_as_float((uint32_t)w[2 * k + e]);
+            pend &= ~bit;
+          }
+        }
+      }
+      if (pend && (++spins & 31u) == 0) {
+        if (failed(sh) || status_now(status) != kStOk) {
+          flag_fail(sh, status, kStOk);
+          return false;
+        }
+        if (now_ns() - t0 > sh.wait_ns) {
+          flag_fail(sh, status, kStTimeout);
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+
 template <int PB = kPollBatch>
+__device__ __forceinline__ void poll(const Seg& s, bool acquire, FlowShared& sh, int* status);
+
+// One out-of-line copy of the poll for every stage (instead of one inlined
+// copy per call site): the token loop's code then fits the instruction
+// caches. Scalar arguments keep the region out of local memory.
+template <int PB>
+__device__ __noinline__ void poll_call(const uint64_t* src, float* dst, int n, int rows, int sstride, int dstride,
+                                       unsigned mask, uint32_t want, int acquire, FlowShared* sh, int* status) {
+  poll<PB>(Seg{src, dst, n, rows, sstride, dstride, mask, want}, acquire != 0, *sh, status);
+}
+
+template <int PB>
 __device__ __forceinline__ void poll(const Seg& s, bool acquire, FlowShared& sh, int* status) {
+  if (((s.n | s.sstride) & 1) == 0 && (reinterpret_cast<uintptr_t>(s.src) & 15) == 0) {
+    poll_pairs<(PB + 1) / 2 < 4 ? 4 : (PB + 1) / 2>(s, sh, status);
+    if (acquire) fence_acquire_gpu();
+    return;
+  }
   const int tid = threadIdx.x;
   const int total = s.rows * s.n;
   const unsigned long long t0 = now_ns();
@@ -548,7 +629,9 @@ struct Flow {
     return mk;
   }
   template <int PB = kPollBatch>
-  __device__ void do_poll(const Seg& s, bool acquire) { poll<PB>(s, acquire, sh, bt.status); }
+  __device__ void do_poll(const Seg& s, bool acquire) {
+    poll_call<PB>(s.src, s.dst, s.n, s.rows, s.sstride, s.dstride, s.mask, s.want, acquire ? 1 : 0, &sh, bt.status);
+  }
 
   // Norm weights of a stage: copied global -> shared with cp.async before
   // the poll (no registers held, the copy overlaps the wait); norm_ready()
@@ -579,6 +662,99 @@ struct Flow {
 
   __device__ static void csync_() { DEFER_CTA_SYNC(); }
 
+  // The epilogue of rows `row` (and `row + 1` when has1) of a projection.
+  __device__ void epi(int kind, int l, uint32_t tg, int row, const float* a0, bool has1, const float* a1) {
+    if (kind == kEpiResid) {
+      resid(row, a0, tg);
+      if (has1) resid(row + 1, a1, tg);
+      return;
+    }
+    if (kind == kEpiHead) {
+
+      const int lane = threadIdx.x & 31;
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        if (lane != g) continue;
+        ol[(size_t)g * geo.ol_f + (row - k0 * kSBlk)] = a0[g];
+        if (has1) ol[(size_t)g * geo.ol_f + (row + 1 - k0 * kSBlk)] = a1[g];
+      }
+      return;
+    }
+    if (kind == kEpiGateUp) {
+
+      const int j = row >> 1;
+      const int lane = threadIdx.x & 31;
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        if (lane != g || !sh.act[g]) continue;
+        const float gate = a0[g], up = a1[g];
+        float act;
+        if (m.gelu != 0) {
+          const float C = 0.7978846f;
+          const float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, gate), gate), gate);
+          act = __fmul_rn(__fmul_rn(0.5f, gate), __fadd_rn(1.0f, tanhf(__fmul_rn(C, __fadd_rn(gate, x3)))));
+        } else {
+          act = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
+        }
+        st_f(fb.gt + (size_t)g * m.FF + j, __fmul_rn(act, up), tg);
+      }
+      return;
+    }
+    // kEpiQkv
+    const DLayer& Ly = ly[l];
+    const int HD = m.HD, HALF = m.HALF, Gh = m.NH / m.NKV;
+    const int qh = m.QD / 2, kh = m.KVD / 2, grp = (Gh + 2) * HD;
+    const int qkvd = m.QD + 2 * m.KVD;
+
+      const int u = row >> 1;
+      int sect, h, i;
+      if (u < qh) {
+        sect = 0;
+        h = u / HALF;
+        i = u % HALF;
+      } else if (u < qh + kh) {
+        sect = 1;
+        h = (u - qh) / HALF;
+        i = (u - qh) % HALF;
+      } else {
+        sect = 2;
+        h = (u - qh - kh) / HALF;
+        i = (u - qh - kh) % HALF;
+      }
+      const int lane = threadIdx.x & 31;
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        if (lane != g || !sh.act[g]) continue;
+        float a = a0[g], c = a1[g];
+        if (Ly.bqkv) {
+          a = __fadd_rn(a, Ly.bqkv[2 * u]);
+          c = __fadd_rn(c, Ly.bqkv[2 * u + 1]);
+        }
+        if (sect < 2) {
+          const float cs = rope[(size_t)g * geo.rope_f + i];
+          const float sn = rope[(size_t)g * geo.rope_f + HALF + i];
+          const float a2 = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(c, sn));
+          const float c2 = __fadd_rn(__fmul_rn(c, cs), __fmul_rn(a, sn));
+          a = a2;
+          c = c2;
+        }
+        uint64_t* qrow = fb.qt + (size_t)g * qkvd;
+        if (sect == 0) {
+          uint64_t* d = qrow + (size_t)(h / Gh) * grp + (h % Gh) * HD;
+          st_f(d + i, a, tg);
+          st_f(d + i + HALF, c, tg);
+        } else {
+          const DSession& S = sh.sess[g];
+          float* dst = (sect == 1 ? S.kc : S.vc) + (((size_t)l * m.NKV + h) * S.cap + sh.pos[g]) * HD;
+          dst[i] = a;
+          dst[i + HALF] = c;
+          uint64_t* d = qrow + (size_t)h * grp + (Gh + sect - 1) * HD;
+          st_f(d + i, a, tg);
+          st_f(d + i + HALF, c, tg);
+        }
+      }
+  }
+
   // This CTA's rows of a slice from the ring against the staged inputs
   // xs[g * xstride + k] (k < K), warp by warp with no CTA barrier: each warp
   // takes row pairs of every piece and hands their sums to
@@ -586,8 +762,13 @@ struct Flow {
   // are RMS-normalised on the fly, n = (x * inv) * w with the norm weights
   // staged in nw (the rounding of stage_norm); each warp computes inv.
   // NR rows (2 or 4) per warp pass; the epilogue still sees row pairs.
-  template <bool NORM, int NR = 2, class Epi>
-  __device__ void gemv(const Slice& sl, const float* xs, int xstride, int K, Epi&& epi) {
+  // Epilogue kinds of gemv (one projection loop per normalisation mode,
+  // the epilogue chosen at run time, so the loop's code exists twice, not
+  // once per stage).
+  enum { kEpiQkv = 0, kEpiResid = 1, kEpiGateUp = 2, kEpiHead = 3 };
+
+  template <bool NORM, int NR = 2>
+  __device__ void gemv(const Slice& sl, const float* xs, int xstride, int K, int kind, int l, uint32_t tg) {
     const int warp = threadIdx.x >> 5;
     float inv[G];
     if (NORM && G == 1) {
@@ -620,7 +801,7 @@ struct Flow {
         warp_dot_smem<BF16, NORM, NR, G>(rows, K, xs, xstride, nw, inv, acc);
 #pragma unroll
         for (int q = 0; q < NR / 2; q++)
-          if (i0 + 2 * q < n) epi(sl.row0 + done + i0 + 2 * q, acc[2 * q], i0 + 2 * q + 1 < n, acc[2 * q + 1]);
+          if (i0 + 2 * q < n) epi(kind, l, tg, sl.row0 + done + i0 + 2 * q, acc[2 * q], i0 + 2 * q + 1 < n, acc[2 * q + 1]);
       }
       ring_release(rg);
       done += n;
@@ -858,59 +1039,7 @@ struct Flow {
       tr_done(s, sid_qkv(l));
       return true;
     }
-    const int HD = m.HD, HALF = m.HALF, Gh = m.NH / m.NKV;
-    const int qh = m.QD / 2, kh = m.KVD / 2, grp = (Gh + 2) * HD;
-    const int qkvd = m.QD + 2 * m.KVD;
-    const uint32_t tg = tag(s, sid_qkv(l));
-    gemv<true>(sl, xr, xstride, H, [&](int row, const float* a0, bool, const float* a1) {
-      const int u = row >> 1;
-      int sect, h, i;
-      if (u < qh) {
-        sect = 0;
-        h = u / HALF;
-        i = u % HALF;
-      } else if (u < qh + kh) {
-        sect = 1;
-        h = (u - qh) / HALF;
-        i = (u - qh) % HALF;
-      } else {
-        sect = 2;
-        h = (u - qh - kh) / HALF;
-        i = (u - qh - kh) % HALF;
-      }
-      const int lane = threadIdx.x & 31;
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-        if (lane != g || !sh.act[g]) continue;
-        float a = a0[g], c = a1[g];
-        if (Ly.bqkv) {
-          a = __fadd_rn(a, Ly.bqkv[2 * u]);
-          c = __fadd_rn(c, Ly.bqkv[2 * u + 1]);
-        }
-        if (sect < 2) {
-          const float cs = rope[(size_t)g * geo.rope_f + i];
-          const float sn = rope[(size_t)g * geo.rope_f + HALF + i];
-          const float a2 = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(c, sn));
-          const float c2 = __fadd_rn(__fmul_rn(c, cs), __fmul_rn(a, sn));
-          a = a2;
-          c = c2;
-        }
-        uint64_t* qrow = fb.qt + (size_t)g * qkvd;
-        if (sect == 0) {
-          uint64_t* d = qrow + (size_t)(h / Gh) * grp + (h % Gh) * HD;
-          st_f(d + i, a, tg);
-          st_f(d + i + HALF, c, tg);
-        } else {
-          const DSession& S = sh.sess[g];
-          float* dst = (sect == 1 ? S.kc : S.vc) + (((size_t)l * m.NKV + h) * S.cap + sh.pos[g]) * HD;
-          dst[i] = a;
-          dst[i + HALF] = c;
-          uint64_t* d = qrow + (size_t)h * grp + (Gh + sect - 1) * HD;
-          st_f(d + i, a, tg);
-          st_f(d + i + HALF, c, tg);
-        }
-      }
-    });
+    gemv<true>(sl, xr, xstride, H, kEpiQkv, l, tag(s, sid_qkv(l)));
     tr_done(s, sid_qkv(l));
     return true;
   }
@@ -1117,12 +1246,7 @@ struct Flow {
 
   // --------------------------------------------------- O / gate-up / down
   __device__ bool oproj(int s, int l) {
-    // Release: after the attention stage's barriers, a fence in every thread
-    // of an appending CTA orders this layer's cache appends before any later
-    // tagged word of the CTA; readers acquire them at their next attention
-    // stage of this layer.
     tr_entry(s, sid_o(l));
-    if (has_kv) fence_release_gpu();
     const Slice sl = slice_of(m, ly, nblk, 1, l, cta, ncta, geo.slot_bytes);
     if (sl.nrows == 0) return true;
     csync_();
@@ -1131,10 +1255,7 @@ struct Flow {
     if (fail()) return false;
     tr_recv(s, sid_o(l));
     const uint32_t tg = tag(s, sid_o(l));
-    gemv<false>(sl, stage, m.QD, m.QD, [&](int row, const float* a0, bool has1, const float* a1) {
-      resid(row, a0, tg);
-      if (has1) resid(row + 1, a1, tg);
-    });
+    gemv<false>(sl, stage, m.QD, m.QD, kEpiResid, l, tg);
     tr_done(s, sid_o(l));
     return true;
   }
@@ -1151,31 +1272,19 @@ struct Flow {
     if (fail()) return false;
     tr_recv(s, sid_gu(l));
     const uint32_t tg = tag(s, sid_gu(l));
-    const bool gelu = m.gelu != 0;
-    gemv<true>(sl, stage, m.H, m.H, [&](int row, const float* a0, bool, const float* a1) {
-      const int j = row >> 1;
-      const int lane = threadIdx.x & 31;
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-        if (lane != g || !sh.act[g]) continue;
-        const float gate = a0[g], up = a1[g];
-        float act;
-        if (gelu) {
-          const float C = 0.7978846f;
-          const float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, gate), gate), gate);
-          act = __fmul_rn(__fmul_rn(0.5f, gate), __fadd_rn(1.0f, tanhf(__fmul_rn(C, __fadd_rn(gate, x3)))));
-        } else {
-          act = __fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate)));
-        }
-        st_f(fb.gt + (size_t)g * m.FF + j, __fmul_rn(act, up), tg);
-      }
-    });
+    gemv<true>(sl, stage, m.H, m.H, kEpiGateUp, l, tg);
     tr_done(s, sid_gu(l));
     return true;
   }
 
   __device__ bool down(int s, int l) {
     tr_entry(s, sid_dn(l));
+    // Release: after the stage barriers since this layer's QKV stage, a fence
+    // in every thread of an appending CTA orders its cache appends before
+    // its down-projection words, which every CTA polls in its next QKV
+    // stage (and acquires). Here, before the poll, the fence's wait for the
+    // thread's own stores overlaps the wait for the gate/up words.
+    if (has_kv) fence_release_gpu();
     const Slice sl = slice_of(m, ly, nblk, 3, l, cta, ncta, geo.slot_bytes);
     if (sl.nrows == 0) return true;
     csync_();
@@ -1184,10 +1293,7 @@ struct Flow {
     if (fail()) return false;
     tr_recv(s, sid_dn(l));
     const uint32_t tg = tag(s, sid_dn(l));
-    gemv<false>(sl, stage, m.FF, m.FF, [&](int row, const float* a0, bool has1, const float* a1) {
-      resid(row, a0, tg);
-      if (has1) resid(row + 1, a1, tg);
-    });
+    gemv<false>(sl, stage, m.FF, m.FF, kEpiResid, l, tg);
     tr_done(s, sid_dn(l));
     return true;
   }
@@ -1260,15 +1366,7 @@ struct Flow {
     csync_();
     if (fail()) return false;
     tr_recv(s, sid_head(m.L));
-    gemv<true>(sl, stage, m.H, m.H, [&](int row, const float* a0, bool has1, const float* a1) {
-      const int lane = threadIdx.x & 31;
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-        if (lane != g) continue;
-        ol[(size_t)g * geo.ol_f + (row - sl.row0)] = a0[g];
-        if (has1) ol[(size_t)g * geo.ol_f + (row + 1 - sl.row0)] = a1[g];
-      }
-    });
+    gemv<true>(sl, stage, m.H, m.H, kEpiHead, 0, 0u);
     emit_stats(act, tag(s, sid_head(m.L)), true);
     tr_done(s, sid_head(m.L));
     return true;

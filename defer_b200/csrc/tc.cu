@@ -213,9 +213,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     umma_commit(&done);
   }
   __syncwarp();
-  // epilogue: lane r of TMEM = slot r; 64 columns = this tile's rows
-  const bool ok = mb_wait(&done, 0u);
-  if (!ok) atomicCAS(g.status, kStOk, kStTimeout);
+  // epilogue: lane r of TMEM = slot r; 64 columns = this tile's rows. The
+  // warp-collective TMEM loads need one decision per warp.
+  const bool ok = __all_sync(0xffffffffu, mb_wait(&done, 0u));
+  if (!ok && lane == 0) atomicCAS(g.status, kStOk, kStTimeout);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (ok && nk > 0) {
     const int r = warp * 32 + lane;
