@@ -75,6 +75,16 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak():
+    """Sustained dense bf16 tensor throughput (TFLOP/s) for a kernel timed
+    inside a long step, from MEASURED_PEAKS.json."""
+    try:
+        d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(d["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:  # noqa: BLE001
+        return 1400.0, "fallback (sustained)"
+
+
 def traffic_per_token():
     """DRAM bytes per token of the token-loop kernel from the committed ncu
     summary (profiles/traffic.json), or None."""
@@ -260,17 +270,21 @@ def session_step(D, m, prompt, seed_bytes, wal_path):
     hdr = D.WalHeader(m.signature, seed_bytes, TEMPERATURE, len(prompt), 0, prompt)
     w = D.WalWriter.create(wal_path, hdr)
     gen = CONTEXT - len(prompt)
+    t0 = m.timing()
     out = s.generate(gen, on_token=lambda sess, t: w.append(t, sess.rng_word_pos()))
+    t1 = m.timing()
     w.close()
     ck = D.WalLog.read(wal_path).to_checkpoint()
     r = D.Session.checkout(m, ck)
+    t2 = m.timing()
     assert r.history() == s.history() and len(out) == gen
     tokens = len(prompt) + gen + CONTEXT
     # host->device: program tokens + PRNG words of each run; device->host:
     # tokens, margins and slot state read back after each run
     h2d = 4 * (len(prompt) + 2 * gen + CONTEXT + gen)
     d2h = 4 * (len(prompt) + 2 * gen + CONTEXT + 2 * gen)
-    return tokens, h2d, d2h
+    phases = {k: (t1[k] - t0[k], t2[k] - t1[k]) for k in ("device_ms", "hbm_bytes", "tokens", "launches")}
+    return tokens, h2d, d2h, phases
 
 
 # ------------------------------------------------ single-session greedy (config 1)
@@ -401,6 +415,69 @@ def batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barr
                     "d2h_bytes_per_step": d2h}}
 
 
+# ------------------------------------------------ 8B-shape WAL replay (config 5)
+C5_SESSIONS = 8
+C5_CONTEXT = 4096
+C5_PROMPT = 32
+C5_T = 0.8
+C5_WORKLOAD = ("config5: Llama-3-8B-shape (hidden 4096, 32 layers, 32/8 heads x 128, FFN 14336, vocab 128256 "
+               "untied), random-init N(0,0.02) weights stored bf16 and computed fp32; per GPU 8 sessions "
+               "(32-token uniform-random prompt, ChaCha8 seeds 1000+8*rank.., T=0.8, sampled to a 4096-token "
+               "context by the batched token loop), whose 4096-position checkpoints are replayed together with "
+               "every sampled token verified")
+
+
+def config5_measure(D, rank, world, max_over_ranks, sum_over_ranks, barrier):
+    """Config 5 on every rank (8 sessions per GPU): load, generate the WAL
+    histories, then the timed batched verified replay. Returns the object."""
+    import numpy as np
+    from defer_b200 import synthetic
+    t0 = time.perf_counter()
+    if rank == 0:  # one writer per box, the other ranks wait for the file
+        synthetic.model_path("llama3-8b", model_dir(), 0)
+    barrier()
+    path = synthetic.model_path("llama3-8b", model_dir(), 0)
+    gen_file_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    m = D.Model.load(path, device=int(os.environ.get("LOCAL_RANK", "0")))
+    load_s = time.perf_counter() - t0
+    V = m.config.vocab_size
+    rng = np.random.default_rng(50 + rank)
+    prompts = [[int(t) for t in rng.integers(0, V, C5_PROMPT)] for _ in range(C5_SESSIONS)]
+    seeds = [D.seed_from_u64(1000 + C5_SESSIONS * rank + i) for i in range(C5_SESSIONS)]
+    toks, gen_ms = D.generate_batch(m, prompts, seeds, [C5_T] * C5_SESSIONS, [C5_CONTEXT - C5_PROMPT] * C5_SESSIONS,
+                                    batch=C5_SESSIONS)
+    cks = [D.DeferCheckpoint(m.signature, seeds[k], C5_T, prompts[k] + toks[k], C5_PROMPT, len(toks[k]))
+           for k in range(C5_SESSIONS)]
+    tokens = sum(len(c.history_tokens) for c in cks)
+    m.timing(reset=True)
+    barrier()
+    t0 = time.perf_counter()
+    res, ms = D.replay_batch(m, cks, batch=C5_SESSIONS)
+    wall = time.perf_counter() - t0
+    barrier()
+    tm = m.timing(reset=True)
+    dev_s = max_over_ranks(ms / 1e3)
+    all_tokens = sum_over_ranks(tokens)
+    fails = sum_over_ranks(sum(1 for r in res if r.status != 0))
+    peak, kind = peaks()
+    achieved = sum_over_ranks(tm["hbm_bytes"]) / dev_s / 1e9
+    weight_bytes = m.config.weight_bytes
+    del m  # frees the 8B weights and caches before the next measurement
+    return {"metric": "batched replay tok/s (8B shape, 8 sessions per GPU)", "value": all_tokens / dev_s,
+            "unit": "tok/s", "n_gpus": world, "scaling": "weak", "sessions_per_gpu": C5_SESSIONS,
+            "tokens": int(all_tokens), "divergences": int(fails), "device_s": dev_s,
+            "gpu_launches": tm["launches"],
+            "generate_tok_s": all_tokens / max_over_ranks(gen_ms / 1e3), "load_s": load_s,
+            "file_write_s": gen_file_s, "weights_bytes": weight_bytes,
+            "config": {"workload": C5_WORKLOAD},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / world / peak, "peak_kind": kind,
+                         "note": "15.01 GB of bf16 weights once per step plus every session's KV read and written"},
+            "e2e": {"value": all_tokens / max_over_ranks(wall), "unit": "tok/s",
+                    "h2d_bytes_per_step": sum(len(c.to_bytes()) for c in cks), "d2h_bytes_per_step": 12 * len(cks)}}
+
+
 # ------------------------------------------------ ablation attribution (config 4)
 ABLATION_WORKLOAD = ("config4: SmolLM2-1.7B-shape fp32 Llama (synthetic N(0,0.02) seed 0); leave-one-out "
                      "attribution over a 128-token uniform-random context: base run plus 127 ablated variants "
@@ -408,12 +485,16 @@ ABLATION_WORKLOAD = ("config4: SmolLM2-1.7B-shape fp32 Llama (synthetic N(0,0.02
                      "position with one masked cache per variant, variants batched in one token loop")
 
 
-def ablation_measure(D, rank, sms, clk_mhz):
+def ablation_measure(D, rank, sms, clk_mhz, barrier):
     """Config 4 on this rank: returns the JSON object (device time of the
     ablation's token-loop launches)."""
     import numpy as np
     from defer_b200 import synthetic
-    m = D.Model.load(synthetic.model_path("smollm2-1.7b", model_dir(), 0))
+    if rank == 0:  # one writer per box, the other ranks wait for the file
+        synthetic.model_path("smollm2-1.7b", model_dir(), 0)
+    barrier()
+    m = D.Model.load(synthetic.model_path("smollm2-1.7b", model_dir(), 0),
+                     device=int(os.environ.get("LOCAL_RANK", "0")))
     ctx = [int(t) for t in np.random.default_rng(4 + rank).integers(0, m.config.vocab_size, 128)]
     positions = list(range(len(ctx) - 1))
     D.ablation_attribution(m, ctx[:16], ctx[16], list(range(15)))  # warm-up
@@ -428,15 +509,26 @@ def ablation_measure(D, rank, sms, clk_mhz):
     H, FF, QD, KVD = c.hidden_size, c.intermediate_size, c.q_dim, c.kv_dim
     mac = c.num_layers * (H * (QD + 2 * KVD) + QD * H + 3 * FF * H) + c.vocab_size * H
     dev_s = tm["device_ms"] / 1e3
-    achieved = forwards * 2.0 * mac / dev_s / 1e12
-    peak = sms * FP32_FMA_PER_SM_CLK * 2 * clk_mhz * 1e6 / 1e12
+    useful = forwards * 2.0 * mac  # the model's projection flops
+    # the tensor-core step computes each product as 3 split-bf16 MMAs (2 for bf16-stored weights)
+    terms = 2 if m.config.weights_bf16 else 3
+    tc = os.environ.get("DEFER_B200_TC", "") != "0" and m.config.hidden_size >= 1024
+    peak_tc, kind_tc = tensor_peak()
+    achieved = useful / dev_s / 1e12
+    roof = ({"bound": "tensor", "achieved": achieved * terms, "peak": peak_tc, "unit": "TFLOP/s",
+             "frac": achieved * terms / peak_tc, "peak_kind": kind_tc,
+             "useful_tflops": achieved, "note": f"executed MMA flops = {terms} split-bf16 products per fp32 product"}
+            if tc else
+            {"bound": "fp32 simt", "achieved": achieved, "peak": sms * FP32_FMA_PER_SM_CLK * 2 * clk_mhz * 1e6 / 1e12,
+             "unit": "TFLOP/s", "peak_kind": f"nominal: {sms} SMs x {FP32_FMA_PER_SM_CLK} fp32 FMA/clk x 2 x "
+                                             f"{clk_mhz:.0f} MHz"})
+    if "frac" not in roof:
+        roof["frac"] = roof["achieved"] / roof["peak"]
     return {"metric": "ablation forwards/s (leave-one-out attribution)", "value": forwards / dev_s,
             "unit": "forwards/s", "variants": len(positions), "forwards": forwards, "device_s": dev_s,
             "wall_s": wall, "gpu_launches": tm["launches"], "base_logprob": base,
-            "config": {"workload": ABLATION_WORKLOAD},
-            "roofline": {"bound": "fp32 simt", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "peak_kind": f"nominal: {sms} SMs x {FP32_FMA_PER_SM_CLK} fp32 "
-                                                               f"FMA/clk x 2 x {clk_mhz:.0f} MHz"}}
+            "path": "tensor-core step (tcgen05, split bf16)" if tc else "CUDA-core step",
+            "config": {"workload": ABLATION_WORKLOAD}, "roofline": roof}
 
 
 def run_b200(args):
@@ -505,11 +597,15 @@ def run_b200(args):
         barrier()
         t0 = time.perf_counter()
         tokens = h2d = d2h = 0
+        ph = {"device_ms": [0.0, 0.0], "hbm_bytes": [0.0, 0.0], "tokens": [0, 0], "launches": [0, 0]}
         for _ in range(args.steps):
-            t, a, b = session_step(D, m, prompt, seed_bytes, wal)
+            t, a, b, p = session_step(D, m, prompt, seed_bytes, wal)
             tokens += t
             h2d += a
             d2h += b
+            for k in ph:
+                ph[k][0] += p[k][0]
+                ph[k][1] += p[k][1]
         wall = time.perf_counter() - t0
         barrier()
     tm = m.timing(reset=True)
@@ -524,12 +620,15 @@ def run_b200(args):
         clk_mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
         replay = batched_replay(D, m, args, rank, world, max_over_ranks, sum_over_ranks, barrier, sms, clk_mhz)
         m.timing(reset=True)
+    config5 = None
+    if not args.no_config5:
+        config5 = config5_measure(D, rank, world, max_over_ranks, sum_over_ranks, barrier)
     ablation = None
     if not args.no_ablation:
         import torch
         sms = torch.cuda.get_device_properties(local).multi_processor_count
         clk_mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
-        ablation = ablation_measure(D, rank, sms, clk_mhz)
+        ablation = ablation_measure(D, rank, sms, clk_mhz, barrier)
     try:
         os.unlink(wal)
     except OSError:
@@ -541,14 +640,22 @@ def run_b200(args):
     value = all_tokens / dev_s
     e2e = all_tokens / wall_s
     peak, peak_kind = peaks()
-    runs = max(tm["runs"], 1)
-    achieved = tm["hbm_bytes"] / (tm["device_ms"] / 1e3) / 1e9
+    # The dominant kernel is the single-session decode (k_flow): the
+    # generation launch of every step, 2016 tokens at positions 32..2047.
+    gen_ms, gen_bytes, gen_tok = ph["device_ms"][0], ph["hbm_bytes"][0], ph["tokens"][0]
+    achieved = gen_bytes / (gen_ms / 1e3) / 1e9
     tpt = traffic_per_token()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "peak_kind": peak_kind, "kernel": "k_flow (dataflow token loop, one launch per run)",
-                "bytes_per_launch": tm["hbm_bytes"] / runs,
-                "traffic": (tpt * tokens / runs) if tpt else None,
-                "launch_ms": tm["device_ms"] / runs}
+                "peak_kind": peak_kind, "kernel": "k_flow (dataflow token loop): the generation launch of each step",
+                "bytes_per_launch": gen_bytes / args.steps, "tokens_per_launch": gen_tok / args.steps,
+                "traffic": (tpt * gen_tok / args.steps) if tpt else None,
+                "launch_ms": gen_ms / args.steps, "us_per_token": 1e3 * gen_ms / max(gen_tok, 1)}
+    rep_ms, rep_bytes, rep_tok = ph["device_ms"][1], ph["hbm_bytes"][1], ph["tokens"][1]
+    checkout_obj = {"what": "position-parallel verified checkout of the WAL (lanes of one cache, grid-barrier kernel)",
+              "tokens_per_step": rep_tok / args.steps, "ms_per_step": rep_ms / args.steps,
+              "tok_s": rep_tok / (rep_ms / 1e3) if rep_ms else None,
+              "launches_per_step": ph["launches"][1] / args.steps,
+              "hbm_gbs": rep_bytes / (rep_ms / 1e3) / 1e9 if rep_ms else None}
     if rank == 0:
         assert tokens == 2 * CONTEXT * args.steps
         line = {"metric": METRIC, "value": value, "unit": "tok/s",
@@ -556,11 +663,11 @@ def run_b200(args):
                 "ms_per_step": 1000.0 * dev_s / args.steps, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": value / world / 17.0, "dtype": "fp32", "data": "synthetic",
                 "config": bench_config(world),
-                "roofline": roofline, "cpu_baseline": cpu, "config1": c1,
+                "roofline": roofline, "checkout": checkout_obj, "cpu_baseline": cpu, "config1": c1,
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d // max(args.steps, 1),
                         "d2h_bytes_per_step": d2h // max(args.steps, 1)},
                 "gpu_launches": tm["launches"], "clocks": clocks, "batched_replay": replay,
-                "ablation": ablation,
+                "ablation": ablation, "config5": config5,
                 "device": {"tokens": tokens, "device_ms": tm["device_ms"], "runs": tm["runs"]}}
         print(json.dumps(line), flush=True)
     if dist:
@@ -582,6 +689,7 @@ def main(argv=None):
                     help="sessions of the batched replay measurement (config 3); 0 skips it")
     ap.add_argument("--replay-gen", type=int, default=512, help="generated tokens per replay session")
     ap.add_argument("--replay-batch", type=int, default=512, help="slots per GPU of the batched replay")
+    ap.add_argument("--no-config5", action="store_true", help="skip config 5 (8B shape, 8 replayed sessions)")
     ap.add_argument("--no-ablation", action="store_true",
                     help="skip config 4 (1.7B-shape leave-one-out attribution, 127 variants)")
     ap.add_argument("--profile-case", nargs="?", const="single", choices=["single", "batched"],

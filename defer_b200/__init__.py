@@ -620,6 +620,21 @@ def generate_batch(model: Model, prompts: Sequence[Sequence[int]], seeds: Sequen
     return [[int(t) for t in outs[i][:no[i]]] for i in range(n)], ms.value
 
 
+def verify(model: Model, seed: bytes, temperature: float, prompt: Sequence[int], runs: int = 10,
+           max_tokens: int = 32, stop: Sequence[int] = ()):
+    """`defer verify` (src/main.rs:620-666): `runs` identical sessions and a
+    checkout of run 0, all bit-identical; returns (tokens, KV fingerprint)
+    or raises DivergenceError."""
+    pa, pp = _u32arr(prompt)
+    sa, sp = _u32arr(stop)
+    out = np.empty(max(max_tokens, 1), np.uint32)
+    n = ctypes.c_size_t(0)
+    fp = (ctypes.c_uint8 * 32)()
+    _check(_L().defer_verify(model._h, _u8(seed), temperature, pp, len(prompt), runs, max_tokens, sp, len(stop),
+                             out.ctypes.data_as(_lib.c_u32p), ctypes.byref(n), fp))
+    return [int(t) for t in out[:n.value]], bytes(fp)
+
+
 def tc_gemm(x: np.ndarray, w: np.ndarray, w_bf16: bool = False, device: int = 0) -> np.ndarray:
     """The tensor-core contraction of the batched attribution step on its
     own: x [m, k] . w [n, k]^T (m <= 128) as split-bf16 tcgen05 MMAs."""

@@ -95,6 +95,8 @@ SIGNATURES = [
     ("defer_wal_close", None, [vp]),
     ("defer_wal_to_checkpoint", ctypes.c_int, [c_u8p, sz, c_u8p, sz, c_szp, c_szp, ctypes.POINTER(ctypes.c_int),
                                                ctypes.POINTER(ctypes.c_uint64)]),
+    ("defer_verify", ctypes.c_int, [vp, c_u8p, ctypes.c_float, c_u32p, sz, ctypes.c_uint32, sz, c_u32p, sz, c_u32p,
+                                    c_szp, c_u8p]),
     ("defer_replay_batch", ctypes.c_int, [vp, ctypes.POINTER(c_u8p), c_szp, sz, ctypes.c_int, c_i32p, c_i32p,
                                           c_u32p, c_u8p, c_f64p]),
     ("defer_generate_batch", ctypes.c_int, [vp, ctypes.POINTER(c_u32p), c_szp, c_u8p, c_f32p, c_szp, sz,

@@ -597,6 +597,21 @@ int defer_debug_trace_read(const defer_model* m, uint64_t* out, size_t cap, size
   });
 }
 
+int defer_verify(defer_model* m, const uint8_t seed[32], float temperature, const uint32_t* prompt, size_t n_prompt,
+                 uint32_t runs, size_t max_tokens, const uint32_t* stop, size_t n_stop, uint32_t* out_tokens,
+                 size_t* n_out, uint8_t fingerprint[32]) {
+  return guard([&] {
+    need(m, "model");
+    if (!seed || !fingerprint || (n_prompt && !prompt) || (n_stop && !stop) || (max_tokens && !out_tokens))
+      defer::fail(defer::kInvalidArgument, "null buffer");
+    std::vector<uint32_t> p(prompt, prompt + n_prompt), st(stop, stop + n_stop);
+    std::vector<uint32_t> out =
+        defer::verify_runs(m->m.get(), seed, temperature, p, (int)runs, max_tokens, st, fingerprint);
+    std::copy(out.begin(), out.end(), out_tokens);
+    if (n_out) *n_out = out.size();
+  });
+}
+
 int defer_debug_tc_gemm(int device, const float* x, uint32_t m, const float* w, uint32_t n, uint32_t k,
                         int32_t w_bf16, float* y) {
   return guard([&] {

@@ -770,6 +770,42 @@ void generate_batch(Model* m, const std::vector<GenRequest>& reqs, int batch, st
   if (device_ms) *device_ms = total_ms;
 }
 
+std::vector<uint32_t> verify_runs(const Model* m, const uint8_t seed[32], float temperature,
+                                  const std::vector<uint32_t>& prompt, int runs, size_t max_tokens,
+                                  const std::vector<uint32_t>& stop, uint8_t fingerprint[32]) {
+  if (runs < 1) fail(kInvalidArgument, "verify needs at least one run");
+  std::vector<uint32_t> ref;
+  uint8_t ref_fp[32] = {0};
+  for (int run = 0; run < runs; run++) {
+    Session s(m, seed, temperature, 0);
+    s.prompt(prompt.data(), prompt.size());
+    std::vector<uint32_t> out = s.generate(max_tokens, stop, nullptr);
+    uint8_t fp[32];
+    cache_fingerprint(s.cache, fp);
+    if (run == 0) {
+      ref = out;
+      memcpy(ref_fp, fp, 32);
+    } else if (out != ref || memcmp(fp, ref_fp, 32) != 0) {
+      fail(kDivergence, "run " + std::to_string(run) + " diverged from run 0");
+    }
+  }
+  // Checkout must reproduce the same cache bits.
+  Checkpoint ck;
+  memcpy(ck.model_signature, m->signature, 32);
+  memcpy(ck.base_seed, seed, 32);
+  ck.temperature = temperature;
+  ck.prompt_len = (uint32_t)prompt.size();
+  ck.history_tokens = prompt;
+  ck.history_tokens.insert(ck.history_tokens.end(), ref.begin(), ref.end());
+  ck.rng_word_pos = U128{(uint64_t)ref.size() * words_per_sample(temperature), 0};
+  std::unique_ptr<Session> restored(Session::checkout(m, ck, 0));
+  uint8_t fp[32];
+  cache_fingerprint(restored->cache, fp);
+  if (memcmp(fp, ref_fp, 32) != 0) fail(kDivergence, "checkout KV cache differs from live cache");
+  memcpy(fingerprint, ref_fp, 32);
+  return ref;
+}
+
 void ablation_batch(Model* m, const uint32_t* context, size_t n, uint32_t target, const size_t* positions,
                     size_t n_pos, int batch, double* base_logprob, double* ablated) {
   if (n == 0) fail(kModel, "cannot ablate an empty context");

@@ -155,6 +155,14 @@ void ablation_batch(Model* m, const uint32_t* context, size_t n, uint32_t target
 
 double log_softmax_at(const float* logits, size_t n, size_t idx);  // attribution.rs:71-85
 
+// `defer verify` (main.rs:620-666): `runs` identical sessions must give the
+// same tokens and KV fingerprint as run 0, and Session::checkout of run 0's
+// checkpoint the same fingerprint; raises Divergence otherwise. Returns run
+// 0's generated tokens and fingerprint.
+std::vector<uint32_t> verify_runs(const Model* m, const uint8_t seed[32], float temperature,
+                                  const std::vector<uint32_t>& prompt, int runs, size_t max_tokens,
+                                  const std::vector<uint32_t>& stop, uint8_t fingerprint[32]);
+
 // One forward step whose scratch lives in a fixed device array instead of
 // allocated buffers (csrc/noalloc.cu); the caller owns the KV cache and the
 // logits buffer.

@@ -63,6 +63,9 @@ SHAPES = {
     # Llama-3-8B shape, bf16-stored (config 5)
     "llama3-8b": Shape(128256, 4096, 14336, 32, 32, 8, 128, 500000.0, False, max_position_embeddings=4097,
                        bf16=True),
+    # the 8B shape's widths with 2 layers (parity tests of config 5's arithmetic)
+    "test-8b-width": Shape(128256, 4096, 14336, 2, 32, 8, 128, 500000.0, False, max_position_embeddings=4097,
+                           bf16=True),
     # small shapes for fast tests
     "test-small": Shape(512, 128, 352, 3, 4, 2, 32, 10000.0, True, max_position_embeddings=1024),
     "test-gqa4": Shape(1000, 256, 512, 2, 8, 2, 32, 500000.0, False, max_position_embeddings=512),

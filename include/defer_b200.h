@@ -193,6 +193,17 @@ DEFER_API void defer_wal_close(defer_wal_writer* w);
 DEFER_API int defer_wal_to_checkpoint(const uint8_t* wal, size_t len, uint8_t* ckpt, size_t cap, size_t* ckpt_len,
                                       size_t* n_records, int* torn_tail, uint64_t* valid_len);
 
+/* `defer verify` (src/main.rs:620-666): `runs` identical sessions (seed,
+ * temperature, prompt, then Session::generate of max_tokens with the stop
+ * tokens) must give run 0's tokens and KV fingerprint, and Session::checkout
+ * of run 0's checkpoint must reproduce that fingerprint; otherwise
+ * Divergence (7) with "run N diverged from run 0" or "checkout KV cache
+ * differs from live cache". out_tokens (max_tokens entries) and
+ * fingerprint receive run 0's results. */
+DEFER_API int defer_verify(defer_model* m, const uint8_t seed[32], float temperature, const uint32_t* prompt,
+                           size_t n_prompt, uint32_t runs, size_t max_tokens, const uint32_t* stop, size_t n_stop,
+                           uint32_t* out_tokens, size_t* n_out, uint8_t fingerprint[32]);
+
 /* ----------------------------------------------------- batched drivers --- */
 /* Session::checkout for n checkpoints at once, `batch` sessions advancing
  * one position per step on the device. Per session: status (0 or the

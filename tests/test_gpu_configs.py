@@ -17,6 +17,9 @@ lengths, through the C ABI:
   config 4: 1.7B shape, leave-one-out ablation over a 128-token context at
             the positions next to the query (p = 124, 125, 126): base and
             ablated log-probabilities and the base logits.
+  config 5: the 8B shape's widths (bf16-stored weights, untied 128256-token
+            head, 32/8 heads x 128) on 2 layers: logits and KV over 40
+            positions, sampled tokens, and the batched verified replay.
 
 The oracle runs are long and single-threaded, so a module fixture starts
 them in spawned worker processes as soon as their inputs exist.
@@ -208,6 +211,40 @@ class _KvView:
 
     def values(self, l):
         return self.kv[l][1]
+
+
+def test_config5_shape_forward_and_replay(tmp_path):
+    """Config 5's arithmetic (8B widths, bf16-stored weights, untied head
+    over 128256 tokens, GQA 32/8 x 128) on a 2-layer model: logits and KV
+    against the oracle over 40 positions, sampled tokens against the
+    oracle's choices, and the batched verified replay of two sessions."""
+    path = model_file(str(tmp_path), "test-8b-width")
+    gm, om = D.Model.load(path), O_model(path)
+    assert gm.config.weights_bf16 and not gm.config.tie_word_embeddings
+    toks = _tokens(gm.config.vocab_size, 40, 12)
+    gc, oc = gm.new_cache(), om.new_cache()
+    worst = 0.0
+    for i, t in enumerate(toks):
+        ok, err, rng = logits_close(gm.forward(t, gc), om.forward(t, oc))
+        assert ok, (i, err, rng)
+        worst = max(worst, err / rng)
+    ok, kv = kv_close(gc, oc, gm.config.num_layers)
+    assert ok, kv
+    prompts = [_tokens(gm.config.vocab_size, 8, 20 + i) for i in range(2)]
+    seeds = [D.seed_from_u64(900 + i) for i in range(2)]
+    gen, _ = D.generate_batch(gm, prompts, seeds, [0.8, 0.8], [24, 24], batch=2)
+    cks = [D.DeferCheckpoint(gm.signature, seeds[k], 0.8, prompts[k] + gen[k], 8, len(gen[k])) for k in range(2)]
+    res, _ = D.replay_batch(gm, cks, batch=2)
+    assert all(r.status == 0 for r in res)
+    reports, _, _ = J.teacher_forced(path, prompts[0] + gen[0], 8, 0.8, seeds[0], [], False)
+    _check_edges(reports, "config5 shape")
+    _record("config5", {"positions": len(toks), "worst_logit_err_over_range": worst, "worst_kv_rel": kv,
+                        "sampled": 24, "oracle_disagreements": len(reports)})
+
+
+def O_model(path):
+    from oracle import oracle as O
+    return O.Model.load(path)
 
 
 def test_config4_ablation_next_to_the_query(runs):

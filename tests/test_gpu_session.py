@@ -267,3 +267,19 @@ def test_ablation_matches_oracle_and_masked_forward(tiny):  # tests/attribution.
         assert D.log_softmax_at(logits, target) == r[q][2]
     with pytest.raises(D.ModelError):
         D.ablation_attribution(m, ctx, target, [len(ctx) - 1])
+
+
+def test_verify_runs_and_checkout_agree_with_the_oracle(tiny):  # src/main.rs:620-666
+    m, p, _ = tiny
+    toks, fp = D.verify(m, D.seed_from_u64(SEED), TEMPERATURE, PROMPT, runs=4, max_tokens=32)
+    assert len(toks) == 32
+    om = O.Model.load(p)
+    os_ = O.Session(om, O.seed_from_u64(SEED), TEMPERATURE)
+    os_.prompt(PROMPT)
+    assert os_.generate(32) == toks  # the reference's stream on its own test model
+    live = D.Session(m, D.seed_from_u64(SEED), TEMPERATURE)
+    live.prompt(PROMPT)
+    live.generate(32)
+    assert live.cache().fingerprint() == fp
+    with pytest.raises(D.InvalidArgumentError):
+        D.verify(m, D.seed_from_u64(SEED), TEMPERATURE, PROMPT, runs=0)
