@@ -26,7 +26,7 @@ int loop_mode() {
 
 int replay_lanes(size_t n) {
   const char* e = getenv("DEFER_B200_REPLAY_LANES");
-  long lanes = 256;
+  long lanes = 512;
   if (e && *e) lanes = strtol(e, nullptr, 10);
   if (lanes < 1) lanes = 1;
   // short histories are cheaper one position per step (dataflow kernel)

@@ -859,15 +859,15 @@ struct Flow {
           const float T = S.temperature;
           float margin = 0.0f;
           uint32_t smp;
-          const float Z = sh.Z[b];
-          if (T != 0.0f && Z > 0.0f && isfinite(Z)) {
-            float* ps = stage;
-            do_poll(seg1(fb.psum + (size_t)b * nblk, ps, nblk, tag(s - 1, sid_s2(m.L))), true);
+          if (T != 0.0f) {
+            // The previous step's logits are complete once every CTA's head
+            // words are: each CTA released its logits stores before them.
+            do_poll(Seg{fb.csm + (size_t)b * fb.cta_cap, stage, ncta, 1, fb.cta_cap, ncta, 1u,
+                        tag(s - 1, sid_head(m.L))},
+                    true);
             csync_();
             if (fail()) return false;
-            const float r = (float)(S.words[k] >> 8) * (1.0f / 16777216.0f);
-            smp = cdf_find(bt.logits + (size_t)b * m.V, m.V, ps, false, nblk, T, sh.M[b], __fdiv_rn(1.0f, Z), r,
-                           &margin, stage + nblk);
+            smp = sample_exact(bt.logits + (size_t)b * m.V, m.V, T, S.words[k], &margin, stage);
           } else {
             float* pr = stage;
             float* lm = stage + 2 * ncta;
@@ -881,7 +881,6 @@ struct Flow {
             }
             csync_();
             smp = argmax_from_blocks(lm, la, ncta, false);
-            if (T != 0.0f) margin = NAN;
           }
           if (S.verify) {
             tok = S.tokens[si];
@@ -1340,6 +1339,10 @@ struct Flow {
     csync_();
     if (threadIdx.x < G && ((slots >> threadIdx.x) & 1u)) {
       const int g = threadIdx.x;
+      // the CTA's logits stores (before the barrier) happen before these
+      // words: a sampling SELECT polls them with an acquire, then reads
+      // the logits
+      if (store) fence_release_gpu();
       ValIdx b{NAN, INT_MAX};
       float sm = -INFINITY;
       for (int w = 0; w < kPW; w++) {
@@ -1388,75 +1391,6 @@ struct Flow {
     emit_stats(slots, tag(-1, sid_head(m.L)), false);
   }
 
-  // Sampler sums of step s for the slots in `slots` (ph_sample1 /
-  // ph_sample2): M from the per-CTA maxima, block e-sums, then Z (the
-  // hierarchical total) and block p-sums.
-  __device__ bool sums(int s, unsigned slots) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* cm = stage;  // [G][ncta]
-    tr_entry(s, sid_s1(m.L));
-    do_poll(Seg{fb.csm, cm, ncta, G, fb.cta_cap, ncta, slots, tag(s, sid_head(m.L))}, false);
-    csync_();
-    if (fail()) return false;
-    tr_recv(s, sid_s1(m.L));
-    if (threadIdx.x < G && ((slots >> threadIdx.x) & 1u)) {
-      float M = -INFINITY;
-      for (int j = 0; j < ncta; j++) M = fmaxf(M, cm[(size_t)threadIdx.x * ncta + j]);
-      sh.M[threadIdx.x] = M;
-    }
-    csync_();
-    const uint32_t t1 = tag(s, sid_s1(m.L));
-    for (int k = k0 + warp; k < k1; k += kPW) {
-      const int i = k * kSBlk + lane;
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-        if (!((slots >> g) & 1u)) continue;
-        const float T = sh.sess[g].temperature;
-        const float e = i < m.V ? e_of(ol[(size_t)g * geo.ol_f + (i - k0 * kSBlk)], T, sh.M[g]) : 0.0f;
-        const float sum = warp_seq_sum(e);
-        if (lane == 0) st_f(fb.esum + (size_t)g * nblk + k, sum, t1);
-      }
-    }
-    tr_done(s, sid_s1(m.L));
-    float* es = stage;  // [G][nblk], then group sums
-    const int ng2 = (nblk + 31) / 32;
-    float* g2 = es + (size_t)G * nblk;
-    float* g3 = g2 + ng2;
-    csync_();
-    tr_entry(s, sid_s2(m.L));
-    do_poll(Seg{fb.esum, es, nblk, G, nblk, nblk, slots, t1}, false);
-    csync_();
-    if (fail()) return false;
-    tr_recv(s, sid_s2(m.L));
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-      if (!((slots >> g) & 1u)) continue;
-      const float Z = hier_total(es + (size_t)g * nblk, nblk, g2, g3, false);
-      if (threadIdx.x == 0) sh.Z[g] = Z;
-    }
-    csync_();
-    if (lane == 0) fence_release_gpu();  // logits stores before the p-sums
-    const uint32_t t2 = tag(s, sid_s2(m.L));
-    for (int k = k0 + warp; k < k1; k += kPW) {
-      const int i = k * kSBlk + lane;
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-        if (!((slots >> g) & 1u)) continue;
-        const float T = sh.sess[g].temperature;
-        const float Z = sh.Z[g];
-        const bool ok = Z > 0.0f && isfinite(Z);
-        float p = 0.0f;
-        if (ok && i < m.V)
-          p = __fmul_rn(e_of(ol[(size_t)g * geo.ol_f + (i - k0 * kSBlk)], T, sh.M[g]), __fdiv_rn(1.0f, Z));
-        const float sum = warp_seq_sum(p);
-        if (lane == 0) st_f(fb.psum + (size_t)g * nblk + k, sum, t2);
-      }
-    }
-    tr_done(s, sid_s2(m.L));
-    csync_();
-    return true;
-  }
-
   __device__ void finalize() {
     if (threadIdx.x != 0) return;
     for (int b = cta; b < bt.B; b += ncta) {
@@ -1472,17 +1406,12 @@ struct Flow {
   }
 
   __device__ void run(int nsteps) {
-    unsigned first = 0, firstT = 0;  // slots whose first step samples from the previous run's logits
+    unsigned first = 0;  // slots whose first step samples from the previous run's logits
     for (int g = 0; g < bt.B; g++) {
       const DSession& S = sh.sess[g];
-      if (!(S.n_prompt == 0 && S.n_total > 0)) continue;
-      first |= 1u << g;
-      if (S.temperature != 0.0f) firstT |= 1u << g;
+      if (S.n_prompt == 0 && S.n_total > 0) first |= 1u << g;
     }
-    if (first) {
-      restat(first);
-      if (firstT && !sums(-1, firstT)) return;
-    }
+    if (first) restat(first);  // the greedy statistics of the previous run's logits
     for (int s = 0; s < nsteps; s++) {
       if (!select(s)) return;
       bool ended = false;
@@ -1498,11 +1427,6 @@ struct Flow {
         break;
       }
       if (!head(s)) return;
-      unsigned samp = 0;
-#pragma unroll
-      for (int g = 0; g < G; g++)
-        if (sh.act[g] && sh.samp[g]) samp |= 1u << g;
-      if (samp && !sums(s, samp)) return;
       if (fail()) return;
     }
     finalize();
@@ -1525,10 +1449,6 @@ __global__ void __launch_bounds__(kFlowThreads, 1)
     sh.fail = 0;
     sh.pfail = 0;
     sh.wait_ns = bt.wait_ns ? bt.wait_ns : kWaitNs;
-    for (int g = 0; g < kMaxGroup; g++) {
-      sh.M[g] = 0.0f;
-      sh.Z[g] = 0.0f;  // no sums yet: a select falls back to the greedy path
-    }
     mbar_fence_init();
   }
   // Programs, slot state, stop lists and the layer table into shared memory.
@@ -1617,6 +1537,7 @@ FlowPlan flow_plan(const DModel& m, int B, int max_chunks, int sms) {
   st = std::max(st, (size_t)G * grid);
   st = std::max(st, (size_t)nblk + ng2 + ng3 + 8);
   st = std::max(st, (size_t)4 * grid);
+  st = std::max(st, sample_exact_floats(m.V));  // the exact sampler of SELECT
   st = (st + 31) & ~(size_t)31;
   const size_t rest = 4 * (st + (size_t)G * (ol_f + ox_f + rope_f) + nw_f) + (((size_t)m.L * sizeof(DLayer) + 15) & ~(size_t)15);
   const size_t budget = (size_t)optin > kStaticSmemReserve ? (size_t)optin - kStaticSmemReserve : 0;

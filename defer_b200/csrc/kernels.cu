@@ -95,14 +95,6 @@ template <bool BF16, int G>
 __global__ void __launch_bounds__(kThreads) k_head(DModel m, DBatch bt) {
   ph_head<BF16, G>(m, bt, blockIdx.x, gridDim.x, dyn_smem);
 }
-template <bool FIRST>
-__global__ void __launch_bounds__(kThreads) k_sample1(DModel m, DBatch bt) {
-  ph_sample1<FIRST>(m, bt, blockIdx.x, gridDim.x, dyn_smem);
-}
-template <bool FIRST>
-__global__ void __launch_bounds__(kThreads) k_sample2(DModel m, DBatch bt) {
-  ph_sample2<FIRST>(m, bt, blockIdx.x, gridDim.x, dyn_smem);
-}
 __global__ void __launch_bounds__(kThreads) k_restat(DModel m, DBatch bt) { ph_restat(m, bt, blockIdx.x, gridDim.x); }
 
 // The device sampler on an arbitrary logits vector (one CTA).
@@ -116,11 +108,7 @@ __global__ void __launch_bounds__(kThreads) k_sample_one(const float* logits, in
   }
 }
 
-size_t sample_one_smem_bytes(int V) {
-  const int nblk = (V + kSBlk - 1) / kSBlk;
-  const int ng2 = (nblk + 31) / 32;
-  return (size_t)(5 * nblk + ng2 + (ng2 + 31) / 32 + 8) * sizeof(float);
-}
+size_t sample_one_smem_bytes(int V) { return sample_exact_floats(V) * sizeof(float); }
 
 void launch_sample_one(const float* logits, int V, float T, uint32_t word, uint32_t* out_tok, float* out_margin,
                        cudaStream_t st) {
@@ -140,14 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
   const int cta = blockIdx.x, ncta = gridDim.x;
   unsigned target = 0;
   if (any_first(bt, false)) {  // the first step samples from the previous run's logits
-    ph_restat(m, bt, cta, ncta);
+    ph_restat(m, bt, cta, ncta);  // their block statistics (the greedy argmax)
     grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
-    if (any_first(bt, true)) {
-      ph_sample1<true>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
-      ph_sample2<true>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
-    }
   }
   for (int s = 0; s < nsteps; s++) {
     ph_select<BF16>(m, bt, s, cta, ncta, dyn_smem);
@@ -172,17 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(DModel m, DBatch bt,
       if (ld_status(bt.status) != kStOk) return;
     }
     ph_head<BF16, G>(m, bt, cta, ncta, dyn_smem);
-    // Decided before the barrier: once a CTA has passed it, the next
-    // step's SELECT may already be changing the slot state this reads, and
-    // every CTA must take the same number of barriers.
-    const bool sampling = any_sampling(bt);
-    grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
-    if (sampling) {
-      ph_sample1<false>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
-      ph_sample2<false>(m, bt, cta, ncta, dyn_smem);
-      grid_barrier(bt.bar, target, bt.status, bt.wait_ns);
-    }
+    grid_barrier(bt.bar, target, bt.status, bt.wait_ns);  // the next SELECT samples from these logits
     if (ld_status(bt.status) != kStOk) return;
   }
   ph_finalize(bt, cta, ncta);
@@ -221,10 +193,8 @@ static size_t step_smem_floats(const DModel& m, int B, int max_chunks) {
     const size_t hs = head_staged_floats(G, m.H, m.bf16 != 0);  // staged head, when it fits
     if (hs * 4 <= 200 * 1024) f = std::max(f, hs);
   }
-  const int nblk = (m.V + kSBlk - 1) / kSBlk;
-  const int ng2 = (nblk + 31) / 32;
-  // sampler sums: the hierarchy's group sums, then a [32][33] buffer per warp
-  f = std::max(f, (((size_t)ng2 + (ng2 + 31) / 32 + 3) & ~(size_t)3) + (size_t)kPW * 32 * 33);
+  // the exact sampler of SELECT
+  f = std::max(f, sample_exact_floats(m.V));
   return (f + 3) & ~(size_t)3;
 }
 
@@ -272,19 +242,13 @@ static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, in
   allow_smem(k_gateup<BF16, G>, smem);
   allow_smem(k_down<BF16, G>, smem);
   allow_smem(k_head<BF16, G>, smem);
-  allow_smem(k_sample1<false>, smem);
-  allow_smem(k_sample1<true>, smem);
-  allow_smem(k_sample2<false>, smem);
-  allow_smem(k_sample2<true>, smem);
   const int B = bt.B;
   const int grid = sms;
   const int attn_units = B * m.NKV * bt.max_chunks;
   (void)hl;
   // statistics of the resident logits for slots whose first step samples
-  // (each kernel skips the slots that do not)
+  // (the kernel skips the slots that do not)
   k_restat<<<grid, kThreads, 0, st>>>(m, bt);
-  k_sample1<true><<<grid, kThreads, smem, st>>>(m, bt);
-  k_sample2<true><<<grid, kThreads, smem, st>>>(m, bt);
   for (int s = 0; s < nsteps; s++) {
     k_select<BF16><<<B, kThreads, smem, st>>>(m, bt, first_step + s);
     for (int l = 0; l < m.L; l++) {
@@ -296,15 +260,12 @@ static void phased_impl(const DModel& m, const DLayer* hl, const DBatch& bt0, in
       k_down<BF16, G><<<grid, kThreads, smem, st>>>(m, bt, l, (unsigned)sf);
     }
     k_head<BF16, G><<<grid, kThreads, smem, st>>>(m, bt);
-    // The sample phases skip every slot that does not sample next.
-    k_sample1<false><<<grid, kThreads, smem, st>>>(m, bt);
-    k_sample2<false><<<grid, kThreads, smem, st>>>(m, bt);
   }
   k_finalize<<<B, kThreads, 0, st>>>(bt);
   DEFER_CUDA(cudaGetLastError());
 }
 
-int launches_per_step_phased(const DModel& m) { return 4 + 5 * m.L; }
+int launches_per_step_phased(const DModel& m) { return 2 + 6 * m.L; }
 
 void launch_steps_phased(const DModel& m, const DLayer* host_layers, const DBatch& bt, int first_step, int nsteps,
                          int sms, cudaStream_t st) {

@@ -540,163 +540,6 @@ __device__ __forceinline__ void block_stats(float l, int idx, bool valid, float 
   }
 }
 
-// Sequential sum of a[k0 .. min(k0 + 32, n)) (terms past n add exactly 0).
-__device__ __forceinline__ float seq_sum32(const float* a, int k0, int n, bool global_src) {
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; j++) v[j] = (k0 + j < n) ? (global_src ? ld_f(a + k0 + j) : a[k0 + j]) : 0.0f;
-  float s = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 32; j++) s = __fadd_rn(s, v[j]);
-  return s;
-}
-
-// Hierarchical totals of block sums `bs[0..nblk)` into smem:
-// g2[nblk/32 groups], g3[groups/32 supergroups]; returns the total (all
-// threads). Sequential at every level.
-static __device__ float hier_total(const float* bs, int nblk, float* g2, float* g3, bool global_src) {
-  const int ng2 = (nblk + 31) / 32, ng3 = (ng2 + 31) / 32;
-  __shared__ float s_tot;
-  for (int t = threadIdx.x; t < ng2; t += kPT) g2[t] = seq_sum32(bs, t * 32, nblk, global_src);
-  DEFER_CTA_SYNC();
-  for (int t = threadIdx.x; t < ng3; t += kPT) g3[t] = seq_sum32(g2, t * 32, ng2, false);
-  DEFER_CTA_SYNC();
-  if (threadIdx.x == 0) {
-    float s = 0.0f;
-    for (int k = 0; k < ng3; k++) s = __fadd_rn(s, g3[k]);
-    s_tot = s;
-  }
-  DEFER_CTA_SYNC();
-  const float r = s_tot;
-  DEFER_CTA_SYNC();
-  return r;
-}
-
-// Finds the sampled token from the block p-sums (CDF search, sampler.rs:94-108).
-// `lg` holds the slot's logits (global). Returns the token; *margin = distance
-// of r to the nearest edge of the chosen token's CDF interval. smem needs
-// ng2 + ng3 floats. Whole CTA.
-static __device__ uint32_t cdf_find(const float* lg, int V, const float* psum, bool global_src, int nblk, float T, float M,
-                             float inv, float r, float* margin, float* smem) {
-  const int ng2 = (nblk + 31) / 32, ng3 = (ng2 + 31) / 32;
-  float* g2 = smem;
-  float* g3 = smem + ng2;
-  hier_total(psum, nblk, g2, g3, global_src);
-  __shared__ int s_blk, s_found, s_tok, s_last, s_grp;
-  __shared__ float s_base, s_Q3, s_Q2, s_Q1, s_margin;
-  if (threadIdx.x == 0) {
-    // supergroup and group searches; cum = Q3 + (Q2 + (Q1 + t))
-    float Q3 = 0.0f;
-    int found = 0, grp = 0;
-    float Q2f = 0.0f;
-    for (int t3 = 0; t3 < ng3 && !found; t3++) {
-      const float Q3n = __fadd_rn(Q3, g3[t3]);
-      if (r < Q3n) {
-        float Q2 = 0.0f;
-        const int e2 = min(ng2, t3 * 32 + 32);
-        for (int t2 = t3 * 32; t2 < e2; t2++) {
-          const float Q2n = __fadd_rn(Q2, g2[t2]);
-          if (r < __fadd_rn(Q3, Q2n) || t2 == e2 - 1) {  // the end of the supergroup is Q3n
-            found = 1;
-            grp = t2;
-            Q2f = Q2;
-            break;
-          }
-          Q2 = Q2n;
-        }
-        s_Q3 = Q3;
-        break;
-      }
-      Q3 = Q3n;
-    }
-    s_found = found;
-    s_grp = grp;
-    s_Q2 = Q2f;
-    s_base = Q3;  // when not found: the CDF total
-  }
-  DEFER_CTA_SYNC();
-  if (threadIdx.x < 32) {
-    // block search inside the group (warp 0), and the last block with p > 0
-    const int lane = threadIdx.x;
-    if (s_found) {
-      const int k = s_grp * 32 + lane;
-      const float bsum = k < nblk ? (global_src ? ld_f(psum + k) : psum[k]) : 0.0f;
-      float Q1 = 0.0f;  // sequential prefix of the block sums before this lane
-      for (int j = 0; j < 32; j++) {
-        const float o = __shfl_sync(0xffffffffu, bsum, j);
-        if (j < lane) Q1 = __fadd_rn(Q1, o);
-      }
-      const float Q3 = s_Q3, Q2 = s_Q2;
-      const bool in = k < nblk && r < __fadd_rn(Q3, __fadd_rn(Q2, __fadd_rn(Q1, bsum)));
-      const unsigned hit = __ballot_sync(0xffffffffu, in);
-      const unsigned valid = __ballot_sync(0xffffffffu, k < nblk);
-      const int j = hit ? __ffs(hit) - 1 : 31 - __clz(valid);  // the group's end is Q3 + Q2n
-      if (lane == j) {
-        s_blk = k;
-        s_Q1 = Q1;
-      }
-    }
-    int lastb = -1;  // highest block with p > 0
-    for (int k0 = ((nblk - 1) / 32) * 32; k0 >= 0 && lastb < 0; k0 -= 32) {
-      const int k = k0 + lane;
-      const bool nz = k < nblk && (global_src ? ld_f(psum + k) : psum[k]) > 0.0f;
-      const unsigned m = __ballot_sync(0xffffffffu, nz);
-      if (m) lastb = k0 + 31 - __clz(m);
-    }
-    if (lane == 0) s_last = lastb;
-  }
-  DEFER_CTA_SYNC();
-  uint32_t tok;
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    if (s_found) {
-      const int i = s_blk * kSBlk + lane;
-      const float p = i < V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
-      float t = 0.0f, prevt = 0.0f;
-      for (int j = 0; j < 32; j++) {
-        const float o = __shfl_sync(0xffffffffu, p, j);
-        if (j <= lane) {
-          prevt = t;
-          t = __fadd_rn(t, o);
-        }
-      }
-      const float Q3 = s_Q3, Q2 = s_Q2, Q1 = s_Q1;
-      const float cum = __fadd_rn(Q3, __fadd_rn(Q2, __fadd_rn(Q1, t)));
-      const float prev = lane == 0 ? __fadd_rn(Q3, __fadd_rn(Q2, Q1)) : __fadd_rn(Q3, __fadd_rn(Q2, __fadd_rn(Q1, prevt)));
-      const unsigned hit = __ballot_sync(0xffffffffu, i < V && r < cum);
-      if (hit) {
-        const int j = __ffs(hit) - 1;
-        if (lane == j) {
-          s_tok = i;
-          s_margin = fminf(__fsub_rn(cum, r), __fsub_rn(r, prev));
-        }
-      } else {
-        // only reachable when the block was chosen as the last of its
-        // group without r falling inside: the last non-zero token
-        const unsigned nz = __ballot_sync(0xffffffffu, i < V && p > 0.0f);
-        if (lane == 0) {
-          s_tok = nz ? s_blk * kSBlk + 31 - __clz(nz) : max(0, s_blk * kSBlk);
-          s_margin = 0.0f;
-        }
-      }
-    } else {
-      const int lb = s_last;
-      const int i = (lb < 0 ? 0 : lb) * kSBlk + lane;
-      const float p = (lb >= 0 && i < V) ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
-      const unsigned nz = __ballot_sync(0xffffffffu, p > 0.0f);
-      if (lane == 0) {
-        s_tok = nz ? lb * kSBlk + 31 - __clz(nz) : 0;
-        s_margin = __fsub_rn(r, s_base);
-      }
-    }
-  }
-  DEFER_CTA_SYNC();
-  tok = (uint32_t)s_tok;
-  *margin = s_margin;
-  DEFER_CTA_SYNC();
-  return tok;
-}
-
 // Greedy choice from the block statistics (exact).
 static __device__ uint32_t argmax_from_blocks(const float* lmax, const int* larg, int nblk, bool global_src) {
   ValIdx best{NAN, INT_MAX};
@@ -725,77 +568,308 @@ static __device__ uint32_t argmax_from_blocks(const float* lmax, const int* larg
   return r;
 }
 
-static __device__ float max_of(const float* a, int n, bool global_src) {
-  float v = -INFINITY;
-  for (int k = threadIdx.x; k < n; k += kPT) v = fmaxf(v, global_src ? ld_f(a + k) : a[k]);
-  v = warp_max(v);
-  __shared__ float s_m[kPW];
-  if ((threadIdx.x & 31) == 0) s_m[threadIdx.x >> 5] = v;
+// ------------------------------------------------------- exact sampler
+// The reference sampler (sampler.rs:43-109) on one logits vector by one
+// CTA, with the reference's own sequential fp32 sums reproduced exactly:
+//   s_i = l_i / T, M = max s_i (NaN skipped), e_i = exp(s_i - M) (0 for NaN
+//   s_i), Z = e_0 + e_1 + ... in index order (fp32), degenerate Z -> the
+//   greedy argmax; p_i = e_i * (1 / Z); r = 24 high bits of the word * 2^-24;
+//   C = p_i added in index order over p_i > 0, the first i with r < C wins,
+//   else the last i with p_i > 0.
+// Exactness in parallel. While the running sum S stays in one binade
+// [2^e, 2^(e+1)), every fp32 addition S + v rounds to the grid u = 2^(e-23),
+// so S advances by q u with q the integer nearest v / u (a tie goes to the
+// even multiple, so it depends on the parity of S / u): an integer sum,
+// until S reaches 2^(e+1). Each thread owns a contiguous chunk; from fp64
+// chunk sums it predicts the binade its chunk runs in and computes the
+// chunk's integer increment for an even and for an odd incoming multiple.
+// Warp 0 then walks the chunks in order with the exact S: a chunk whose
+// prediction holds and that stays below the next power of two advances S by
+// its increment; any other chunk (the first one, where S starts at 0, and
+// those in which S crosses a power of two) is added element by element in
+// fp32 by one lane. The result equals the sequential sum bit for bit, for
+// any chunking. (e_i uses CUDA's expf; the reference's libm may differ in
+// the last bit of some e_i.)
+
+constexpr int kNoBinade = INT_MIN;
+
+__device__ __forceinline__ int binade_of(float s) { return ((__float_as_int(s) >> 23) & 0xFF) - 127; }
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }  // -126 <= k <= 127
+
+// v_i of one exact pass: e_i (Z) or p_i = e_i * inv (CDF).
+struct SampleVals {
+  const float* lg;
+  float T, M, inv;
+  bool p;
+  __device__ __forceinline__ float operator()(int i) const {
+    const float e = e_of(ld_f(lg + i), T, M);
+    return p ? __fmul_rn(e, inv) : e;
+  }
+};
+
+// Shared memory of sample_exact: fp64 chunk prefix, chunk binades and
+// increments, one chunk's values for an element-wise walk.
+__host__ __device__ __forceinline__ size_t sample_exact_floats(int V) {
+  const int c = (V + kPT - 1) / kPT;
+  return (size_t)2 * (kPT + 2) + 3 * kPT + c + 8;
+}
+
+// The sequential fp32 sum of v(0..n) (find < 0), or with find >= 0 the CDF
+// search: the first i with v_i > 0 and r < S_{i+1}; returns S (sum) or the
+// index (-1 when r is never below the CDF), with *prev / *at the CDF before
+// and at that index. Whole CTA.
+static __device__ float exact_seq(const SampleVals& v, int n, bool find, float r, int* found, float* prev, float* at,
+                                  float* smem) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  double* pre = reinterpret_cast<double*>(smem);
+  int* pe = reinterpret_cast<int*>(smem + 2 * (kPT + 2));
+  int* d0 = pe + kPT;
+  int* d1 = d0 + kPT;
+  float* walk = reinterpret_cast<float*>(d1 + kPT);
+  const int c = (n + kPT - 1) / kPT;
+  const int i0 = min(n, tid * c), i1 = min(n, i0 + c);
+  __shared__ float s_res;
+  __shared__ int s_found;
+  __shared__ float s_prev, s_at;
+  // chunk sums (fp64)
+  double sum = 0.0;
+  for (int i = i0; i < i1; i++) sum += (double)v(i);
+  pre[tid + 1] = sum;
   DEFER_CTA_SYNC();
-  float r = -INFINITY;
-  for (int w = 0; w < kPW; w++) r = fmaxf(r, s_m[w]);
+  if (tid < 32) {  // exclusive prefix over the chunks (warp 0)
+    const int per = (kPT + 31) / 32;
+    double loc = 0.0;
+    for (int j = 0; j < per; j++) {
+      const int k = lane * per + j;
+      if (k < kPT) loc += pre[k + 1];
+    }
+    double incl = loc;
+    for (int off = 1; off < 32; off <<= 1) {
+      const double o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    double run = incl - loc;
+    for (int j = 0; j < per; j++) {
+      const int k = lane * per + j;
+      if (k < kPT) {
+        const double x = pre[k + 1];
+        pre[k + 1] = run;  // exclusive prefix of chunk k stored at k + 1 for now
+        run += x;
+      }
+    }
+  }
+  DEFER_CTA_SYNC();
+  {
+    // predicted binade of this chunk and its integer increments
+    const double lo = pre[tid + 1];
+    const double hi = lo + sum;
+    const float flo = (float)lo, fhi = (float)hi;
+    int e = kNoBinade;
+    if (i1 > i0 && flo > 0.0f && isfinite(fhi)) {
+      const int el = binade_of(flo), eh = binade_of(fhi);
+      if (el == eh && el >= -126 + 24 && el <= 100) e = el;
+    }
+    int dd0 = 0, dd1 = 0;
+    if (e != kNoBinade) {
+      const float scale = pow2f(23 - e);
+      int par0 = 0, par1 = 1;
+      for (int i = i0; i < i1; i++) {
+        const float x = __fmul_rn(v(i), scale);
+        if (!(x < 33554432.0f)) {  // >= 2^25 (or not finite): the chunk certainly leaves the binade
+          dd0 = dd1 = 1 << 26;
+          break;
+        }
+        const float fl = floorf(x);
+        const float fr = __fsub_rn(x, fl);
+        const int f = (int)fl;
+        if (fr == 0.5f) {
+          const int q0 = f + ((par0 + f) & 1), q1 = f + ((par1 + f) & 1);
+          dd0 += q0;
+          dd1 += q1;
+          par0 = (par0 + q0) & 1;
+          par1 = (par1 + q1) & 1;
+        } else {
+          const int q = f + (fr > 0.5f ? 1 : 0);
+          dd0 += q;
+          dd1 += q;
+          par0 = (par0 + q) & 1;
+          par1 = (par1 + q) & 1;
+        }
+        if (dd0 > (1 << 26)) dd0 = 1 << 26;
+        if (dd1 > (1 << 26)) dd1 = 1 << 26;
+      }
+    }
+    pe[tid] = e;
+    d0[tid] = dd0;
+    d1[tid] = dd1;
+  }
+  DEFER_CTA_SYNC();
+  if (tid < 32) {
+    // the walk over the chunks with the exact running sum (every lane keeps it)
+    float S = 0.0f, P = 0.0f;
+    int hit = -1;
+    for (int k = 0; k < kPT && hit < 0; k++) {
+      const int a = min(n, k * c), b = min(n, a + c);
+      if (a >= b) break;
+      const int e = pe[k];
+      bool done = false;
+      if (e != kNoBinade && S > 0.0f && binade_of(S) == e) {
+        const int M = (int)__fmul_rn(S, pow2f(23 - e));
+        const int d = (M & 1) ? d1[k] : d0[k];
+        if (M + d < (1 << 24)) {
+          const float Sn = __fmul_rn((float)(M + d), pow2f(e - 23));
+          if (!(find && r < Sn)) {
+            S = Sn;
+            done = true;
+          }
+        }
+      }
+      if (!done) {  // element by element in fp32
+        for (int i = a + lane; i < b; i += 32) walk[i - a] = v(i);
+        __syncwarp();
+        if (lane == 0) {
+          for (int i = a; i < b; i++) {
+            const float x = walk[i - a];
+            if (find) {
+              if (x > 0.0f) {
+                const float Sn = __fadd_rn(S, x);
+                if (r < Sn) {
+                  hit = i;
+                  P = S;
+                  S = Sn;
+                  break;
+                }
+                S = Sn;
+              }
+            } else {
+              S = __fadd_rn(S, x);
+            }
+          }
+        }
+        S = __shfl_sync(0xffffffffu, S, 0);
+        if (!find && !isfinite(S)) break;  // NaN / inf stays so: the sum is degenerate
+        P = __shfl_sync(0xffffffffu, P, 0);
+        hit = __shfl_sync(0xffffffffu, hit, 0);
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {
+      s_res = S;
+      s_found = hit;
+      s_prev = P;
+      s_at = S;
+    }
+  }
+  DEFER_CTA_SYNC();
+  const float res = s_res;
+  if (found) *found = s_found;
+  if (prev) *prev = s_prev;
+  if (at) *at = s_at;
+  DEFER_CTA_SYNC();
+  return res;
+}
+
+// Argmax of the raw logits (NaN skipped, lowest index on ties; 0 when all
+// are NaN), M = max of s = l / T (T > 0), and the last index with
+// predicate p_i > 0 when `inv` is given (lastp). Whole CTA.
+static __device__ void logits_scan(const float* lg, int V, float T, int* amax, float* M) {
+  ValIdx best{NAN, INT_MAX};
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += kPT) {
+    const float l = ld_f(lg + i);
+    const ValIdx c{l, isnan(l) ? INT_MAX : i};
+    if (vi_better(c, best)) best = c;
+    if (T != 0.0f) m = fmaxf(m, __fdiv_rn(l, T));
+  }
+  best = vi_warp_best(best);
+  m = warp_max(m);
+  __shared__ float s_v[kPW], s_m[kPW];
+  __shared__ int s_i[kPW];
+  __shared__ int s_res;
+  __shared__ float s_max;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    s_v[warp] = best.v;
+    s_i[warp] = best.i;
+    s_m[warp] = m;
+  }
+  DEFER_CTA_SYNC();
+  if (warp == 0) {
+    ValIdx c = lane < kPW ? ValIdx{s_v[lane], s_i[lane]} : ValIdx{NAN, INT_MAX};
+    float mm = lane < kPW ? s_m[lane] : -INFINITY;
+    c = vi_warp_best(c);
+    mm = warp_max(mm);
+    if (lane == 0) {
+      s_res = c.i == INT_MAX ? 0 : c.i;
+      s_max = mm;
+    }
+  }
+  DEFER_CTA_SYNC();
+  *amax = s_res;
+  *M = s_max;
+  DEFER_CTA_SYNC();
+}
+
+// Last index with p_i > 0 (sampler.rs:101-108), -1 when none. Whole CTA.
+static __device__ int last_positive(const SampleVals& v, int V) {
+  int last = -1;
+  for (int i = threadIdx.x; i < V; i += kPT)
+    if (v(i) > 0.0f) last = i;
+  for (int off = 16; off > 0; off >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, off));
+  __shared__ int s_l[kPW];
+  __shared__ int s_last;
+  if ((threadIdx.x & 31) == 0) s_l[threadIdx.x >> 5] = last;
+  DEFER_CTA_SYNC();
+  if (threadIdx.x == 0) {
+    int r = -1;
+    for (int w = 0; w < kPW; w++) r = max(r, s_l[w]);
+    s_last = r;
+  }
+  DEFER_CTA_SYNC();
+  const int r = s_last;
   DEFER_CTA_SYNC();
   return r;
 }
 
-// Whole sampler on one logits vector by one CTA (same arithmetic as the
-// distributed path: the block statistics and sums are computed here).
-// smem: 5 * nblk + ng2 + ng3 floats.
-static __device__ uint32_t sample_cta(const float* lg, int V, float T, uint32_t word, float* margin, float* smem) {
-  const int nblk = (V + kSBlk - 1) / kSBlk;
-  float* lmax = smem;
-  int* larg = reinterpret_cast<int*>(smem + nblk);
-  float* smax = smem + 2 * nblk;
-  float* esum = smem + 3 * nblk;
-  float* psum = smem + 4 * nblk;
-  float* tail = smem + 5 * nblk;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int k = warp; k < nblk; k += kPW) {
-    const int i = k * kSBlk + lane;
-    const bool valid = i < V;
-    const float l = valid ? ld_f(lg + i) : NAN;
-    block_stats(l, i, valid, T, lmax + k, larg + k, smax + k);
-  }
-  DEFER_CTA_SYNC();
+// sampler::sample_token with the PRNG word already drawn. *margin = the
+// distance of r to the nearer edge of the chosen token's CDF interval (0
+// for greedy, NaN for the degenerate one-hot fallback). smem:
+// sample_exact_floats(V) floats. Whole CTA.
+static __device__ uint32_t sample_exact(const float* lg, int V, float T, uint32_t word, float* margin, float* smem) {
+  int amax;
+  float M;
+  logits_scan(lg, V, T, &amax, &M);
   if (T == 0.0f) {
     *margin = 0.0f;
-    return argmax_from_blocks(lmax, larg, nblk, false);
+    return (uint32_t)amax;
   }
-  const float M = max_of(smax, nblk, false);
-  for (int k = warp; k < nblk; k += kPW) {
-    const int i = k * kSBlk + lane;
-    const float e = i < V ? e_of(ld_f(lg + i), T, M) : 0.0f;
-    const float s = warp_seq_sum(e);
-    if (lane == 0) esum[k] = s;
-  }
-  DEFER_CTA_SYNC();
-  const float Z = hier_total(esum, nblk, tail, tail + (nblk + 31) / 32, false);
+  const SampleVals ve{lg, T, M, 0.0f, false};
+  const float Z = exact_seq(ve, V, false, 0.0f, nullptr, nullptr, nullptr, smem);
   if (!(Z > 0.0f) || !isfinite(Z)) {
     *margin = NAN;
-    return argmax_from_blocks(lmax, larg, nblk, false);
+    return (uint32_t)amax;
   }
   const float inv = __fdiv_rn(1.0f, Z);
-  for (int k = warp; k < nblk; k += kPW) {
-    const int i = k * kSBlk + lane;
-    const float p = i < V ? __fmul_rn(e_of(ld_f(lg + i), T, M), inv) : 0.0f;
-    const float s = warp_seq_sum(p);
-    if (lane == 0) psum[k] = s;
-  }
-  DEFER_CTA_SYNC();
+  const SampleVals vp{lg, T, M, inv, true};
   const float r = (float)(word >> 8) * (1.0f / 16777216.0f);
-  return cdf_find(lg, V, psum, false, nblk, T, M, inv, r, margin, tail);
+  int hit;
+  float prev, at;
+  const float total = exact_seq(vp, V, true, r, &hit, &prev, &at, smem);
+  if (hit >= 0) {
+    *margin = fminf(__fsub_rn(r, prev), __fsub_rn(at, r));
+    return (uint32_t)hit;
+  }
+  const int last = last_positive(vp, V);
+  *margin = __fsub_rn(r, total);
+  return (uint32_t)(last < 0 ? 0 : last);
+}
+
+// Whole sampler on one logits vector by one CTA (the exact sampler above).
+static __device__ uint32_t sample_cta(const float* lg, int V, float T, uint32_t word, float* margin, float* smem) {
+  return sample_exact(lg, V, T, word, margin, smem);
 }
 
 // ----------------------------------------------------------- select / embed
-// Whether slot b samples at T > 0 in the step after the current one.
-__device__ __forceinline__ bool samples_next(const DBatch& bt, int b) {
-  const DSession& S = bt.sess[b];
-  if (S.temperature == 0.0f) return false;
-  if (!ld_i(&bt.st[b].active) || ld_i(&bt.st[b].done)) return false;
-  const int nxt = ld_i(&bt.st[b].step) + 1;
-  return nxt >= S.n_prompt && nxt < S.n_total;
-}
-
 // Advances the slots that fed a token in the previous step, picks the
 // token of this step for every slot (prompt token, sample from the
 // previous step's statistics, or verified replay of a recorded token) and
@@ -839,24 +913,12 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
       const int k = vi - S.n_prompt;
       const float T = S.temperature;
       const int nb = bt.nblk;
-      const float* lmax = bt.ss.lmax + (size_t)b * nb;
-      const int* larg = bt.ss.larg + (size_t)b * nb;
       float margin = 0.0f;
       uint32_t smp;
       if (T == 0.0f) {
-        smp = argmax_from_blocks(lmax, larg, nb, true);
+        smp = argmax_from_blocks(bt.ss.lmax + (size_t)b * nb, bt.ss.larg + (size_t)b * nb, nb, true);
       } else {
-        const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
-        const int ng2 = (nb + 31) / 32;
-        const float Z = hier_total(bt.ss.esum + (size_t)b * nb, nb, smem, smem + ng2, true);
-        if (!(Z > 0.0f) || !isfinite(Z)) {
-          smp = argmax_from_blocks(lmax, larg, nb, true);
-          margin = NAN;
-        } else {
-          const float r = (float)(S.words[k] >> 8) * (1.0f / 16777216.0f);
-          smp = cdf_find(bt.logits + (size_t)b * m.V, m.V, bt.ss.psum + (size_t)b * nb, true, nb, T, M,
-                         __fdiv_rn(1.0f, Z), r, &margin, smem);
-        }
+        smp = sample_exact(bt.logits + (size_t)b * m.V, m.V, T, S.words[k], &margin, smem);
       }
       if (S.verify) {
         if (tid == 0 && smp != S.tokens[vi]) {
@@ -1561,113 +1623,6 @@ static __device__ void ph_restat(const DModel& m, const DBatch& bt, int cta, int
       block_stats(valid ? ld_f(lg + i) : NAN, i, valid, T, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
     }
   }
-}
-
-// Whether slot b's sampler sums are needed: for the next step (FIRST =
-// false) or for the first step of the run (FIRST = true).
-template <bool FIRST>
-__device__ __forceinline__ bool needs_sums(const DBatch& bt, int b) {
-  if (FIRST) return samples_first(bt, b) && bt.sess[b].temperature != 0.0f;
-  return samples_next(bt, b);
-}
-
-// The sampler sums are split over (slot, block) pairs: CTA `cta` takes a
-// contiguous range of the flattened index b * nblk + k, so each slot's
-// whole-vector reductions (the max of s, the total of e) are computed only
-// by the one or two CTAs that hold its blocks.
-__device__ __forceinline__ void sum_range(const DBatch& bt, int cta, int ncta, int& f0, int& f1) {
-  const long long n = (long long)bt.B * bt.nblk;
-  f0 = (int)(n * cta / ncta);
-  f1 = (int)(n * (cta + 1) / ncta);
-}
-
-// Sums of the blocks [ka, kb) of kSBlk values each, every sum sequential in
-// element order (the sums warp_seq_sum gives), written to out[k]. A warp
-// takes 32 blocks at a time: it computes val(i) for their 32 x 32 elements
-// with coalesced loads, stages them in buf (its own [32][33] floats) and
-// lane j then adds block j's values one after another.
-// `src` holds the raw values (a slot's logits, n of them); val(i, x) maps
-// raw value x of element i to the summand. All 32 loads of a lane are in
-// flight before any is used.
-template <class F>
-__device__ __forceinline__ void block_seq_sums(int ka, int kb, const float* src, int n, F val, float* buf,
-                                               float* out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  static_assert(kSBlk == 32, "one lane per block of 32 values");
-  for (int kc = ka + 32 * warp; kc < kb; kc += 32 * kPW) {
-    const int nk = min(32, kb - kc);
-    float x[32];
-#pragma unroll
-    for (int r = 0; r < 32; r++) {
-      const int i = (kc + r) * kSBlk + lane;
-      x[r] = (r < nk && i < n) ? ld_f(src + i) : 0.0f;
-    }
-#pragma unroll
-    for (int r = 0; r < 32; r++) {
-      const int i = (kc + r) * kSBlk + lane;
-      buf[r * 33 + lane] = (r < nk && i < n) ? val(x[r]) : 0.0f;
-    }
-    __syncwarp();
-    if (lane < nk) {
-      float sm = 0.0f;
-#pragma unroll
-      for (int t = 0; t < 32; t++) sm = __fadd_rn(sm, buf[lane * 33 + t]);
-      out[kc + lane] = sm;
-    }
-    __syncwarp();
-  }
-}
-
-// Block sums of e for slots sampling next (needs the max over all blocks).
-// smem: kPW * 32 * 33 floats.
-template <bool FIRST>
-__device__ void ph_sample1(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
-  const int warp = threadIdx.x >> 5;
-  const int nb = bt.nblk;
-  int f0, f1;
-  sum_range(bt, cta, ncta, f0, f1);
-  if (f0 >= f1) return;
-  for (int b = f0 / nb; b <= (f1 - 1) / nb; b++) {
-    if (!needs_sums<FIRST>(bt, b)) continue;
-    const float T = bt.sess[b].temperature;
-    const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
-    const float* lg = bt.logits + (size_t)b * m.V;
-    block_seq_sums(max(f0 - b * nb, 0), min(f1 - b * nb, nb), lg, m.V,
-                   [T, M](float l) { return e_of(l, T, M); }, smem + (size_t)warp * 32 * 33,
-                   bt.ss.esum + (size_t)b * nb);
-  }
-}
-
-// Block sums of p = e * (1/Z) for slots sampling next.
-// smem: the hierarchy's group sums, then kPW * 32 * 33 floats.
-template <bool FIRST>
-__device__ void ph_sample2(const DModel& m, const DBatch& bt, int cta, int ncta, float* smem) {
-  const int warp = threadIdx.x >> 5;
-  const int nb = bt.nblk;
-  const int ng2 = (nb + 31) / 32;
-  const size_t tail = ((size_t)ng2 + (ng2 + 31) / 32 + 3) & ~(size_t)3;
-  int f0, f1;
-  sum_range(bt, cta, ncta, f0, f1);
-  if (f0 >= f1) return;
-  for (int b = f0 / nb; b <= (f1 - 1) / nb; b++) {
-    if (!needs_sums<FIRST>(bt, b)) continue;
-    const float T = bt.sess[b].temperature;
-    const float M = max_of(bt.ss.smax + (size_t)b * nb, nb, true);
-    const float Z = hier_total(bt.ss.esum + (size_t)b * nb, nb, smem, smem + ng2, true);
-    if (!(Z > 0.0f) || !isfinite(Z)) continue;  // SELECT falls back to argmax
-    const float inv = __fdiv_rn(1.0f, Z);
-    const float* lg = bt.logits + (size_t)b * m.V;
-    block_seq_sums(max(f0 - b * nb, 0), min(f1 - b * nb, nb), lg, m.V,
-                   [T, M, inv](float l) { return __fmul_rn(e_of(l, T, M), inv); },
-                   smem + tail + (size_t)warp * 32 * 33, bt.ss.psum + (size_t)b * nb);
-  }
-}
-
-// Whether any slot samples at T > 0 next (identical in every CTA).
-__device__ __forceinline__ bool any_sampling(const DBatch& bt) {
-  for (int b = 0; b < bt.B; b++)
-    if (samples_next(bt, b)) return true;
-  return false;
 }
 
 // ------------------------------------------------------------- attention
