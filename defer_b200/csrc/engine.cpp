@@ -238,11 +238,11 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   // the dataflow kernel reads a step's cached rows before that step's
   // appends are known to be visible, so lanes (which read rows other lanes
   // append in the same step) take the grid-barrier kernel
-  if (mode && flow_words_ && !any_lanes) plan = flow_plan(m_->dm, n, max_chunks_, m_->sms);
+  if (mode && flow_words_ && !any_lanes && !m_->tc_all) plan = flow_plan(m_->dm, n, max_chunks_, m_->sms);
   // DEFER_B200_LOOP=flow requires the dataflow kernel for the runs it can
   // take at all (position-parallel lanes and the tensor-core step are
   // other kernels by design)
-  if (mode == 2 && !plan.ok && !any_lanes && !(use_tc && n <= kTcM))
+  if (mode == 2 && !plan.ok && !any_lanes && !(use_tc && n <= kTcM) && !m_->tc_all)
     fail(kInvalidArgument, std::string("the dataflow token loop does not apply: ") +
                                (flow_words_ ? plan.why : "batch wider than its slot group"));
   FlowBufs fb{};
@@ -268,7 +268,11 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
     bt.trace_step = m_->dbg_trace_step;
   }
   bool tc = false;
-  if (use_tc && n <= kTcM && !any_lanes) {
+  if (m_->tc_all) {
+    // the model's arithmetic family: every run on the tensor-core step
+    if (n > kTcM) fail(kInvalidArgument, "runs of this model take at most 128 slots (tensor-core step)");
+    tc = true;
+  } else if (use_tc && n <= kTcM && !any_lanes) {
     // DEFER_B200_TC: 0 never, 1 whenever the run qualifies, default when the
     // hidden size makes the tensor cores pay off
     const char* e = getenv("DEFER_B200_TC");
@@ -547,7 +551,8 @@ Session* Session::checkout(const Model* m, const Checkpoint& ck, int cache_cap) 
     SlotProgram base = replay_program(ck, s->cache);
     base.want_margins = true;
     std::vector<SlotResult> res;
-    const int lanes = ck.prompt_len >= 1 ? replay_lanes(n) : 1;
+    int lanes = ck.prompt_len >= 1 ? replay_lanes(n) : 1;
+    if (m->tc_all) lanes = std::min(lanes, kTcM);  // one tensor-core tile of slots
     if (lanes <= 1) {
       std::vector<SlotProgram> progs(1, std::move(base));
       s->runner_->run(progs, res);
@@ -674,7 +679,14 @@ void replay_batch(Model* m, const std::vector<Checkpoint>& cks, int batch, bool 
   if (todo.empty()) return;
   if (batch <= 0) batch = 1;
   batch = std::min<int>(batch, (int)todo.size());
-  Runner runner(m, batch, cap);
+  // Tensor-core models replay position-parallel: the 128 slots of a tile
+  // are shared by the batch's sessions as lanes.
+  int lanes = 1;
+  if (m->tc_all) {
+    batch = std::min(batch, kTcM);
+    lanes = std::max(1, std::min(replay_lanes((size_t)cap), kTcM / batch));
+  }
+  Runner runner(m, batch * lanes, cap);
   std::vector<std::unique_ptr<KvCache>> caches;
   for (int b = 0; b < batch; b++) caches.emplace_back(cache_new(m, cap));
   EventPair ev;
@@ -682,9 +694,25 @@ void replay_batch(Model* m, const std::vector<Checkpoint>& cks, int batch, bool 
   for (size_t w = 0; w < todo.size(); w += batch) {
     const size_t nw = std::min<size_t>(batch, todo.size() - w);
     std::vector<SlotProgram> progs;
+    std::vector<int> first(nw), count(nw);  // each session's slots
     for (size_t b = 0; b < nw; b++) {
       caches[b]->len = 0;
-      progs.push_back(replay_program(cks[todo[w + b]], caches[b].get()));
+      const Checkpoint& ck = cks[todo[w + b]];
+      const int ln = (lanes > 1 && ck.prompt_len >= 1 && replay_lanes(ck.history_tokens.size()) > 1) ? lanes : 1;
+      first[b] = (int)progs.size();
+      count[b] = ln;
+      progs.push_back(replay_program(ck, caches[b].get()));
+      if (ln > 1) {
+        progs.back().lanes = ln;
+        for (int j = 1; j < ln; j++) {
+          SlotProgram p;
+          p.cache = caches[b].get();
+          p.verify = true;
+          p.lanes = ln;
+          p.lane = j;
+          progs.push_back(std::move(p));
+        }
+      }
     }
     std::vector<SlotResult> res;
     DEFER_CUDA(cudaEventRecord(ev.a, m->stream));
@@ -697,13 +725,21 @@ void replay_batch(Model* m, const std::vector<Checkpoint>& cks, int batch, bool 
     for (size_t b = 0; b < nw; b++) {
       ReplayOutcome& o = out[todo[w + b]];
       const Checkpoint& ck = cks[todo[w + b]];
-      if (res[b].div_step >= 0) {
+      SlotResult rb = res[first[b]];
+      for (int j = 1; j < count[b]; j++) {  // the first divergence in position order over the lanes
+        const SlotResult& rj = res[first[b] + j];
+        if (rj.div_step >= 0 && (rb.div_step < 0 || rj.div_step < rb.div_step)) {
+          rb.div_step = rj.div_step;
+          rb.div_token = rj.div_token;
+        }
+      }
+      if (rb.div_step >= 0) {
         o.status = kDivergence;
-        o.div_step = res[b].div_step;
-        o.div_token = res[b].div_token;
-        o.message = "replay sampled token " + std::to_string(res[b].div_token) + " at position " +
-                    std::to_string(res[b].div_step) + ", checkpoint recorded " +
-                    std::to_string(ck.history_tokens[res[b].div_step]);
+        o.div_step = rb.div_step;
+        o.div_token = rb.div_token;
+        o.message = "replay sampled token " + std::to_string(rb.div_token) + " at position " +
+                    std::to_string(rb.div_step) + ", checkpoint recorded " +
+                    std::to_string(ck.history_tokens[rb.div_step]);
       } else if (fingerprints) {
         cache_fingerprint(caches[b].get(), o.fingerprint);
       }
@@ -729,6 +765,7 @@ void generate_batch(Model* m, const std::vector<GenRequest>& reqs, int batch, st
   if (reqs.empty()) return;
   if (batch <= 0) batch = 1;
   batch = std::min<int>(batch, (int)reqs.size());
+  if (m->tc_all) batch = std::min(batch, kTcM);
   Runner runner(m, batch, cap);
   std::vector<std::unique_ptr<KvCache>> caches;
   for (int b = 0; b < batch; b++) caches.emplace_back(cache_new(m, cap));
@@ -835,6 +872,7 @@ void ablation_batch(Model* m, const uint32_t* context, size_t n, uint32_t target
   if (n_pos == 0) return;
   if (batch <= 0) batch = 1;
   batch = std::min<int>(batch, (int)n_pos);
+  if (m->tc_all) batch = std::min(batch, kTcM);
   Runner runner(m, batch, cap);
   runner.use_tc = true;
   std::vector<std::unique_ptr<KvCache>> caches;

@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <cerrno>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -411,6 +412,10 @@ Model* load_model(const std::string& path, int device) {
   for (auto& r : lr)
     for (const TensorRef* t : {r.wq, r.wk, r.wv, r.wo, r.wg, r.wu, r.wd}) all_bf16 = all_bf16 && t->dtype == DType::BF16;
   M->bf16 = all_bf16;
+  {
+    const char* e = getenv("DEFER_B200_TC");
+    M->tc_all = all_bf16 && c.hidden_size >= 2048 && !(e && e[0] == '0');
+  }
   const uint64_t E = M->bf16 ? 8 : 4;
   if (H % E || Q % E || FF % E)
     fail(kModel, "hidden, q and intermediate sizes must be multiples of " + std::to_string(E) + " on the B200 path");

@@ -29,6 +29,10 @@ struct Model {
   int device = 0;
   int sms = 0;
   bool bf16 = false;  // big matrices kept as bf16 in HBM
+  // Every token loop of this model runs on the tensor-core step (its
+  // arithmetic family): bf16-stored weights with hidden >= 2048, unless
+  // DEFER_B200_TC=0 at load.
+  bool tc_all = false;
   bool has_bias = false;
   void* arena = nullptr;
   size_t arena_bytes = 0;

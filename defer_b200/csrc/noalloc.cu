@@ -80,6 +80,9 @@ void forward_noalloc(Model* m, float* k_cache, float* v_cache, uint32_t cap, uin
                      float* logits_out, cudaStream_t st) {
   const DModel& d = m->dm;
   if (!k_cache || !v_cache || !logits_out) fail(kInvalidArgument, "cache and logits buffers must not be NULL");
+  if (m->tc_all)
+    fail(kInvalidArgument, "this model's token loop runs on the tensor cores; the allocation-free step computes "
+                           "on the CUDA cores and would not match it");
   if (cap == 0) fail(kInvalidArgument, "cache capacity must be positive");
   if (token >= (uint32_t)d.V) fail(kModel, "token id " + std::to_string(token) + " out of range");
   if (pos >= (uint32_t)d.max_seq) fail(kModel, "context length " + std::to_string(d.max_seq) + " exceeded");

@@ -131,6 +131,7 @@ struct TcGemmArgs {
   float* Y;                // [splits][kTcM][n_pad] partial sums
   int nkb, splits, n_pad, wterms;
   int* status;
+  const int* active;  // the step's "any slot active" flag, or null (always run)
 };
 
 __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ TcGemmArgs g) {
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (g.active && __ldcg(g.active) == 0) return;  // no slot fed a token this step
   const int tile = blockIdx.x / g.splits, sp = blockIdx.x % g.splits;
   const int kb0 = sp * g.nkb / g.splits, kb1 = (sp + 1) * g.nkb / g.splits;
   const int nk = kb1 - kb0;
@@ -293,8 +295,9 @@ __global__ void k_tc_pack_w(const void* W, int N, int K, int bf16, int nkb, int 
 // ((x * inv) * w, inv = 1 / sqrt(ss / K + eps) with ss a fixed-tree sum),
 // split into bf16 terms. Rows of slots >= B or not active are zero.
 __global__ void __launch_bounds__(256) k_tc_prep(const float* x, const float* nw, float eps, int K, int nkb, int B,
-                                                 const DSlotState* st, unsigned char* A) {
+                                                 const DSlotState* st, unsigned char* A, const int* active) {
   const int b = blockIdx.x, tid = threadIdx.x;
+  if (active && __ldcg(active) == 0) return;
   __shared__ float red[8];
   __shared__ float s_inv;
   const bool live = b < B && __ldcg(&st[b].active) != 0;
@@ -386,6 +389,24 @@ __global__ void k_tc_head_epi(DModel m, DBatch bt, const float* Y, int splits, i
   }
 }
 
+// Greedy block statistics of the new logits (a greedy SELECT reads them).
+__global__ void __launch_bounds__(kThreads) k_tc_stats(DModel m, DBatch bt) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = bt.nblk;
+  for (size_t u = (size_t)blockIdx.x * kPW + warp; u < (size_t)bt.B * nb; u += (size_t)gridDim.x * kPW) {
+    const int b = (int)(u / nb), k = (int)(u - (size_t)b * nb);
+    if (!live_slot(bt, b)) continue;
+    const int i = k * kSBlk + lane;
+    const bool valid = i < m.V;
+    const size_t o = (size_t)b * nb + k;
+    block_stats(valid ? ld_f(bt.logits + (size_t)b * m.V + i) : NAN, i, valid, bt.sess[b].temperature,
+                bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+  }
+}
+__global__ void __launch_bounds__(kThreads) k_tc_restat(DModel m, DBatch bt) {
+  ph_restat(m, bt, blockIdx.x, gridDim.x);
+}
+
 // The step's phases that stay on the CUDA cores.
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads) k_tc_select(DModel m, DBatch bt, int run_step) {
@@ -429,8 +450,8 @@ TcMatrix tc_pack(const void* W, int N, int K, bool bf16, unsigned char* out, cud
 size_t tc_act_bytes(int K) { return (size_t)div_up(K, kTcBK) * 2 * kTcABytes; }
 
 void tc_prep(const float* x, const float* nw, float eps, int K, int B, const DSlotState* st, unsigned char* A,
-             cudaStream_t s) {
-  k_tc_prep<<<kTcM, 256, 0, s>>>(x, nw, eps, K, div_up(K, kTcBK), B, st, A);
+             cudaStream_t s, const int* active) {
+  k_tc_prep<<<kTcM, 256, 0, s>>>(x, nw, eps, K, div_up(K, kTcBK), B, st, A, active);
   DEFER_CUDA(cudaGetLastError());
 }
 
@@ -451,7 +472,8 @@ static bool first_on_device(unsigned long long& mask) {
   return true;
 }
 
-void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s) {
+void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s,
+             const int* active) {
   static unsigned long long attr = 0;
   const int smem = kTcStages * kTcStageBytes;
   if (first_on_device(attr))
@@ -465,6 +487,7 @@ void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, in
   g.n_pad = w.ntile * kTcBN;
   g.wterms = w.wterms;
   g.status = status;
+  g.active = active;
   k_tc_gemm<<<w.ntile * splits, kTcThreads, smem, s>>>(g);
   DEFER_CUDA(cudaGetLastError());
 }
@@ -487,35 +510,40 @@ void launch_steps_tc(const DModel& m, const TcModel& tm, const DBatch& bt0, int 
   if (smem > 200 * 1024) fail(kInvalidArgument, "tensor-core step: phase shared memory too large");
   const int attn_units = bt.B * m.NKV * bt.max_chunks;
   const int ew = std::min(sms * 8, 4096);  // epilogue grid
+  const int nb = bt.nblk;
+  // statistics of the resident logits for slots whose first step samples
+  k_tc_restat<<<std::min(sms, std::max(1, nb / kPW)), kThreads, 0, st>>>(m, bt);
   for (int s = 0; s < nsteps; s++) {
     if (m.bf16) k_tc_select<true><<<bt.B, kThreads, smem, st>>>(m, bt, s);
     else k_tc_select<false><<<bt.B, kThreads, smem, st>>>(m, bt, s);
+    const int* act = bt.any_active + (s & 1);  // set by this step's SELECT
     for (int l = 0; l < m.L; l++) {
       const TcLayer& T = tm.layers[l];
-      tc_prep(bt.x, T.attn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st);
-      tc_gemm(wk.A, T.qkv, wk.Y, T.s_qkv, bt.status, st);
+      tc_prep(bt.x, T.attn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st, act);
+      tc_gemm(wk.A, T.qkv, wk.Y, T.s_qkv, bt.status, st, act);
       k_tc_qkv_epi<<<ew, 256, 0, st>>>(m, bt, l, wk.Y, T.s_qkv, T.qkv.ntile * kTcBN);
       k_tc_attn<<<std::min(attn_units, sms * 8), kThreads, smem, st>>>(m, bt, l);
       k_tc_combine<<<sms, kThreads, 0, st>>>(m, bt);
-      tc_prep(bt.att, nullptr, 0.0f, m.QD, bt.B, bt.st, wk.A, st);
-      tc_gemm(wk.A, T.o, wk.Y, T.s_o, bt.status, st);
+      tc_prep(bt.att, nullptr, 0.0f, m.QD, bt.B, bt.st, wk.A, st, act);
+      tc_gemm(wk.A, T.o, wk.Y, T.s_o, bt.status, st, act);
       k_tc_resid<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_o, T.o.ntile * kTcBN);
-      tc_prep(bt.x, T.ffn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st);
-      tc_gemm(wk.A, T.gu, wk.Y, T.s_gu, bt.status, st);
+      tc_prep(bt.x, T.ffn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st, act);
+      tc_gemm(wk.A, T.gu, wk.Y, T.s_gu, bt.status, st, act);
       k_tc_gu_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_gu, T.gu.ntile * kTcBN);
-      tc_prep(bt.g, nullptr, 0.0f, m.FF, bt.B, bt.st, wk.A, st);
-      tc_gemm(wk.A, T.down, wk.Y, T.s_down, bt.status, st);
+      tc_prep(bt.g, nullptr, 0.0f, m.FF, bt.B, bt.st, wk.A, st, act);
+      tc_gemm(wk.A, T.down, wk.Y, T.s_down, bt.status, st, act);
       k_tc_resid<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_down, T.down.ntile * kTcBN);
     }
-    tc_prep(bt.x, m.norm, m.eps, m.H, bt.B, bt.st, wk.A, st);
-    tc_gemm(wk.A, tm.head, wk.Y, tm.s_head, bt.status, st);
+    tc_prep(bt.x, m.norm, m.eps, m.H, bt.B, bt.st, wk.A, st, act);
+    tc_gemm(wk.A, tm.head, wk.Y, tm.s_head, bt.status, st, act);
     k_tc_head_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, tm.s_head, tm.head.ntile * kTcBN);
+    k_tc_stats<<<std::min(sms * 4, std::max(1, bt.B * nb / kPW)), kThreads, 0, st>>>(m, bt);
   }
   k_tc_finalize<<<bt.B, kThreads, 0, st>>>(bt);
   DEFER_CUDA(cudaGetLastError());
 }
 
-int launches_per_step_tc(const DModel& m) { return 3 + 12 * m.L; }
+int launches_per_step_tc(const DModel& m) { return 4 + 12 * m.L; }
 
 void tc_gemm_check(int device, const float* X, int M, const float* W, int N, int K, bool w_bf16, float* Y) {
   if (M < 1 || M > kTcM || N < 1 || K < 1) fail(kInvalidArgument, "tensor-core GEMM check: bad shape");

@@ -60,9 +60,11 @@ int tc_splits(const TcMatrix& w, int sms);
 size_t tc_y_floats(const TcMatrix& w, int splits);
 // A [128 slots][K] operand from x ([B][K]), RMS-normalised by nw when non-null.
 void tc_prep(const float* x, const float* nw, float eps, int K, int B, const DSlotState* st, unsigned char* A,
-             cudaStream_t s);
+             cudaStream_t s, const int* active = nullptr);
 // Y[split][slot][n] partial sums of A . W^T.
-void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s);
+// With `active` (a device flag) the launch does nothing when it is 0.
+void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s,
+             const int* active = nullptr);
 
 // Runs nsteps token steps of a batch of at most 128 slots whose programs
 // never sample, the projections on the tensor cores.
