@@ -692,11 +692,14 @@ def main(argv=None):
     ap.add_argument("--no-config5", action="store_true", help="skip config 5 (8B shape, 8 replayed sessions)")
     ap.add_argument("--no-ablation", action="store_true",
                     help="skip config 4 (1.7B-shape leave-one-out attribution, 127 variants)")
-    ap.add_argument("--profile-case", nargs="?", const="single", choices=["single", "batched"],
+    ap.add_argument("--profile-case", nargs="?", const="single", choices=["single", "batched", "ablation", "tc-gemm"],
                     help="no measurement: a small case for profiles. single: the 135M model, 16-token "
                          "prompt, then one launch of 32 sampled tokens (dataflow kernel). batched: "
                          "--profile-slots sessions with --profile-prompt prompts and 2 sampled tokens "
-                         "in one batch on the per-stage launch path (one kernel per stage)")
+                         "in one batch on the per-stage launch path (one kernel per stage). ablation: "
+                         "config 4's leave-one-out attribution on the 1.7B shape over a 24-token "
+                         "context (tensor-core step). tc-gemm: three tensor-core GEMMs of 128 slots x "
+                         "the 1.7B shape's gate/up matrix (16384 x 2048, fp32 weights)")
     ap.add_argument("--profile-slots", type=int, default=512)
     ap.add_argument("--profile-prompt", type=int, default=128)
     ap.add_argument("--trace", action="store_true",
@@ -710,6 +713,10 @@ def main(argv=None):
         return profile_trace(a.profile_prompt, a.trace_out)
     if a.profile_case == "batched":
         return profile_case_batched(a.profile_slots, a.profile_prompt)
+    if a.profile_case == "ablation":
+        return profile_case_ablation()
+    if a.profile_case == "tc-gemm":
+        return profile_case_tc_gemm()
     if a.profile_case:
         return profile_case()
     return run_b200(a)
@@ -730,6 +737,31 @@ def profile_case():
     return 0
 
 
+def profile_case_ablation():
+    """Config 4's attribution on the 1.7B shape over a 24-token context."""
+    import numpy as np
+    import defer_b200 as D
+    from defer_b200 import synthetic
+    m = D.Model.load(synthetic.model_path("smollm2-1.7b", model_dir(), 0))
+    ctx = [int(t) for t in np.random.default_rng(4).integers(0, m.config.vocab_size, 24)]
+    base, _ = D.ablation_attribution(m, ctx, ctx[-1], list(range(len(ctx) - 1)))
+    print(json.dumps({"profile_case": "ablation", "base_logprob": base, **m.timing()}))
+    return 0
+
+
+def profile_case_tc_gemm():
+    """Three tensor-core GEMMs: 128 slots x the 1.7B gate/up matrix."""
+    import numpy as np
+    import defer_b200 as D
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((128, 2048)).astype(np.float32)
+    w = (rng.standard_normal((16384, 2048)) * 0.02).astype(np.float32)
+    for _ in range(3):
+        y = D.tc_gemm(x, w)
+    print(json.dumps({"profile_case": "tc-gemm", "checksum": float(np.abs(y).sum())}))
+    return 0
+
+
 STAGE_KINDS = ("qkv", "attn", "o", "gateup", "down")
 
 
@@ -747,7 +779,9 @@ def trace_summary(tr, L: int):
     last finish over CTAs; span = end(k) - end(p) (its share of the step);
     handoff = a CTA's receipt minus end(p) (last producer store to the
     consumer holding every input); compute = a CTA's last warp finish minus
-    its receipt; tail = end(k) minus the median CTA's finish."""
+    its receipt; tail = end(k) minus the median CTA's finish. `select`: the
+    sampling CTAs' time to poll the previous logits' statistics, to sample,
+    and to finish the stage, from their entry."""
     import numpy as np
     tr = np.asarray(tr, dtype=np.int64)
     names = stage_names(L)
@@ -776,8 +810,8 @@ def trace_summary(tr, L: int):
         kind = name.rstrip("0123456789")
         r = rows.setdefault(kind, {"n": 0, "span": [], "handoff_med": [], "handoff_max": [], "compute_med": [],
                                    "compute_max": [], "tail": [], "ctas": [], "mark10": [], "mark11": [],
-                                   "mark12": [], "mark13": []})
-        for mk in (10, 11, 12, 13):  # warp 0's sub-stage marks, from the receipt
+                                   "mark12": [], "mark13": [], "mark14": [], "mark15": []})
+        for mk in (10, 11, 12, 13, 14, 15):  # warp 0's sub-stage marks, from the receipt
             ok = part & (tr[:, k, mk] > 0)
             if ok.any():
                 r[f"mark{mk}"].append(float(np.median((tr[ok, k, mk] - recv[ok, k]) / 1e3)))
@@ -793,6 +827,17 @@ def trace_summary(tr, L: int):
     for kind, r in rows.items():
         out[kind] = {"stages": r["n"], **{key: round(float(np.mean(v)), 3) for key, v in r.items()
                                           if key != "n" and len(v)}}
+    own = (tr[:, 0, 11] > 0) & (tr[:, 0, 10] > 0)  # CTAs that sampled a slot's token in SELECT
+    if own.any():
+        sel = tr[own, 0, :]
+        out["select"] = {"ctas": int(own.sum()),
+                         "inputs_polled": round(float(np.median(sel[:, 10] - sel[:, 0])) / 1e3, 3),
+                         "sampler": round(float(np.median(sel[:, 11] - sel[:, 10])) / 1e3, 3),
+                         "sum_rows": round(float(np.median(sel[:, 12] - sel[:, 10])) / 1e3, 3),
+                         "sum_walk": round(float(np.median(sel[:, 13] - sel[:, 12])) / 1e3, 3),
+                         "cdf_rows": round(float(np.median(sel[:, 14] - sel[:, 13])) / 1e3, 3),
+                         "cdf_walk": round(float(np.median(sel[:, 15] - sel[:, 14])) / 1e3, 3),
+                         "done": round(float(np.median(done[own, 0] - sel[:, 0])) / 1e3, 3)}
     t0 = tr[:, 0, 0][tr[:, 0, 0] > 0].min() if (tr[:, 0, 0] > 0).any() else 0
     last = int(max(i for i in range(len(names)) if ends[i] > 0))
     return {"step_us": round((ends[last] - t0) / 1e3, 3), "last_stage": names[last], "per_kind_us": out}

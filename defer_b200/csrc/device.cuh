@@ -24,13 +24,10 @@
 //    out = O / L.
 //  * SiLU/GeLU, residual add: no contraction, ops.rs:120-156 order.
 //  * sampler (sampler.rs:24-109): argmax exact (NaN skipped, lowest index on
-//    ties); s = l / T, M = max s, e = expf(s - M), Z = sum of e, p = e * (1/Z).
-//    Every sum is hierarchical and sequential at each level: 32 elements per
-//    block, 32 blocks per group, 32 groups per supergroup, then supergroups.
-//    The CDF at element i is Q3 + (Q2 + (Q1 + t)) with Q3/Q2/Q1 the
-//    sequential prefixes of the supergroup / group / block sums before i and
-//    t the sequential prefix inside i's block, so it is monotone and its
-//    value at every block / group / supergroup end equals the running total.
+//    ties); s = l / T, M = max s, e = expf(s - M), Z = e_0 + e_1 + ... and
+//    the CDF over p = e * (1/Z) as the reference's sequential fp32 sums,
+//    reproduced bit for bit by integer runs inside one binade (phases.cuh,
+//    exact sampler); only expf itself may differ from the reference's libm.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -152,9 +149,12 @@ struct DBatch {
 
 // Trace record of one stage of one CTA (dataflow kernel): slot 0 = stage
 // entry, 1 = inputs received (after the poll), 2 + w = warp w done; warp 0
-// also marks 10 = RMS statistic ready / attention rows staged, 11 = first
-// weight piece in shared memory / attention scores done, 12 = attention
-// softmax done, 13 = attention weighted sum done.
+// also marks 10 = RMS statistic ready / attention rows staged / sampler
+// inputs polled, 11 = first weight piece in shared memory / attention
+// scores done / token sampled, 12 = attention softmax done / sampler sum
+// rows ready, 13 = attention weighted sum done / sum walked, 14 = attention
+// units done / sampler CDF rows ready, 15 = attention combines done / CDF
+// walked.
 constexpr int kTraceSlots = 16;
 
 }  // namespace defer

@@ -347,7 +347,7 @@ void Runner::run(std::vector<SlotProgram>& progs, std::vector<SlotResult>& resul
   bytes += (double)steps_run * (double)m_->weight_bytes;
   m_->t_device_ms += ms;
   m_->t_runs += 1;
-  m_->t_launches += tc ? (uint64_t)nsteps * (uint64_t)launches_per_step_tc(d) + 1
+  m_->t_launches += tc ? (uint64_t)nsteps * (uint64_t)launches_per_step_tc(d) + 2  // + restat, finalize
                        : persistent ? 1 : (uint64_t)nsteps * (uint64_t)launches_per_step_phased(d) + 1;
   m_->t_tokens += tokens;
   m_->t_bytes += bytes;

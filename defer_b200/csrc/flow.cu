@@ -159,6 +159,28 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
                : "memory");
 }
 
+// The same with an L2 eviction policy (createpolicy): the layers' weights
+// pass through L2 once per token and go first; lm_head rows are kept, so
+// that across tokens they are read from L2 rather than HBM.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, unsigned bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Ampere-style asynchronous 16-byte copy global -> shared (no registers).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -207,6 +229,21 @@ __device__ __forceinline__ void producer_fail(FlowShared& sh, int* status) {
 }
 
 // ------------------------------------------------------------------ polls
+// A wait longer than a hand-off (the token choice of SELECT, attention on a
+// few CTAs) would otherwise keep every thread of every waiting CTA
+// re-reading the same few L2 lines, which slows the CTAs doing the work.
+// Past kPollSpinNs of waiting a thread sleeps a quarter of the time it has
+// waited beyond that between rounds (at most kPollSleepMaxNs), so a long
+// wait is noticed at most ~25 % late and a short one not at all.
+constexpr unsigned long long kPollSpinNs = 1500;
+constexpr unsigned long long kPollSleepMaxNs = 1000;
+__device__ __forceinline__ void poll_backoff(unsigned long long waited) {
+  if (waited > kPollSpinNs) {
+    const unsigned long long t = (waited - kPollSpinNs) >> 2;
+    __nanosleep((unsigned)(t < kPollSleepMaxNs ? t : kPollSleepMaxNs));
+  }
+}
+
 // One polled region: `rows` rows (only those with (mask >> r) & 1) of n
 // words each, row r at src + r * sstride, its values to dst + r * dstride.
 struct Seg {
@@ -271,15 +308,17 @@ __device__ __forceinline__ bool poll_pairs(const Seg& s, FlowShared& sh, int* st
           }
         }
       }
-      if (pend && (++spins & 31u) == 0) {
-        if (failed(sh) || status_now(status) != kStOk) {
+      if (pend) {
+        const unsigned long long el = now_ns() - t0;
+        if ((++spins & 31u) == 0 && (failed(sh) || status_now(status) != kStOk)) {
           flag_fail(sh, status, kStOk);
           return false;
         }
-        if (now_ns() - t0 > sh.wait_ns) {
+        if (el > sh.wait_ns) {
           flag_fail(sh, status, kStTimeout);
           return false;
         }
+        poll_backoff(el);
       }
     }
   }
@@ -339,17 +378,19 @@ __device__ __forceinline__ void poll(const Seg& s, bool acquire, FlowShared& sh,
           pend &= ~(1u << k);
         }
       }
-      if (pend && (++spins & 31u) == 0) {
-        if (failed(sh) || status_now(status) != kStOk) {
+      if (pend) {
+        const unsigned long long el = now_ns() - t0;
+        if ((++spins & 31u) == 0 && (failed(sh) || status_now(status) != kStOk)) {
           flag_fail(sh, status, kStOk);
           ok = false;
           break;
         }
-        if (now_ns() - t0 > sh.wait_ns) {
+        if (el > sh.wait_ns) {
           flag_fail(sh, status, kStTimeout);
           ok = false;
           break;
         }
+        poll_backoff(el);
       }
     }
   }
@@ -452,6 +493,7 @@ __device__ Slice slice_of(const DModel& m, const DLayer* ly, int nblk, int kind,
 __device__ void produce(const DModel& m, const DLayer* ly, int nblk, Ring& rg, FlowShared& sh, int nsteps, int cta,
                         int ncta, int* status) {
   bool stopped = false;
+  const uint64_t pol_layer = policy_evict_first(), pol_head = policy_evict_last();
   for (int s = 0; s < nsteps && !stopped; s++) {
     for (int l = 0; l <= m.L && !stopped; l++) {
       const int nk = l < m.L ? 4 : 1;
@@ -479,7 +521,8 @@ __device__ void produce(const DModel& m, const DLayer* ly, int nblk, Ring& rg, F
           }
           const unsigned bytes = (unsigned)(n * sl.rb);
           mbar_expect_tx(&rg.full[slot], bytes);
-          bulk_g2s(rg.base + (size_t)slot * rg.slot_bytes, sl.src + (size_t)done * sl.rb, bytes, &rg.full[slot]);
+          bulk_g2s_hint(rg.base + (size_t)slot * rg.slot_bytes, sl.src + (size_t)done * sl.rb, bytes, &rg.full[slot],
+                        l < m.L ? pol_layer : pol_head);
           rg.p++;
           done += n;
         }
@@ -867,7 +910,17 @@ struct Flow {
                     true);
             csync_();
             if (fail()) return false;
-            smp = sample_exact(bt.logits + (size_t)b * m.V, m.V, T, S.words[k], &margin, stage);
+            // M = the largest of the CTAs' maxima of s
+            float mx = -INFINITY;
+            for (int j = tid; j < ncta; j += kPT) mx = fmaxf(mx, stage[j]);
+            mx = cta_max(mx);
+            tr_mark(10);
+            const float* rm = reinterpret_cast<const float*>(fb.esum) + (size_t)b * 2 * nblk;
+            unsigned long long* mk =
+                (bt.trace && s == bt.trace_step) ? bt.trace + (size_t)cta * KS * kTraceSlots + 12 : nullptr;
+            smp = sample_exact(bt.logits + (size_t)b * m.V, m.V, T, S.words[k], &margin, stage, true, mx, rm,
+                               rm + nblk, mk);
+            tr_mark(11);
           } else {
             float* pr = stage;
             float* lm = stage + 2 * ncta;
@@ -1212,6 +1265,7 @@ struct Flow {
       csync_();
       if (u == cta) tr_mark(13);
     }
+    tr_mark(14);
     // Combine per (slot, query head), chunks in order.
     for (int bh = 0; bh < bt.B * m.NH; bh++) {
       if ((units + bh) % ncta != cta) continue;
@@ -1239,6 +1293,7 @@ struct Flow {
       }
       csync_();
     }
+    tr_mark(15);
     tr_done(s, sid_att(l));
     return true;
   }
@@ -1271,7 +1326,7 @@ struct Flow {
     if (fail()) return false;
     tr_recv(s, sid_gu(l));
     const uint32_t tg = tag(s, sid_gu(l));
-    gemv<true>(sl, stage, m.H, m.H, kEpiGateUp, l, tg);
+    gemv<true, 4>(sl, stage, m.H, m.H, kEpiGateUp, l, tg);  // ~20 rows a CTA: one pass of 4 rows a warp
     tr_done(s, sid_gu(l));
     return true;
   }
@@ -1325,7 +1380,16 @@ struct Flow {
         const float T = sh.sess[g].temperature;
         float sv = -INFINITY;
         if (valid && T != 0.0f) sv = __fdiv_rn(l, T);
-        smx[g] = fmaxf(smx[g], warp_max(sv));
+        const float mr = warp_max(sv);
+        smx[g] = fmaxf(smx[g], mr);
+        if (T != 0.0f) {  // the row's statistics that steer the exact sampler's walk
+          const float z = row_expsum(sv, valid, mr);
+          if (lane == 0) {
+            float* rm = reinterpret_cast<float*>(fb.esum) + (size_t)g * 2 * nblk;
+            rm[k] = mr;
+            rm[nblk + k] = z;
+          }
+        }
       }
     }
     if (lane == 0) {
@@ -1339,10 +1403,10 @@ struct Flow {
     csync_();
     if (threadIdx.x < G && ((slots >> threadIdx.x) & 1u)) {
       const int g = threadIdx.x;
-      // the CTA's logits stores (before the barrier) happen before these
-      // words: a sampling SELECT polls them with an acquire, then reads
-      // the logits
-      if (store) fence_release_gpu();
+      // the CTA's logits and row-statistics stores (before the barrier)
+      // happen before these words: a sampling SELECT polls them with an
+      // acquire, then reads both
+      fence_release_gpu();
       ValIdx b{NAN, INT_MAX};
       float sm = -INFINITY;
       for (int w = 0; w < kPW; w++) {

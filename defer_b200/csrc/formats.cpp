@@ -94,7 +94,9 @@ void Checkpoint::save(const std::string& path) const {
   std::string tmp = path;
   size_t slash = tmp.find_last_of('/');
   size_t dot = tmp.find_last_of('.');
-  if (dot != std::string::npos && (slash == std::string::npos || dot > slash + 1)) tmp = tmp.substr(0, dot);
+  // a leading dot starts the name, not an extension (".hidden" -> ".hidden.ckpt.tmp")
+  const size_t name0 = slash == std::string::npos ? 0 : slash + 1;
+  if (dot != std::string::npos && dot > name0) tmp = tmp.substr(0, dot);
   tmp += ".ckpt.tmp";
   std::vector<uint8_t> b = to_bytes();
   FILE* f = fopen(tmp.c_str(), "wb");

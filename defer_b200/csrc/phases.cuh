@@ -84,6 +84,18 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Max over the CTA's phase threads (every thread gets it). Whole CTA.
+__device__ __forceinline__ float cta_max(float v) {
+  __shared__ float s_w[kPW];
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) s_w[threadIdx.x >> 5] = v;
+  DEFER_CTA_SYNC();
+  float r = -INFINITY;
+  for (int w = 0; w < kPW; w++) r = fmaxf(r, s_w[w]);
+  DEFER_CTA_SYNC();
+  return r;
+}
+
 // Sequential sum of the 32 lane values in lane order (all lanes get it).
 __device__ __forceinline__ float warp_seq_sum(float v) {
   float s = 0.0f;
@@ -524,19 +536,31 @@ __device__ __forceinline__ float e_of(float l, float T, float M) {
   return isnan(s) ? 0.0f : expf(__fsub_rn(s, M));
 }
 
+// Sum over the warp of exp(s - mr) (0 for NaN s or an empty row): with the
+// row's max mr, the statistics that steer the exact sampler's walk (their
+// rounding is free).
+__device__ __forceinline__ float row_expsum(float s, bool valid, float mr) {
+  float z = (valid && !isnan(s) && mr > -INFINITY) ? expf(__fsub_rn(s, mr)) : 0.0f;
+  for (int off = 16; off > 0; off >>= 1) z += __shfl_xor_sync(0xffffffffu, z, off);
+  return z;
+}
+
 // Warp statistics of one 32-element block held one value per lane
-// (`valid` false past the vocabulary): raw argmax and max of s = l / T.
+// (`valid` false past the vocabulary): raw argmax, max of s = l / T and,
+// when T != 0, the sum of exp(s - max).
 __device__ __forceinline__ void block_stats(float l, int idx, bool valid, float T, float* lmax, int* larg,
-                                            float* smax) {
+                                            float* smax, float* zsum) {
   ValIdx me{l, (valid && !isnan(l)) ? idx : INT_MAX};
   ValIdx best = vi_warp_best(me);
   float s = -INFINITY;
   if (valid && T != 0.0f) s = __fdiv_rn(l, T);
-  s = warp_max(s);  // fmaxf skips NaN
+  const float mr = warp_max(s);  // fmaxf skips NaN
+  const float z = T != 0.0f ? row_expsum(s, valid, mr) : 0.0f;
   if ((threadIdx.x & 31) == 0) {
     *lmax = best.v;
     *larg = best.i;
-    *smax = s;
+    *smax = mr;
+    *zsum = z;
   }
 }
 
@@ -580,180 +604,340 @@ static __device__ uint32_t argmax_from_blocks(const float* lmax, const int* larg
 // [2^e, 2^(e+1)), every fp32 addition S + v rounds to the grid u = 2^(e-23),
 // so S advances by q u with q the integer nearest v / u (a tie goes to the
 // even multiple, so it depends on the parity of S / u): an integer sum,
-// until S reaches 2^(e+1). Each thread owns a contiguous chunk; from fp64
-// chunk sums it predicts the binade its chunk runs in and computes the
-// chunk's integer increment for an even and for an odd incoming multiple.
-// Warp 0 then walks the chunks in order with the exact S: a chunk whose
-// prediction holds and that stays below the next power of two advances S by
-// its increment; any other chunk (the first one, where S starts at 0, and
-// those in which S crosses a power of two) is added element by element in
-// fp32 by one lane. The result equals the sequential sum bit for bit, for
-// any chunking. (e_i uses CUDA's expf; the reference's libm may differ in
-// the last bit of some e_i.)
+// until S reaches 2^(e+1). The values are cut into rows of 32 consecutive
+// values and blocks of 32 rows. From approximate prefix
+// sums every row gets a predicted binade and, under it, its integer
+// increment for an even and for an odd incoming multiple; blocks compose
+// their rows' increments when all share one binade. Warp 0 then walks the
+// blocks in order with the exact S, 32 items at a time: each lane composes
+// the increments of the items up to its own and checks that they run in
+// S's binade and stay below the next power of two; S jumps to the last
+// item before the first that fails, and that item is descended into
+// (block -> rows -> values; a value is added in fp32). A prediction only
+// decides how far S jumps, never its value, so the result equals the
+// sequential sum bit for bit. (e_i uses CUDA's expf; the reference's libm
+// may differ in the last bit of some e_i.)
 
-constexpr int kNoBinade = INT_MIN;
+__device__ __forceinline__ unsigned long long gtimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr int kNoBinade = INT_MIN;       // no prediction: the item is descended into
+constexpr int kAnyBinade = INT_MIN + 1;  // all values zero: S unchanged in any binade
+constexpr int kStashRows = 32;           // rows without a prediction kept in shared memory
 
 __device__ __forceinline__ int binade_of(float s) { return ((__float_as_int(s) >> 23) & 0xFF) - 127; }
 __device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }  // -126 <= k <= 127
+// Binade of a running sum in which the integer steps apply (u and 2^24 u
+// normal numbers), else kNoBinade (S = 0, tiny, huge or not finite).
+__device__ __forceinline__ int walk_binade(float s) {
+  if (!(s > 0.0f) || !isfinite(s)) return kNoBinade;
+  const int e = binade_of(s);
+  return e >= -102 && e <= 100 ? e : kNoBinade;
+}
 
 // v_i of one exact pass: e_i (Z) or p_i = e_i * inv (CDF).
 struct SampleVals {
   const float* lg;
   float T, M, inv;
   bool p;
-  __device__ __forceinline__ float operator()(int i) const {
-    const float e = e_of(ld_f(lg + i), T, M);
+  __device__ __forceinline__ float raw(int i) const { return ld_f(lg + i); }
+  __device__ __forceinline__ float of(float l) const {
+    const float e = e_of(l, T, M);
     return p ? __fmul_rn(e, inv) : e;
   }
+  __device__ __forceinline__ float operator()(int i) const { return of(raw(i)); }
 };
 
-// Shared memory of sample_exact: fp64 chunk prefix, chunk binades and
-// increments, one chunk's values for an element-wise walk.
+// Shared memory of sample_exact (floats): per row its sum, prefix, binade
+// and two increments; per block the same but the sum; the stashed rows;
+// one [32][9] transposition tile per warp.
 __host__ __device__ __forceinline__ size_t sample_exact_floats(int V) {
-  const int c = (V + kPT - 1) / kPT;
-  return (size_t)2 * (kPT + 2) + 3 * kPT + c + 8;
+  const size_t R = (size_t)(V + 31) / 32, NB = (R + 31) / 32;
+  return 5 * R + 4 * NB + 32 * (size_t)kStashRows + (size_t)kPW * 32 * 9 + 8;
 }
 
-// The sequential fp32 sum of v(0..n) (find < 0), or with find >= 0 the CDF
-// search: the first i with v_i > 0 and r < S_{i+1}; returns S (sum) or the
-// index (-1 when r is never below the CDF), with *prev / *at the CDF before
-// and at that index. Whole CTA.
-static __device__ float exact_seq(const SampleVals& v, int n, bool find, float r, int* found, float* prev, float* at,
-                                  float* smem) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  double* pre = reinterpret_cast<double*>(smem);
-  int* pe = reinterpret_cast<int*>(smem + 2 * (kPT + 2));
-  int* d0 = pe + kPT;
-  int* d1 = d0 + kPT;
-  float* walk = reinterpret_cast<float*>(d1 + kPT);
-  const int c = (n + kPT - 1) / kPT;
-  const int i0 = min(n, tid * c), i1 = min(n, i0 + c);
-  __shared__ float s_res;
-  __shared__ int s_found;
-  __shared__ float s_prev, s_at;
-  // chunk sums (fp64)
-  double sum = 0.0;
-  for (int i = i0; i < i1; i++) sum += (double)v(i);
-  pre[tid + 1] = sum;
-  DEFER_CTA_SYNC();
-  if (tid < 32) {  // exclusive prefix over the chunks (warp 0)
-    const int per = (kPT + 31) / 32;
-    double loc = 0.0;
-    for (int j = 0; j < per; j++) {
-      const int k = lane * per + j;
-      if (k < kPT) loc += pre[k + 1];
+// Increments of a run of values in binade e (multiples of u = 2^(e-23)):
+// d0 for an even incoming multiple, d1 for an odd one; saturate at 2^26.
+struct Incr {
+  int d0, d1;
+};
+// Run a, then run b (one binade).
+__device__ __forceinline__ Incr incr_then(Incr a, Incr b) {
+  Incr c;
+  c.d0 = min(a.d0 + ((a.d0 & 1) ? b.d1 : b.d0), 1 << 26);
+  c.d1 = min(a.d1 + (((1 + a.d1) & 1) ? b.d1 : b.d0), 1 << 26);
+  return c;
+}
+// One value v >= 0 in binade e: q = v / u rounded to nearest; a tie takes
+// the even total.
+__device__ __forceinline__ Incr value_incr(float v, int e, bool* tie) {
+  const float x = __fmul_rn(v, pow2f(23 - e));  // exact: a power-of-two scale
+  *tie = false;
+  if (!(x < 33554432.0f)) return Incr{1 << 25, 1 << 25};  // leaves the binade (or NaN)
+  const float f = floorf(x);
+  const float fr = __fsub_rn(x, f);
+  const int fl = (int)f;
+  if (fr == 0.5f) {
+    *tie = true;
+    return Incr{fl + (fl & 1), fl + ((fl + 1) & 1)};
+  }
+  const int q = fl + (fr > 0.5f ? 1 : 0);
+  return Incr{q, q};
+}
+
+// One level of the walk, by warp 0: lane j holds item j (its binade and
+// increments). S advances over items j0, j0 + 1, ... < n while each item is
+// all zeros or runs in S's binade, S stays below the next power of two and
+// (searching) r >= S. Returns the first item that stops it (n if none),
+// with S the exact sum before that item.
+__device__ __forceinline__ int walk_level(float& S, int j0, int n, int e, Incr d, bool find, float r) {
+  const int lane = threadIdx.x & 31;
+  const bool in = lane >= j0 && lane < n;
+  const int eS = walk_binade(S);
+  const bool ok = e == kAnyBinade || (eS != kNoBinade && e == eS);
+  Incr t = (in && ok && e != kAnyBinade) ? d : Incr{0, 0};
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const Incr o{__shfl_up_sync(0xffffffffu, t.d0, off), __shfl_up_sync(0xffffffffu, t.d1, off)};
+    if (lane >= off) t = incr_then(o, t);
+  }
+  float Sj = S;
+  bool stop = !ok;
+  if (eS != kNoBinade) {
+    const int M = (int)__fmul_rn(S, pow2f(23 - eS));
+    const int dd = (M & 1) ? t.d1 : t.d0;
+    if (M + dd >= (1 << 24)) stop = true;
+    else Sj = __fmul_rn((float)(M + dd), pow2f(eS - 23));
+  }
+  if (find && r < Sj) stop = true;
+  const unsigned sm = __ballot_sync(0xffffffffu, in && stop);
+  const int f = sm ? __ffs(sm) - 1 : n;
+  const float Sb = __shfl_sync(0xffffffffu, Sj, f > 0 ? min(f, 32) - 1 : 0);
+  if (f > j0) S = Sb;
+  return f;
+}
+
+// One row value by value (v = this lane's value, base = index of lane 0):
+// integer runs in S's binade, fp32 additions where they stop. True when the
+// walk ends here (the CDF hit, or a sum that is no longer finite).
+__device__ __forceinline__ bool walk_values(float& S, float& P, int& hit, float v, int base, bool find, float r) {
+  int j0 = 0;
+  for (int round = 0; round <= 32; round++) {  // every round consumes a value
+    const int eS = walk_binade(S);
+    bool tie;
+    const Incr d = eS != kNoBinade ? value_incr(v, eS, &tie) : Incr{0, 0};
+    const int e = v == 0.0f ? kAnyBinade : (eS != kNoBinade ? eS : kNoBinade);
+    const int f = walk_level(S, j0, 32, e, d, find, r);
+    if (f >= 32) return false;
+    const float vf = __shfl_sync(0xffffffffu, v, f);
+    const float Sp = S;
+    S = __fadd_rn(S, vf);
+    if (find && vf > 0.0f && r < S) {
+      hit = base + f;
+      P = Sp;
+      return true;
     }
-    double incl = loc;
+    if (!isfinite(S)) return true;
+    j0 = f + 1;
+  }
+  return false;
+}
+
+// The sequential fp32 sum of v(0..n) (find = false), or the CDF search
+// (find = true): the first i with v_i > 0 and r < S_{i+1}, reported with
+// the CDF before and at it; S is returned either way (the total when not
+// found). smem[0..R) holds the rows' sums on entry (they only steer the
+// walk, so any rounding will do).
+static __device__ float exact_seq(const SampleVals& v, int n, bool find, float r, int* found, float* prev,
+                                  float* at, float* smem, unsigned long long* marks = nullptr) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = (n + 31) / 32, NB = (R + 31) / 32;
+  float* rs = smem;                                // [R] row sums
+  float* rp = rs + R;                              // [R] row prefix
+  int* re = reinterpret_cast<int*>(rp + R);        // [R] row binade
+  int* rd0 = re + R;                               // [R] (stash slot of an unpredicted row)
+  int* rd1 = rd0 + R;                              // [R]
+  int* be = rd1 + R;                               // [NB] block binade
+  int* bd0 = be + NB;                              // [NB]
+  int* bd1 = bd0 + NB;                             // [NB]
+  float* bp = reinterpret_cast<float*>(bd1 + NB);  // [NB] block prefix
+  float* stash = bp + NB;                          // [kStashRows][32]
+  __shared__ float s_res, s_prev, s_at;
+  __shared__ int s_found, s_nstash;
+  if (tid == 0) s_nstash = 0;
+  // prefixes: rows inside their block (warp per block), then the blocks
+  for (int b = warp; b < NB; b += kPW) {
+    const int row = b * 32 + lane;
+    const float x = row < R ? rs[row] : 0.0f;
+    float inc = x;
+#pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-      const double o = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += o;
+      const float o = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += o;
     }
-    double run = incl - loc;
-    for (int j = 0; j < per; j++) {
-      const int k = lane * per + j;
-      if (k < kPT) {
-        const double x = pre[k + 1];
-        pre[k + 1] = run;  // exclusive prefix of chunk k stored at k + 1 for now
-        run += x;
+    const float ex = __shfl_up_sync(0xffffffffu, inc, 1);
+    if (row < R) rp[row] = lane ? ex : 0.0f;
+    if (lane == 31) bp[b] = inc;
+  }
+  DEFER_CTA_SYNC();
+  if (warp == 0) {
+    float carry = 0.0f;
+    for (int b0 = 0; b0 < NB; b0 += 32) {
+      const int b = b0 + lane;
+      const float x = b < NB ? bp[b] : 0.0f;
+      float inc = x;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float o = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += o;
       }
+      if (b < NB) bp[b] = carry + (inc - x);
+      carry += __shfl_sync(0xffffffffu, inc, 31);
     }
   }
   DEFER_CTA_SYNC();
-  {
-    // predicted binade of this chunk and its integer increments
-    const double lo = pre[tid + 1];
-    const double hi = lo + sum;
-    const float flo = (float)lo, fhi = (float)hi;
+  for (int row = tid; row < R; row += kPT) rp[row] += bp[row >> 5];
+  DEFER_CTA_SYNC();
+  // rows: predicted binade and increments. A warp takes a block of 32 rows,
+  // lane = row. The values arrive 8 columns at a time through the warp's
+  // [32][9] tile of shared memory (a load instruction covers 4 rows x 8
+  // columns: whole 32-byte sectors), computed where they are loaded; then
+  // each lane adds its row's values in order, keeping the running parity
+  // that ties need, for an even and an odd incoming multiple.
+  float* tile = stash + 32 * kStashRows + warp * (32 * 9);
+  for (int b = warp; b < NB; b += kPW) {
+    const int row = b * 32 + lane;
+    const bool has = row < R;
     int e = kNoBinade;
-    if (i1 > i0 && flo > 0.0f && isfinite(fhi)) {
-      const int el = binade_of(flo), eh = binade_of(fhi);
-      if (el == eh && el >= -126 + 24 && el <= 100) e = el;
-    }
-    int dd0 = 0, dd1 = 0;
-    if (e != kNoBinade) {
-      const float scale = pow2f(23 - e);
-      int par0 = 0, par1 = 1;
-      for (int i = i0; i < i1; i++) {
-        const float x = __fmul_rn(v(i), scale);
-        if (!(x < 33554432.0f)) {  // >= 2^25 (or not finite): the chunk certainly leaves the binade
-          dd0 = dd1 = 1 << 26;
-          break;
-        }
-        const float fl = floorf(x);
-        const float fr = __fsub_rn(x, fl);
-        const int f = (int)fl;
-        if (fr == 0.5f) {
-          const int q0 = f + ((par0 + f) & 1), q1 = f + ((par1 + f) & 1);
-          dd0 += q0;
-          dd1 += q1;
-          par0 = (par0 + q0) & 1;
-          par1 = (par1 + q1) & 1;
-        } else {
-          const int q = f + (fr > 0.5f ? 1 : 0);
-          dd0 += q;
-          dd1 += q;
-          par0 = (par0 + q) & 1;
-          par1 = (par1 + q) & 1;
-        }
-        if (dd0 > (1 << 26)) dd0 = 1 << 26;
-        if (dd1 > (1 << 26)) dd1 = 1 << 26;
+    if (has) {
+      const float lo = rp[row], hi = lo + rs[row];
+      if (lo > 0.0f && isfinite(hi)) {
+        const int el = binade_of(lo);
+        if (el == binade_of(hi) && el >= -102 && el <= 100) e = el;
       }
     }
-    pe[tid] = e;
-    d0[tid] = dd0;
-    d1[tid] = dd1;
+    int slot = -1;  // stash slot of a row the walk will likely cross
+    if (has && e == kNoBinade) {
+      slot = atomicAdd(&s_nstash, 1);
+      if (slot >= kStashRows) slot = -1;
+    }
+    const float scale = e != kNoBinade ? pow2f(23 - e) : 0.0f;
+    int a0 = 0, a1 = 0;  // increments for an even / odd incoming multiple
+    bool nz = false;
+    for (int c = 0; c < 4; c++) {
+      float raw[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int i = (b * 32 + k * 4 + (lane >> 3)) * 32 + c * 8 + (lane & 7);
+        raw[k] = i < n ? v.raw(i) : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int rr = k * 4 + (lane >> 3);
+        const int i = (b * 32 + rr) * 32 + c * 8 + (lane & 7);
+        tile[rr * 9 + (lane & 7)] = i < n ? v.of(raw[k]) : 0.0f;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float x = tile[lane * 9 + j];
+        nz |= x != 0.0f;
+        if (slot >= 0) stash[slot * 32 + c * 8 + j] = x;
+        if (e != kNoBinade) {
+          const float y = __fmul_rn(x, scale);  // exact: a power-of-two scale
+          if (!(y < 33554432.0f)) {  // leaves the binade (or not finite)
+            a0 = a1 = 1 << 26;
+          } else {
+            const float f = floorf(y);
+            const float fr = __fsub_rn(y, f);
+            const int fl = (int)f;
+            if (fr == 0.5f) {  // a tie goes to the even total
+              a0 += fl + ((a0 + fl) & 1);
+              a1 += fl + ((1 + a1 + fl) & 1);
+            } else {
+              const int q = fl + (fr > 0.5f ? 1 : 0);
+              a0 += q;
+              a1 += q;
+            }
+            a0 = min(a0, 1 << 26);
+            a1 = min(a1, 1 << 26);
+          }
+        }
+      }
+      __syncwarp();
+    }
+    if (has) {
+      if (!nz) {
+        re[row] = kAnyBinade;
+        rd0[row] = rd1[row] = 0;
+      } else {
+        re[row] = e;
+        rd0[row] = e == kNoBinade ? slot : a0;
+        rd1[row] = a1;
+      }
+    }
   }
   DEFER_CTA_SYNC();
-  if (tid < 32) {
-    // the walk over the chunks with the exact running sum (every lane keeps it)
+  // blocks: the composed increments when every row is all zeros or runs in
+  // one binade
+  for (int b = warp; b < NB; b += kPW) {
+    const int row = b * 32 + lane;
+    const int e = row < R ? re[row] : kAnyBinade;
+    int common = kAnyBinade;
+    for (int j = 0; j < 32; j++) {
+      const int ej = __shfl_sync(0xffffffffu, e, j);
+      if (ej == kAnyBinade) continue;
+      if (common == kAnyBinade) common = ej;
+      else if (ej != common) common = kNoBinade;
+    }
+    Incr d = (row < R && e != kAnyBinade && e != kNoBinade) ? Incr{rd0[row], rd1[row]} : Incr{0, 0};
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Incr o{__shfl_up_sync(0xffffffffu, d.d0, off), __shfl_up_sync(0xffffffffu, d.d1, off)};
+      if (lane >= off) d = incr_then(o, d);
+    }
+    if (lane == 31) {
+      be[b] = common;
+      bd0[b] = d.d0;
+      bd1[b] = d.d1;
+    }
+  }
+  DEFER_CTA_SYNC();
+  if (marks && tid == 0) marks[0] = gtimer_ns();
+  if (warp == 0) {  // the walk; every lane keeps the exact S
     float S = 0.0f, P = 0.0f;
     int hit = -1;
-    for (int k = 0; k < kPT && hit < 0; k++) {
-      const int a = min(n, k * c), b = min(n, a + c);
-      if (a >= b) break;
-      const int e = pe[k];
-      bool done = false;
-      if (e != kNoBinade && S > 0.0f && binade_of(S) == e) {
-        const int M = (int)__fmul_rn(S, pow2f(23 - e));
-        const int d = (M & 1) ? d1[k] : d0[k];
-        if (M + d < (1 << 24)) {
-          const float Sn = __fmul_rn((float)(M + d), pow2f(e - 23));
-          if (!(find && r < Sn)) {
-            S = Sn;
-            done = true;
-          }
+    bool end = false;
+    for (int c = 0; c < NB && !end; c += 32) {
+      const int nb = min(32, NB - c);
+      const int eb = lane < nb ? be[c + lane] : kAnyBinade;
+      const Incr db = lane < nb ? Incr{bd0[c + lane], bd1[c + lane]} : Incr{0, 0};
+      for (int jb = 0; jb < nb && !end;) {
+        const int fb = walk_level(S, jb, nb, eb, db, find, r);
+        if (fb >= nb) break;
+        const int b = c + fb;  // into the block's rows
+        const int nr = min(32, R - b * 32);
+        const int er = lane < nr ? re[b * 32 + lane] : kAnyBinade;
+        const Incr dr = lane < nr ? Incr{rd0[b * 32 + lane], rd1[b * 32 + lane]} : Incr{0, 0};
+        for (int jr = 0; jr < nr && !end;) {
+          const int fr = walk_level(S, jr, nr, er, dr, find, r);
+          if (fr >= nr) break;
+          const int row = b * 32 + fr;  // into the row's values
+          const int e_row = __shfl_sync(0xffffffffu, er, fr);
+          const int slot = __shfl_sync(0xffffffffu, dr.d0, fr);
+          const int i = row * 32 + lane;
+          const float x = (e_row == kNoBinade && slot >= 0) ? stash[slot * 32 + lane] : (i < n ? v(i) : 0.0f);
+          end = walk_values(S, P, hit, x, row * 32, find, r);
+          jr = fr + 1;
         }
-      }
-      if (!done) {  // element by element in fp32
-        for (int i = a + lane; i < b; i += 32) walk[i - a] = v(i);
-        __syncwarp();
-        if (lane == 0) {
-          for (int i = a; i < b; i++) {
-            const float x = walk[i - a];
-            if (find) {
-              if (x > 0.0f) {
-                const float Sn = __fadd_rn(S, x);
-                if (r < Sn) {
-                  hit = i;
-                  P = S;
-                  S = Sn;
-                  break;
-                }
-                S = Sn;
-              }
-            } else {
-              S = __fadd_rn(S, x);
-            }
-          }
-        }
-        S = __shfl_sync(0xffffffffu, S, 0);
-        if (!find && !isfinite(S)) break;  // NaN / inf stays so: the sum is degenerate
-        P = __shfl_sync(0xffffffffu, P, 0);
-        hit = __shfl_sync(0xffffffffu, hit, 0);
-        __syncwarp();
+        jb = fb + 1;
       }
     }
     if (lane == 0) {
+      if (marks) marks[1] = gtimer_ns();
       s_res = S;
       s_found = hit;
       s_prev = P;
@@ -767,6 +951,31 @@ static __device__ float exact_seq(const SampleVals& v, int n, bool find, float r
   if (at) *at = s_at;
   DEFER_CTA_SYNC();
   return res;
+}
+
+// Row sums of v (the walk's steering; any rounding) into smem[0..R).
+static __device__ void row_sums(const SampleVals& v, int n, float* rs) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int R = (n + 31) / 32;
+  constexpr int kU = 8;
+  for (int r0 = warp; r0 < R; r0 += kPW * kU) {
+    float raw[kU];
+#pragma unroll
+    for (int u = 0; u < kU; u++) {
+      const int i = (r0 + u * kPW) * 32 + lane;
+      raw[u] = i < n ? v.raw(i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; u++) {
+      const int row = r0 + u * kPW;
+      if (row >= R) break;
+      float x = row * 32 + lane < n ? v.of(raw[u]) : 0.0f;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+      if (lane == 0) rs[row] = x;
+    }
+  }
+  DEFER_CTA_SYNC();
 }
 
 // Argmax of the raw logits (NaN skipped, lowest index on ties; 0 when all
@@ -834,27 +1043,47 @@ static __device__ int last_positive(const SampleVals& v, int V) {
 // sampler::sample_token with the PRNG word already drawn. *margin = the
 // distance of r to the nearer edge of the chosen token's CDF interval (0
 // for greedy, NaN for the degenerate one-hot fallback). smem:
-// sample_exact_floats(V) floats. Whole CTA.
-static __device__ uint32_t sample_exact(const float* lg, int V, float T, uint32_t word, float* margin, float* smem) {
-  int amax;
-  float M;
-  logits_scan(lg, V, T, &amax, &M);
+// sample_exact_floats(V) floats. Whole CTA. `m_given`: M = m_max is known
+// (the max of s gathered from per-CTA statistics), so no scan finds it.
+// `row_m`, `row_z`: per row of 32 logits the max of s and the sum of
+// exp(s - max) (block_stats), which steer the walk in place of a pass of
+// row sums. `marks` (instrumentation, or null): globaltimer stamps when
+// each pass's rows and blocks are ready and when its walk ends (4 words).
+static __device__ uint32_t sample_exact(const float* lg, int V, float T, uint32_t word, float* margin, float* smem,
+                                       bool m_given = false, float m_max = 0.0f, const float* row_m = nullptr,
+                                       const float* row_z = nullptr, unsigned long long* marks = nullptr) {
+  int amax = 0;
+  float M = m_max;
+  if (!m_given || T == 0.0f) logits_scan(lg, V, T, &amax, &M);
   if (T == 0.0f) {
     *margin = 0.0f;
     return (uint32_t)amax;
   }
   const SampleVals ve{lg, T, M, 0.0f, false};
-  const float Z = exact_seq(ve, V, false, 0.0f, nullptr, nullptr, nullptr, smem);
+  if (row_m) {  // rows' max of s and sum of exp(s - max), from the logits' producers
+    for (int row = threadIdx.x; row < (V + 31) / 32; row += kPT) {
+      const float z = ld_f(row_z + row);
+      smem[row] = z > 0.0f ? z * expf(ld_f(row_m + row) - M) : 0.0f;
+    }
+    DEFER_CTA_SYNC();
+  } else {
+    row_sums(ve, V, smem);
+  }
+  const float Z = exact_seq(ve, V, false, 0.0f, nullptr, nullptr, nullptr, smem, marks);
   if (!(Z > 0.0f) || !isfinite(Z)) {
+    float unused;
+    if (m_given) logits_scan(lg, V, T, &amax, &unused);
     *margin = NAN;
     return (uint32_t)amax;
   }
   const float inv = __fdiv_rn(1.0f, Z);
+  for (int row = threadIdx.x; row < (V + 31) / 32; row += kPT) smem[row] *= inv;  // rows of p, roughly
+  DEFER_CTA_SYNC();
   const SampleVals vp{lg, T, M, inv, true};
   const float r = (float)(word >> 8) * (1.0f / 16777216.0f);
   int hit;
   float prev, at;
-  const float total = exact_seq(vp, V, true, r, &hit, &prev, &at, smem);
+  const float total = exact_seq(vp, V, true, r, &hit, &prev, &at, smem, marks ? marks + 2 : nullptr);
   if (hit >= 0) {
     *margin = fminf(__fsub_rn(r, prev), __fsub_rn(at, r));
     return (uint32_t)hit;
@@ -918,7 +1147,14 @@ __device__ void ph_select(const DModel& m, const DBatch& bt, int run_step, int c
       if (T == 0.0f) {
         smp = argmax_from_blocks(bt.ss.lmax + (size_t)b * nb, bt.ss.larg + (size_t)b * nb, nb, true);
       } else {
-        smp = sample_exact(bt.logits + (size_t)b * m.V, m.V, T, S.words[k], &margin, smem);
+        // M from the rows' maxima of s (the head's block statistics), which
+        // with the rows' exp-sums also steer the exact walk
+        const float* sm = bt.ss.smax + (size_t)b * nb;
+        float mx = -INFINITY;
+        for (int j = tid; j < nb; j += kPT) mx = fmaxf(mx, ld_f(sm + j));
+        mx = cta_max(mx);
+        smp = sample_exact(bt.logits + (size_t)b * m.V, m.V, T, S.words[k], &margin, smem, true, mx, sm,
+                           bt.ss.esum + (size_t)b * nb);
       }
       if (S.verify) {
         if (tid == 0 && smp != S.tokens[vi]) {
@@ -1421,7 +1657,8 @@ __device__ void ph_head_wide_direct(const DModel& m, const DBatch& bt, const Par
         const float v = tbuf[s * kSBlk + lane];
         if (valid) bt.logits[(size_t)b * m.V + i] = v;
         const size_t o = (size_t)b * nb + k;
-        block_stats(v, i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+        block_stats(v, i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o,
+                    bt.ss.esum + o);
       }
       __syncwarp();
     }
@@ -1501,7 +1738,7 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
         const int i = k * kSBlk + lane;
         constexpr int Q = (G + kPW - 1) / kPW;
         ValIdx best[Q];
-        float smx[Q];
+        float smx[Q], sown[Q];
 #pragma unroll
         for (int q = 0; q < Q; q++) {
           const int gg = warp + q * kPW;
@@ -1511,6 +1748,7 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
           const float T = on ? g_temp[gg] : 0.0f;
           best[q] = ValIdx{v, !isnan(v) ? i : INT_MAX};
           smx[q] = (on && T != 0.0f) ? __fdiv_rn(v, T) : -INFINITY;
+          sown[q] = smx[q];
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
@@ -1521,15 +1759,17 @@ __device__ void ph_head_wide(const DModel& m, const DBatch& bt, int cta, int nct
             smx[q] = fmaxf(smx[q], __shfl_xor_sync(0xffffffffu, smx[q], off));
           }
         }
-        if (lane == 0) {
 #pragma unroll
-          for (int q = 0; q < Q; q++) {
-            const int gg = warp + q * kPW;
-            if (gg >= G || !g_act[gg]) continue;
+        for (int q = 0; q < Q; q++) {
+          const int gg = warp + q * kPW;
+          const bool samp = gg < G && g_act[gg] && g_temp[gg] != 0.0f;  // warp-uniform
+          const float z = samp ? row_expsum(sown[q], true, smx[q]) : 0.0f;
+          if (lane == 0 && gg < G && g_act[gg]) {
             const size_t o = (size_t)(b0 + gg) * nb + k;
             bt.ss.lmax[o] = best[q].v;
             bt.ss.larg[o] = best[q].i;
             bt.ss.smax[o] = smx[q];
+            bt.ss.esum[o] = z;
           }
         }
         // the sums are rewritten from the next half on, after its barrier
@@ -1585,7 +1825,8 @@ __device__ void ph_head(const DModel& m, const DBatch& bt, int cta, int ncta, fl
         if (!g_act[gg]) continue;
         if (valid) bt.logits[(size_t)b * m.V + i] = mine[g];
         const size_t o = (size_t)b * nb + k;
-        block_stats(mine[g], i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+        block_stats(mine[g], i, valid, bt.sess[b].temperature, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o,
+                    bt.ss.esum + o);
       }
     }
     DEFER_CTA_SYNC();
@@ -1620,7 +1861,8 @@ static __device__ void ph_restat(const DModel& m, const DBatch& bt, int cta, int
       const int i = k * kSBlk + lane;
       const bool valid = i < m.V;
       const size_t o = (size_t)b * nb + k;
-      block_stats(valid ? ld_f(lg + i) : NAN, i, valid, T, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+      block_stats(valid ? ld_f(lg + i) : NAN, i, valid, T, bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o,
+                    bt.ss.esum + o);
     }
   }
 }

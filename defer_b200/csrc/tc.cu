@@ -4,12 +4,14 @@
 // over up to 128 slots, on the 5th-generation tensor cores with the
 // accumulator in tensor memory.
 //
-// Precision. The weights and activations are fp32; each is split into two
-// bf16 terms, x = x_hi + x_lo with x_hi = bf16(x) and x_lo = bf16(x - x_hi)
-// (|x - x_hi - x_lo| <= 2^-18 |x|), and the product is accumulated in fp32
-// as x_hi.w_hi + x_hi.w_lo + x_lo.w_hi (the dropped x_lo.w_lo term is below
-// 2^-18 of the product). Weights stored as bf16 are exact in one term
-// (w_lo = 0, two products). Results are checked against the CPU oracle at
+// Precision. The activations are fp32 and split into bf16 terms, x_hi =
+// bf16(x), x_mid = bf16(x - x_hi), x_lo = bf16(x - x_hi - x_mid) (each
+// residual exact in fp32). Weights stored as bf16 are exact in one term:
+// the product is x_hi.w + x_mid.w + x_lo.w, off by at most 2^-27 of each
+// term's magnitude (below fp32's own rounding). fp32 weights are split in
+// two, w_hi + w_lo, and the activations in two: x_hi.w_hi + x_hi.w_lo +
+// x_lo.w_hi with x_lo = bf16(x - x_hi), within 2^-17 of each product.
+// Accumulation is fp32 in tensor memory. Results are checked against the CPU oracle at
 // the parity tolerance; they are deterministic run to run (fixed K-block
 // order, split-K partial sums added in split order), but not bit-identical
 // to the CUDA-core path of the other token loops.
@@ -19,18 +21,24 @@
 // bytes), a 64-wide K block of R rows stored as (row group g, k chunk c) at
 // (g * 8 + c) * 128 bytes, so the leading byte offset (next k chunk) is 128
 // and the stride byte offset (next row group) is 1024. Activations of one
-// K block: [hi: 128 rows][lo: 128 rows] (32 KB); weights are packed once
-// into tiles of 64 rows x 64 k, [hi][lo] per tile (16 KB, 8 KB when bf16),
-// ordered row tile major, K block minor, so a CTA's K range is contiguous.
+// K block: [hi][mid][lo] or [hi][lo], 128 rows each (16 KB per term);
+// weights are packed once into tiles of 64 rows x 64 k, [hi][lo] per tile
+// (16 KB, 8 KB when bf16), ordered row tile major, K block minor, so a
+// CTA's K range is contiguous.
 //
-// GEMM kernel (k_tc_gemm): one CTA per (64-row tile, K split); 4 warps.
-// Thread 0 streams A and W blocks with bulk copies into a 4-stage ring
-// (mbarrier complete_tx); thread 32 issues the MMAs (M = 128, N = 64,
-// K = 16 per instruction, 2-3 products per k step) and commits each stage
-// back to the producer; after the last block all 128 threads read their
-// TMEM lane (slot) with tcgen05.ld and store the 64 partial sums. Every
-// wait is bounded; a wait that runs out sets the status word, the CTA
-// drains its copies in flight and frees its tensor memory.
+// GEMM kernel (k_tc_gemm): one CTA per (64-row tile, K split); 6 warps.
+// Warp 4 streams A and W blocks with bulk copies into a 4-stage ring
+// (mbarrier complete_tx); warp 5 issues the MMAs (M = 128, N = 64, K = 16
+// per instruction, 3 products per k step) and commits each stage back to
+// the producer. The tensor core's own fp32 accumulation loses accuracy over
+// long chains (on the 8B widths a 32-block chain was ~10x less accurate than
+// fp32 dot products), so the K range is cut into groups of kTcGroup blocks:
+// each group accumulates from zero into one of two TMEM buffers, and warps
+// 0-3 read it (tcgen05.ld, TMEM lane = slot) and add it into registers in
+// group order while the next group runs in the other buffer; they store the
+// 64 partial sums at the end. Every wait is bounded; a wait that runs out
+// sets the status word, the CTA drains its copies and MMAs in flight and
+// frees its tensor memory.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -52,8 +60,9 @@ constexpr int kTcBK = 64;                        // K per block
 constexpr int kTcStages = 4;
 constexpr int kTcABytes = kTcM * kTcBK * 2;      // one bf16 term of an activation block
 constexpr int kTcWBytes = kTcBN * kTcBK * 2;     // one bf16 term of a weight tile
-constexpr int kTcStageBytes = 2 * kTcABytes + 2 * kTcWBytes;
-constexpr int kTcThreads = 128;
+constexpr int kTcStageMax = 3 * kTcABytes + kTcWBytes;  // the largest stage: 3 + 1 terms (2 + 2 is less)
+constexpr int kTcThreads = 192;  // warps 0-3 drain TMEM, 4 copies, 5 issues MMAs
+constexpr int kTcGroup = 4;      // K blocks per tensor-core accumulation chain
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 __device__ __forceinline__ unsigned long long gtime() {
@@ -126,17 +135,21 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 struct TcGemmArgs {
-  const unsigned char* A;  // [nkb][2][kTcM * kTcBK] bf16
+  const unsigned char* A;  // [nkb][aterms][kTcM * kTcBK] bf16
   const unsigned char* W;  // [ntile][nkb][wterms][kTcBN * kTcBK] bf16
   float* Y;                // [splits][kTcM][n_pad] partial sums
-  int nkb, splits, n_pad, wterms;
+  int nkb, splits, n_pad, wterms, aterms;  // aterms = 3 when wterms = 1, else 2
   int* status;
   const int* active;  // the step's "any slot active" flag, or null (always run)
 };
 
+__device__ __forceinline__ void mb_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ TcGemmArgs g) {
   extern __shared__ __align__(1024) unsigned char tsm[];
-  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], acc_full[2], acc_empty[2], drain;
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -144,20 +157,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   const int tile = blockIdx.x / g.splits, sp = blockIdx.x % g.splits;
   const int kb0 = sp * g.nkb / g.splits, kb1 = (sp + 1) * g.nkb / g.splits;
   const int nk = kb1 - kb0;
+  const int ngroups = (nk + kTcGroup - 1) / kTcGroup;
   unsigned char* ring = tsm;
   if (tid == 0) {
     for (int s = 0; s < kTcStages; s++) {
       mb_init(&full[s], 1);
       mb_init(&empty[s], 1);
     }
-    mb_init(&done, 1);
+    for (int b = 0; b < 2; b++) {
+      mb_init(&acc_full[b], 1);
+      mb_init(&acc_empty[b], 4);  // one arrival per draining warp
+    }
+    mb_init(&drain, 1);
     failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncwarp();
-  if (warp == 0) {  // 64 columns of tensor memory: the 128 x 64 fp32 accumulator
+  if (warp == 5) {  // two 128 x 64 fp32 accumulators: 128 columns of tensor memory
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base)),
-                 "r"(kTcBN)
+                 "r"(2 * kTcBN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -166,89 +183,124 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tm = tmem_base;
   const size_t wtile = (size_t)g.wterms * kTcWBytes;
-  const unsigned stage_bytes = 2u * kTcABytes + (unsigned)wtile;
+  const unsigned a_bytes = (unsigned)g.aterms * kTcABytes;
+  const unsigned stage_bytes = a_bytes + (unsigned)wtile;  // a multiple of 1024
 
-  if (tid == 0) {
-    // producer: this CTA's K blocks of A and of its weight tile
-    int issued = 0;
-    for (int i = 0; i < nk; i++) {
-      const int s = i % kTcStages;
-      if (i >= kTcStages && !mb_wait(&empty[s], (unsigned)((i / kTcStages - 1) & 1))) {
-        atomicCAS(g.status, kStOk, kStTimeout);
-        *(volatile int*)&failed = 1;
-        break;
+  if (warp == 4) {
+    if (lane == 0) {
+      // producer: this CTA's K blocks of A and of its weight tile
+      int issued = 0;
+      for (int i = 0; i < nk; i++) {
+        const int s = i % kTcStages;
+        if (i >= kTcStages && !mb_wait(&empty[s], (unsigned)((i / kTcStages - 1) & 1))) {
+          atomicCAS(g.status, kStOk, kStTimeout);
+          *(volatile int*)&failed = 1;
+          break;
+        }
+        if (*(volatile int*)&failed) break;
+        unsigned char* st = ring + (size_t)s * stage_bytes;
+        mb_expect_tx(&full[s], stage_bytes);
+        bulk_copy(st, g.A + (size_t)(kb0 + i) * a_bytes, a_bytes, &full[s]);
+        bulk_copy(st + a_bytes, g.W + ((size_t)tile * g.nkb + kb0 + i) * wtile, (unsigned)wtile, &full[s]);
+        issued = i + 1;
       }
-      if (*(volatile int*)&failed) break;
-      unsigned char* st = ring + (size_t)s * kTcStageBytes;
-      mb_expect_tx(&full[s], stage_bytes);
-      bulk_copy(st, g.A + (size_t)(kb0 + i) * 2 * kTcABytes, 2u * kTcABytes, &full[s]);
-      bulk_copy(st + 2 * kTcABytes, g.W + ((size_t)tile * g.nkb + kb0 + i) * wtile, (unsigned)wtile, &full[s]);
-      issued = i + 1;
+      // copies still in flight land before the CTA leaves: the last one of each stage
+      for (int i = max(0, issued - kTcStages); i < issued; i++)
+        if (!mb_wait(&full[i % kTcStages], (unsigned)((i / kTcStages) & 1))) atomicCAS(g.status, kStOk, kStTimeout);
     }
-    // copies still in flight land before the CTA leaves: the last one of each stage
-    for (int i = max(0, issued - kTcStages); i < issued; i++)
-      if (!mb_wait(&full[i % kTcStages], (unsigned)((i / kTcStages) & 1))) atomicCAS(g.status, kStOk, kStTimeout);
-  } else if (tid == 32) {
-    // MMA issuer
-    int i = 0;
-    for (; i < nk; i++) {
-      const int s = i % kTcStages;
-      if (!mb_wait(&full[s], (unsigned)((i / kTcStages) & 1))) {
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // MMA issuer: group gi of kTcGroup K blocks accumulates from zero into
+      // buffer gi & 1, which the draining warps empty while the next group runs
+      bool ok = true;
+      int i = 0;
+      for (int gi = 0; gi < ngroups && ok; gi++) {
+        const int buf = gi & 1;
+        if (gi >= 2 && !mb_wait(&acc_empty[buf], (unsigned)(((gi >> 1) - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tm + (uint32_t)(buf * kTcBN);
+        const int i0 = gi * kTcGroup, iend = min(nk, i0 + kTcGroup);
+        for (i = i0; i < iend; i++) {
+          const int s = i % kTcStages;
+          if (!mb_wait(&full[s], (unsigned)((i / kTcStages) & 1))) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = saddr(ring + (size_t)s * stage_bytes);
+          const uint32_t a_hi = st, a_2 = st + kTcABytes, w_hi = st + a_bytes, w_lo = w_hi + kTcWBytes;
+#pragma unroll
+          for (int ks = 0; ks < kTcBK / 16; ks++) {
+            const uint32_t o = (uint32_t)ks * 256u;  // two 8-wide k chunks of 128 bytes each
+            const uint64_t ah = smem_desc(a_hi + o, 128, 1024), a2 = smem_desc(a_2 + o, 128, 1024);
+            const uint64_t wh = smem_desc(w_hi + o, 128, 1024);
+            umma(d, ah, wh, (i > i0 || ks > 0) ? 1u : 0u);
+            umma(d, a2, wh, 1u);  // x_mid (3 terms) or x_lo (2 terms) times w_hi
+            if (g.wterms == 2) umma(d, ah, smem_desc(w_lo + o, 128, 1024), 1u);
+            else umma(d, smem_desc(a_2 + kTcABytes + o, 128, 1024), wh, 1u);  // x_lo times w
+          }
+          umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      if (!ok) {
         atomicCAS(g.status, kStOk, kStTimeout);
         *(volatile int*)&failed = 1;
-        break;
       }
+      // every MMA issued has completed before tensor memory is freed
+      umma_commit(&drain);
+      if (!mb_wait(&drain, 0u)) atomicCAS(g.status, kStOk, kStTimeout);
+    }
+  } else {
+    // warps 0-3: lane r of TMEM = slot r; each group's 64 partial sums are
+    // added into registers in group order (fp32, round to nearest), which
+    // keeps every tensor-core accumulation chain to kTcGroup K blocks
+    float acc[kTcBN];
+#pragma unroll
+    for (int c = 0; c < kTcBN; c++) acc[c] = 0.0f;
+    bool ok = true;
+    for (int gi = 0; gi < ngroups; gi++) {
+      const int buf = gi & 1;
+      // the warp-collective TMEM loads need one decision per warp
+      ok = __all_sync(0xffffffffu, mb_wait(&acc_full[buf], (unsigned)((gi >> 1) & 1)));
+      if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t st = saddr(ring + (size_t)s * kTcStageBytes);
-      const uint32_t a_hi = st, a_lo = st + kTcABytes, w_hi = st + 2 * kTcABytes, w_lo = w_hi + kTcWBytes;
 #pragma unroll
-      for (int ks = 0; ks < kTcBK / 16; ks++) {
-        const uint32_t o = (uint32_t)ks * 256u;  // two 8-wide k chunks of 128 bytes each
-        const uint64_t ah = smem_desc(a_hi + o, 128, 1024), al = smem_desc(a_lo + o, 128, 1024);
-        const uint64_t wh = smem_desc(w_hi + o, 128, 1024);
-        umma(tm, ah, wh, (i > 0 || ks > 0) ? 1u : 0u);
-        umma(tm, al, wh, 1u);
-        if (g.wterms == 2) umma(tm, ah, smem_desc(w_lo + o, 128, 1024), 1u);
+      for (int c0 = 0; c0 < kTcBN; c0 += 16) {
+        uint32_t v[16];
+        const uint32_t ta = tm + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * kTcBN + c0);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(ta));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 16; j++) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(v[j]));
       }
-      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mb_arrive(&acc_empty[buf]);
     }
-    umma_commit(&done);
-  }
-  __syncwarp();
-  // epilogue: lane r of TMEM = slot r; 64 columns = this tile's rows. The
-  // warp-collective TMEM loads need one decision per warp.
-  const bool ok = __all_sync(0xffffffffu, mb_wait(&done, 0u));
-  if (!ok && lane == 0) atomicCAS(g.status, kStOk, kStTimeout);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (ok && nk > 0) {
-    const int r = warp * 32 + lane;
-    float* y = g.Y + ((size_t)sp * kTcM + r) * g.n_pad + (size_t)tile * kTcBN;
+    if (!ok) {
+      if (lane == 0) atomicCAS(g.status, kStOk, kStTimeout);
+      *(volatile int*)&failed = 1;
+    } else {
+      const int r = warp * 32 + lane;  // an empty K range stores zeros
+      float* y = g.Y + ((size_t)sp * kTcM + r) * g.n_pad + (size_t)tile * kTcBN;
 #pragma unroll
-    for (int c0 = 0; c0 < kTcBN; c0 += 16) {
-      uint32_t v[16];
-      const uint32_t ta = tm + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-          : "r"(ta));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-      for (int q = 0; q < 4; q++)
-        *reinterpret_cast<float4*>(y + c0 + 4 * q) =
-            make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
-                        __uint_as_float(v[4 * q + 3]));
+      for (int c = 0; c < kTcBN; c += 4)
+        *reinterpret_cast<float4*>(y + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
     }
-  } else if (ok) {
-    const int r = warp * 32 + lane;  // an empty K range contributes zeros
-    float* y = g.Y + ((size_t)sp * kTcM + r) * g.n_pad + (size_t)tile * kTcBN;
-    for (int c = 0; c < kTcBN; c += 4) *reinterpret_cast<float4*>(y + c) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 5) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kTcBN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(2 * kTcBN) : "memory");
   }
 }
 
@@ -260,6 +312,12 @@ __host__ __device__ __forceinline__ size_t core_off(int r, int kk) {
 __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
   hi = __float2bfloat16_rn(x);
   lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+}
+__device__ __forceinline__ void split3_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& mid, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(x);
+  const float r = __fsub_rn(x, __bfloat162float(hi));
+  mid = __float2bfloat16_rn(r);
+  lo = __float2bfloat16_rn(__fsub_rn(r, __bfloat162float(mid)));
 }
 
 // Weight packing: W [N][K] (fp32, or bf16 when `bf16`) -> tiles; one thread
@@ -290,18 +348,34 @@ __global__ void k_tc_pack_w(const void* W, int N, int K, int bf16, int nkb, int 
   }
 }
 
-// Activations -> A blocks: slot row b (one CTA each, 128 of them) of `x`
-// ([B][K], row stride K), RMS-normalised with weight `nw` when nw != null
-// ((x * inv) * w, inv = 1 / sqrt(ss / K + eps) with ss a fixed-tree sum),
-// split into bf16 terms. Rows of slots >= B or not active are zero.
-__global__ void __launch_bounds__(256) k_tc_prep(const float* x, const float* nw, float eps, int K, int nkb, int B,
-                                                 const DSlotState* st, unsigned char* A, const int* active) {
-  const int b = blockIdx.x, tid = threadIdx.x;
-  if (active && __ldcg(active) == 0) return;
+// The 8 values at k0.. of one A row, split into `aterms` bf16 terms and
+// stored in the operand's core-matrix layout.
+__device__ __forceinline__ void put_a_chunk(unsigned char* A, int b, int k0, const float* v, int aterms) {
+  __align__(16) __nv_bfloat16 hi[8], mid[8], lo[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    if (aterms == 3) split3_bf16(v[e], hi[e], mid[e], lo[e]);
+    else split_bf16(v[e], hi[e], mid[e]);  // [hi][lo]: the second term in mid
+  }
+  const int kb = k0 / kTcBK, kk = k0 % kTcBK;
+  unsigned char* blk = A + (size_t)kb * aterms * kTcABytes;
+  *reinterpret_cast<uint4*>(blk + core_off(b, kk) * 2) = *reinterpret_cast<const uint4*>(hi);
+  *reinterpret_cast<uint4*>(blk + kTcABytes + core_off(b, kk) * 2) = *reinterpret_cast<const uint4*>(mid);
+  if (aterms == 3)
+    *reinterpret_cast<uint4*>(blk + 2 * kTcABytes + core_off(b, kk) * 2) = *reinterpret_cast<const uint4*>(lo);
+}
+
+// Slot row b of the A operand from row xr ([K]), RMS-normalised with weight
+// `nw` when nw != null ((x * inv) * w, inv = 1 / sqrt(ss / K + eps) with ss
+// a fixed-tree sum: thread t's fmaf chain over k = t, t + 256, ..., warp
+// butterfly, warps in order), split into `aterms` bf16 terms; zero when the
+// slot is not live. A whole 256-thread CTA; a thread's first loop reads only
+// the k = t + 256 j it may itself have just written.
+__device__ __forceinline__ void prep_row(const float* xr, const float* nw, float eps, int K, int nkb, bool live, int b,
+                                         unsigned char* A, int aterms) {
+  const int tid = threadIdx.x;
   __shared__ float red[8];
   __shared__ float s_inv;
-  const bool live = b < B && __ldcg(&st[b].active) != 0;
-  const float* xr = x + (size_t)b * K;
   if (nw && live) {
     float acc = 0.0f;
     for (int k = tid; k < K; k += 256) {
@@ -321,22 +395,29 @@ __global__ void __launch_bounds__(256) k_tc_prep(const float* x, const float* nw
   const float inv = (nw && live) ? s_inv : 1.0f;
   const int kpad = nkb * kTcBK;
   for (int k0 = tid * 8; k0 < kpad; k0 += 256 * 8) {
-    __align__(16) __nv_bfloat16 hi[8], lo[8];
+    float v[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) {
       const int k = k0 + e;
-      float v = 0.0f;
+      v[e] = 0.0f;
       if (live && k < K) {
-        v = __ldcg(xr + k);
-        if (nw) v = __fmul_rn(__fmul_rn(v, inv), nw[k]);
+        v[e] = __ldcg(xr + k);
+        if (nw) v[e] = __fmul_rn(__fmul_rn(v[e], inv), nw[k]);
       }
-      split_bf16(v, hi[e], lo[e]);
     }
-    const int kb = k0 / kTcBK, kk = k0 % kTcBK;
-    unsigned char* blk = A + (size_t)kb * 2 * kTcABytes;
-    *reinterpret_cast<uint4*>(blk + core_off(b, kk) * 2) = *reinterpret_cast<const uint4*>(hi);
-    *reinterpret_cast<uint4*>(blk + kTcABytes + core_off(b, kk) * 2) = *reinterpret_cast<const uint4*>(lo);
+    put_a_chunk(A, b, k0, v, aterms);
   }
+}
+
+// Activations -> A blocks: slot row b (one CTA each, 128 of them) of `x`
+// ([B][K], row stride K). Rows of slots >= B or not active are zero.
+__global__ void __launch_bounds__(256) k_tc_prep(const float* x, const float* nw, float eps, int K, int nkb, int B,
+                                                 const DSlotState* st, unsigned char* A, const int* active,
+                                                 int aterms) {
+  const int b = blockIdx.x;
+  if (active && __ldcg(active) == 0) return;
+  const bool live = b < B && __ldcg(&st[b].active) != 0;
+  prep_row(x + (size_t)b * K, nw, eps, K, nkb, live, b, A, aterms);
 }
 
 // Sum of the split-K partials of (slot b, column n), in split order.
@@ -360,23 +441,40 @@ __global__ void k_tc_qkv_epi(DModel m, DBatch bt, int l, const float* Y, int spl
   }
 }
 
-// x[b][n] += Y (O and down projections).
-__global__ void k_tc_resid(DModel m, DBatch bt, const float* Y, int splits, int n_pad) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < bt.B * m.H; i += gridDim.x * blockDim.x) {
-    const int b = i / m.H, n = i - b * m.H;
-    if (!live_slot(bt, b)) continue;
-    float* x = bt.x + (size_t)b * m.H + n;
-    *x = __fadd_rn(*x, ysum(Y, splits, n_pad, b, n));
-  }
+// x[b] += Y (the O or down projection, split sums in order), then slot row
+// b of the next projection's A operand from the updated row, normalised
+// with `nw` (the next RMSNorm's weights): one launch and one pass over x
+// instead of a residual kernel and a prep. One CTA per slot.
+__global__ void __launch_bounds__(256) k_tc_resid_prep(DModel m, DBatch bt, const float* Y, int splits, int n_pad,
+                                                       const float* nw, int nkb, unsigned char* A,
+                                                       const int* active, int aterms) {
+  const int b = blockIdx.x, tid = threadIdx.x;
+  if (active && __ldcg(active) == 0) return;
+  const bool live = b < bt.B && live_slot(bt, b);
+  float* xr = bt.x + (size_t)b * m.H;
+  if (live)
+    for (int k = tid; k < m.H; k += 256) xr[k] = __fadd_rn(xr[k], ysum(Y, splits, n_pad, b, k));
+  __syncthreads();
+  prep_row(xr, nw, m.eps, m.H, nkb, live, b, A, aterms);
 }
 
-// g = act(gate) * up (gate/up rows interleaved).
-__global__ void k_tc_gu_epi(DModel m, DBatch bt, const float* Y, int splits, int n_pad) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < bt.B * m.FF; i += gridDim.x * blockDim.x) {
-    const int b = i / m.FF, j = i - b * m.FF;
-    if (!live_slot(bt, b)) continue;
-    bt.g[(size_t)b * m.FF + j] =
-        gate_act_mul(m, ysum(Y, splits, n_pad, b, 2 * j), ysum(Y, splits, n_pad, b, 2 * j + 1));
+// g = act(gate) * up of slot row b, straight into the down projection's A
+// operand (g itself is not stored). One CTA per slot.
+__global__ void __launch_bounds__(256) k_tc_gu_prep(DModel m, DBatch bt, const float* Y, int splits, int n_pad,
+                                                    int nkb, unsigned char* A, const int* active, int aterms) {
+  const int b = blockIdx.x, tid = threadIdx.x;
+  if (active && __ldcg(active) == 0) return;
+  const bool live = b < bt.B && live_slot(bt, b);
+  const int kpad = nkb * kTcBK;
+  for (int k0 = tid * 8; k0 < kpad; k0 += 256 * 8) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int j = k0 + e;
+      v[e] = (live && j < m.FF) ? gate_act_mul(m, ysum(Y, splits, n_pad, b, 2 * j), ysum(Y, splits, n_pad, b, 2 * j + 1))
+                                : 0.0f;
+    }
+    put_a_chunk(A, b, k0, v, aterms);
   }
 }
 
@@ -400,7 +498,7 @@ __global__ void __launch_bounds__(kThreads) k_tc_stats(DModel m, DBatch bt) {
     const bool valid = i < m.V;
     const size_t o = (size_t)b * nb + k;
     block_stats(valid ? ld_f(bt.logits + (size_t)b * m.V + i) : NAN, i, valid, bt.sess[b].temperature,
-                bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o);
+                bt.ss.lmax + o, bt.ss.larg + o, bt.ss.smax + o, bt.ss.esum + o);
   }
 }
 __global__ void __launch_bounds__(kThreads) k_tc_restat(DModel m, DBatch bt) {
@@ -447,11 +545,14 @@ TcMatrix tc_pack(const void* W, int N, int K, bool bf16, unsigned char* out, cud
   return t;
 }
 
-size_t tc_act_bytes(int K) { return (size_t)div_up(K, kTcBK) * 2 * kTcABytes; }
+size_t tc_act_bytes(int K) { return (size_t)div_up(K, kTcBK) * 3 * kTcABytes; }
+
+int tc_aterms(const TcMatrix& w) { return w.wterms == 1 ? 3 : 2; }
 
 void tc_prep(const float* x, const float* nw, float eps, int K, int B, const DSlotState* st, unsigned char* A,
-             cudaStream_t s, const int* active) {
-  k_tc_prep<<<kTcM, 256, 0, s>>>(x, nw, eps, K, div_up(K, kTcBK), B, st, A, active);
+             int aterms, cudaStream_t s, const int* active) {
+  if (aterms != 2 && aterms != 3) fail(kInvalidArgument, "tensor-core step: activation terms must be 2 or 3");
+  k_tc_prep<<<kTcM, 256, 0, s>>>(x, nw, eps, K, div_up(K, kTcBK), B, st, A, active, aterms);
   DEFER_CUDA(cudaGetLastError());
 }
 
@@ -475,9 +576,10 @@ static bool first_on_device(unsigned long long& mask) {
 void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s,
              const int* active) {
   static unsigned long long attr = 0;
-  const int smem = kTcStages * kTcStageBytes;
   if (first_on_device(attr))
-    DEFER_CUDA(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    DEFER_CUDA(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kTcStages * kTcStageMax));
+  const int smem = kTcStages * (tc_aterms(w) * kTcABytes + w.wterms * kTcWBytes);
   TcGemmArgs g;
   g.A = A;
   g.W = w.data;
@@ -486,6 +588,7 @@ void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, in
   g.splits = splits;
   g.n_pad = w.ntile * kTcBN;
   g.wterms = w.wterms;
+  g.aterms = tc_aterms(w);
   g.status = status;
   g.active = active;
   k_tc_gemm<<<w.ntile * splits, kTcThreads, smem, s>>>(g);
@@ -513,28 +616,31 @@ void launch_steps_tc(const DModel& m, const TcModel& tm, const DBatch& bt0, int 
   const int nb = bt.nblk;
   // statistics of the resident logits for slots whose first step samples
   k_tc_restat<<<std::min(sms, std::max(1, nb / kPW)), kThreads, 0, st>>>(m, bt);
+  const int at = tc_aterms(tm.head);  // the model's weights share one type
+  const int nkb_h = div_up(m.H, kTcBK), nkb_ff = div_up(m.FF, kTcBK);
   for (int s = 0; s < nsteps; s++) {
     if (m.bf16) k_tc_select<true><<<bt.B, kThreads, smem, st>>>(m, bt, s);
     else k_tc_select<false><<<bt.B, kThreads, smem, st>>>(m, bt, s);
     const int* act = bt.any_active + (s & 1);  // set by this step's SELECT
+    tc_prep(bt.x, tm.layers[0].attn_norm, m.eps, m.H, bt.B, bt.st, wk.A, at, st, act);
     for (int l = 0; l < m.L; l++) {
       const TcLayer& T = tm.layers[l];
-      tc_prep(bt.x, T.attn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st, act);
+      // the A operand of QKV is ready (the step's first prep, or the last
+      // layer's residual)
       tc_gemm(wk.A, T.qkv, wk.Y, T.s_qkv, bt.status, st, act);
       k_tc_qkv_epi<<<ew, 256, 0, st>>>(m, bt, l, wk.Y, T.s_qkv, T.qkv.ntile * kTcBN);
       k_tc_attn<<<std::min(attn_units, sms * 8), kThreads, smem, st>>>(m, bt, l);
       k_tc_combine<<<sms, kThreads, 0, st>>>(m, bt);
-      tc_prep(bt.att, nullptr, 0.0f, m.QD, bt.B, bt.st, wk.A, st, act);
+      tc_prep(bt.att, nullptr, 0.0f, m.QD, bt.B, bt.st, wk.A, at, st, act);
       tc_gemm(wk.A, T.o, wk.Y, T.s_o, bt.status, st, act);
-      k_tc_resid<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_o, T.o.ntile * kTcBN);
-      tc_prep(bt.x, T.ffn_norm, m.eps, m.H, bt.B, bt.st, wk.A, st, act);
+      k_tc_resid_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.s_o, T.o.ntile * kTcBN, T.ffn_norm, nkb_h, wk.A, act, at);
       tc_gemm(wk.A, T.gu, wk.Y, T.s_gu, bt.status, st, act);
-      k_tc_gu_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_gu, T.gu.ntile * kTcBN);
-      tc_prep(bt.g, nullptr, 0.0f, m.FF, bt.B, bt.st, wk.A, st, act);
+      k_tc_gu_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.s_gu, T.gu.ntile * kTcBN, nkb_ff, wk.A, act, at);
       tc_gemm(wk.A, T.down, wk.Y, T.s_down, bt.status, st, act);
-      k_tc_resid<<<ew, 256, 0, st>>>(m, bt, wk.Y, T.s_down, T.down.ntile * kTcBN);
+      const float* next_norm = l + 1 < m.L ? tm.layers[l + 1].attn_norm : m.norm;
+      k_tc_resid_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.s_down, T.down.ntile * kTcBN, next_norm, nkb_h, wk.A, act,
+                                           at);
     }
-    tc_prep(bt.x, m.norm, m.eps, m.H, bt.B, bt.st, wk.A, st, act);
     tc_gemm(wk.A, tm.head, wk.Y, tm.s_head, bt.status, st, act);
     k_tc_head_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, tm.s_head, tm.head.ntile * kTcBN);
     k_tc_stats<<<std::min(sms * 4, std::max(1, bt.B * nb / kPW)), kThreads, 0, st>>>(m, bt);
@@ -543,7 +649,7 @@ void launch_steps_tc(const DModel& m, const TcModel& tm, const DBatch& bt0, int 
   DEFER_CUDA(cudaGetLastError());
 }
 
-int launches_per_step_tc(const DModel& m) { return 4 + 12 * m.L; }
+int launches_per_step_tc(const DModel& m) { return 5 + 11 * m.L; }
 
 void tc_gemm_check(int device, const float* X, int M, const float* W, int N, int K, bool w_bf16, float* Y) {
   if (M < 1 || M > kTcM || N < 1 || K < 1) fail(kInvalidArgument, "tensor-core GEMM check: bad shape");
@@ -583,7 +689,7 @@ void tc_gemm_check(int device, const float* X, int M, const float* W, int N, int
   const int splits = tc_splits(w, sms);
   DEFER_CUDA(cudaMalloc(&dY, tc_y_floats(w, splits) * sizeof(float)));
   tc_prep(static_cast<float*>(dX), nullptr, 0.0f, K, M, static_cast<DSlotState*>(dS), static_cast<unsigned char*>(dA),
-          st);
+          tc_aterms(w), st);
   tc_gemm(static_cast<unsigned char*>(dA), w, static_cast<float*>(dY), splits, status, st);
   std::vector<float> part(tc_y_floats(w, splits));
   int stat = 0;

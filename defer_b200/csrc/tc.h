@@ -58,9 +58,12 @@ size_t tc_act_bytes(int K);
 TcMatrix tc_pack(const void* W, int N, int K, bool bf16, unsigned char* out, cudaStream_t st);
 int tc_splits(const TcMatrix& w, int sms);
 size_t tc_y_floats(const TcMatrix& w, int splits);
-// A [128 slots][K] operand from x ([B][K]), RMS-normalised by nw when non-null.
+// bf16 terms of the activations for weights `w`: 3 when w is bf16, else 2.
+int tc_aterms(const TcMatrix& w);
+// A [128 slots][K] operand from x ([B][K]), RMS-normalised by nw when
+// non-null, split into `aterms` bf16 terms.
 void tc_prep(const float* x, const float* nw, float eps, int K, int B, const DSlotState* st, unsigned char* A,
-             cudaStream_t s, const int* active = nullptr);
+             int aterms, cudaStream_t s, const int* active = nullptr);
 // Y[split][slot][n] partial sums of A . W^T.
 // With `active` (a device flag) the launch does nothing when it is 0.
 void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s,

@@ -46,8 +46,8 @@ def greedy_run(path, prompt, n):
 def edge_report(O, lo, t, word, got):
     """Where the oracle's sampler (sequential fp32 CDF, sampler.rs:95-104)
     chooses another token than `got`: both choices, the distance of r to the
-    exact (float64) CDF edge between them, and how far the sequential fp32
-    CDF has drifted from the exact one at that edge."""
+    sequential fp32 CDF edge between them (seq_edge), to the exact float64
+    edge, and how far the sequential CDF has drifted from the exact one."""
     want = int(O.sample_token_word(lo, t, word))
     if want == got:
         return None
@@ -61,7 +61,8 @@ def edge_report(O, lo, t, word, got):
     c_seq = np.add.accumulate(p32, dtype=np.float32).astype(np.float64)
     r = float(O.unit_f32(word))
     k = min(want, got)
-    return {"oracle": want, "gpu": got, "edge": abs(r - c_exact[k]), "drift": abs(c_seq[k] - c_exact[k])}
+    return {"oracle": want, "gpu": got, "edge": abs(r - c_exact[k]), "drift": abs(c_seq[k] - c_exact[k]),
+            "seq_edge": abs(r - c_seq[k])}
 
 
 def teacher_forced(path, tokens, n_prompt, t, seed, check_steps, want_kv):

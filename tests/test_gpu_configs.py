@@ -8,8 +8,9 @@ lengths, through the C ABI:
             to a 2048-token context, then teacher-forced through the oracle:
             logits at every 8th position and the last 64, KV at the end, and
             every sampled token the oracle's sequential-CDF sampler would
-            choose differently, each within that sampler's own CDF drift of
-            an exact edge. The disagreement rate is reported.
+            choose differently (its logits differ from the GPU's by rounding)
+            within a few ulps of an edge of that sampler's own CDF. The
+            disagreement rate is reported.
   config 3: 512 sessions (prompts 16-256, seeds 0..511, T = 0.8, 512
             generated tokens each) replayed in one batch with no divergence;
             the sessions with the shortest and the longest prompt are
@@ -121,11 +122,17 @@ def _check_logits(gpu, cpu, label):
     return worst
 
 
-def _check_edges(reports, label):
-    # A differing choice is only possible where r lies within the sequential
-    # fp32 CDF's drift (plus the GPU's hierarchical-sum error) of an edge.
+def _check_edges(reports, label, sampled):
+    # The device sampler is the reference's sequential-CDF sampler bit for
+    # bit (test_gpu_parity checks it on identical logits), so a differing
+    # choice comes from the forward's own rounding differences (logits within
+    # ~1e-6 of their range): r then lies within a few fp32 ulps of the edge
+    # between the two tokens in the oracle's own sequential CDF. With ~V
+    # edges in [0, 1) such near-ties occur at a rate of roughly V x 1e-7
+    # per sampled token.
     for r in reports:
-        assert r["edge"] <= r["drift"] + 2e-6, f"{label}: {r}"
+        assert r["seq_edge"] <= 1e-6, f"{label}: {r}"
+    assert len(reports) <= max(3, 0.02 * sampled), f"{label}: {len(reports)} of {sampled}"
 
 
 def _record(name, obj):
@@ -172,7 +179,7 @@ def test_config2_teacher_forced_over_2048_positions(runs):
         for g, o in ((kg, okv[l][0]), (vg, okv[l][1])):
             kv = max(kv, float(np.abs(g.astype(np.float64) - o).max()) / float(np.abs(o).max()))
     assert kv <= KV_TOL, kv
-    _check_edges(reports, "config2")
+    _check_edges(reports, "config2", 2048 - 32)
     rate = len(reports) / (2048 - 32)
     _record("config2", {"sampled": 2048 - 32, "oracle_disagreements": len(reports), "rate": rate,
                         "reports": reports, "worst_logit_err_over_range": worst, "worst_kv_rel": kv})
@@ -194,7 +201,7 @@ def test_config3_batched_replay_and_two_sessions_teacher_forced(runs):
         worst = _check_logits(glog, ologits, f"config3 session {k}")
         ok, kv = kv_close(gc, _KvView(okv), gm.config.num_layers)
         assert ok, kv
-        _check_edges(reports, f"config3 session {k}")
+        _check_edges(reports, f"config3 session {k}", len(hist) - n_prompt)
         out[k] = {"tokens": len(hist), "prompt": n_prompt, "oracle_disagreements": len(reports),
                   "reports": reports, "worst_logit_err_over_range": worst, "worst_kv_rel": kv}
     _record("config3", out)
@@ -237,7 +244,7 @@ def test_config5_shape_forward_and_replay(tmp_path):
     res, _ = D.replay_batch(gm, cks, batch=2)
     assert all(r.status == 0 for r in res)
     reports, _, _ = J.teacher_forced(path, prompts[0] + gen[0], 8, 0.8, seeds[0], [], False)
-    _check_edges(reports, "config5 shape")
+    _check_edges(reports, "config5 shape", 24)
     _record("config5", {"positions": len(toks), "worst_logit_err_over_range": worst, "worst_kv_rel": kv,
                         "sampled": 24, "oracle_disagreements": len(reports)})
 

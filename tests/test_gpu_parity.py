@@ -218,6 +218,46 @@ def test_device_sampler_equals_the_reference_sampler():
         assert got == O.sample_token_word(l, t, w), (k, n, kind, t)
 
 
+def _sampled_by_reference(gm, hist, n_prompt, t, seed):
+    """Indices where the oracle's sampler, given the GPU's own logits of
+    that step (teacher-forced, bit-identical to the token loop's), picks
+    another token than the recorded one."""
+    c = gm.new_cache(len(hist) + 1)
+    words = D.chacha8_words(seed, 0, len(hist) - n_prompt)
+    bad = []
+    for i, tok in enumerate(hist[:-1]):
+        lo = gm.forward_ext(tok, c, (), logits=i + 1 >= n_prompt)
+        if i + 1 >= n_prompt:
+            want = int(O.sample_token_word(lo, t, int(words[i + 1 - n_prompt])))
+            if want != hist[i + 1]:
+                bad.append(i + 1)
+    return bad
+
+
+@pytest.mark.parametrize("name,n_sessions", [("smollm2-135m", 1), ("test-small", 1), ("smollm2-135m", 12)])
+def test_in_loop_sampler_matches_the_reference_sampler(mdir, name, n_sessions):
+    """Every sampled token of GPU sessions equals sampler.rs's choice on the
+    logits the GPU computed at that step: one session runs the dataflow
+    token loop, twelve the grid-barrier kernel, whose heads hand the exact
+    sampler their per-row statistics."""
+    gm = D.Model.load(model_file(mdir, name))
+    V = gm.config.vocab_size
+    seeds = [D.seed_from_u64(70 + k) for k in range(n_sessions)]
+    prompts = [_tokens(V, 9 + k, 30 + k) for k in range(n_sessions)]
+    temps = [(0.7, 1.0, 1.3)[k % 3] for k in range(n_sessions)]
+    n_gen = 160 if n_sessions == 1 else 48
+    if n_sessions == 1:
+        s = D.Session(gm, seeds[0], temps[0])
+        s.prompt(prompts[0])
+        s.generate(n_gen)
+        hists = [s.history()]
+    else:
+        gen, _ = D.generate_batch(gm, prompts, seeds, temps, [n_gen] * n_sessions, batch=n_sessions)
+        hists = [p + g for p, g in zip(prompts, gen)]
+    for k, h in enumerate(hists):
+        assert _sampled_by_reference(gm, h, len(prompts[k]), temps[k], seeds[k]) == [], (name, k)
+
+
 def test_sampler_rejects_bad_input():
     with pytest.raises(D.InvalidArgumentError):
         D.sample_logits(np.zeros(0, np.float32), 0.7, 1)

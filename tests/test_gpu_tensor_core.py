@@ -1,9 +1,10 @@
 """The tensor-core (tcgen05) contraction of the batched attribution step.
 
 The GEMM alone against a float64 product: split-bf16 operands with fp32
-accumulation keep each output within a few 1e-6 of sum |x| |w| (the
-bf16 split leaves 2^-18 of each operand; fp32 sums add their own rounding),
-for shapes that pad rows and K, several K splits and bf16-stored weights.
+accumulation keep each output within a few 1e-6 of sum |x| |w| for fp32
+weights (two terms per operand leave 2^-17 of each product) and within
+about fp32 rounding for bf16-stored weights (three activation terms leave
+2^-27), for shapes that pad rows and K and several K splits.
 Then the attribution batch on the tensor-core step (DEFER_B200_TC=1): the
 same log-probabilities for every batch width (each slot's rows of the
 contraction are independent of the others), within the parity tolerance
@@ -43,7 +44,9 @@ def test_tc_gemm_bf16_weights_and_row_independence():
     y = D.tc_gemm(x, wb, w_bf16=True)
     ref = x.astype(np.float64) @ wb.astype(np.float64).T
     scale = np.abs(x).astype(np.float64) @ np.abs(wb).astype(np.float64).T
-    assert (np.abs(y - ref) / scale).max() < 2e-5
+    err = np.abs(y - ref) / scale
+    assert err.max() < 3e-6, err.max()
+    assert np.median(err) < 3e-7, np.median(err)
     # a row's result does not depend on the other rows of the tile
     y7 = D.tc_gemm(x[7:8], wb, w_bf16=True)
     assert y7.tobytes() == y[7:8].tobytes()

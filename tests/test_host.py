@@ -60,6 +60,18 @@ def test_checkpoint_bytes_match_oracle(tmp_path):
     assert not os.path.exists(str(tmp_path / "x.ckpt.tmp"))
 
 
+@pytest.mark.parametrize("name,tmp", [(".hidden", ".hidden.ckpt.tmp"), ("run.ckpt", "run.ckpt.tmp"),
+                                      ("plain", "plain.ckpt.tmp"), ("d.x/.hidden", "d.x/.hidden.ckpt.tmp")])
+def test_checkpoint_temp_name_follows_with_extension(tmp_path, monkeypatch, name, tmp):
+    # Path::with_extension("ckpt.tmp") (checkpoint.rs:94): a directory in the
+    # way makes the final rename fail, so the temp file stays to be seen
+    monkeypatch.chdir(tmp_path)
+    os.makedirs(name)
+    with pytest.raises(D.DeferError):
+        _ck().save(name)
+    assert os.path.isfile(tmp), sorted(os.listdir("."))
+
+
 @pytest.mark.parametrize("mutate,err", [
     (lambda b: b.__setitem__(50, b[50] ^ 1), D.CheckpointError),
     (lambda b: b.__setitem__(0, ord("X")), D.CheckpointError),
