@@ -150,10 +150,10 @@ struct DBatch {
 // Trace record of one stage of one CTA (dataflow kernel): slot 0 = stage
 // entry, 1 = inputs received (after the poll), 2 + w = warp w done; warp 0
 // also marks 10 = RMS statistic ready / attention rows staged / sampler
-// inputs polled, 11 = first weight piece in shared memory / attention
-// scores done / token sampled, 12 = attention softmax done / sampler sum
-// rows ready, 13 = attention weighted sum done / sum walked, 14 = attention
-// units done / sampler CDF rows ready, 15 = attention combines done / CDF
+// started, 11 = first weight piece in shared memory / attention scores
+// done / token sampled, 12 = attention softmax done / sampler sum records
+// published, 13 = attention weighted sum done / sum walked, 14 = attention
+// units done / CDF records published, 15 = attention combines done / CDF
 // walked.
 constexpr int kTraceSlots = 16;
 

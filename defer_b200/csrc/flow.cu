@@ -228,6 +228,104 @@ __device__ __forceinline__ void producer_fail(FlowShared& sh, int* status) {
   atomicCAS(status, kStOk, kStTimeout);
 }
 
+// ------------------------------------------------- distributed sampler
+// Out of line (one copy, its own register budget): the records of rows
+// k0..k1 of one slot's logits held in shared memory (olg: logit i at
+// olg[i - k0 * 32]), published with tag tg; `pre` is the approximate
+// running sum before row k0. Warp 0 of a CTA.
+__device__ __noinline__ void records_rows(const float* olg, int k0, int k1, int V, float T, float M, float inv,
+                                          int cdf, const float* rm, const float* rz, float pre, uint64_t* rec,
+                                          float* tile, uint32_t tg) {
+  const int lane = threadIdx.x & 31;
+  const float scale = cdf ? inv : 1.0f;
+  const SharedVals v{olg, k0 * kSBlk, T, M, inv, cdf != 0};
+  const int n = min(V, k1 * kSBlk);
+  for (int row0 = k0; row0 < k1; row0 += 32) {
+    const int row = row0 + lane;
+    const bool has = row < k1;
+    float rs = 0.0f;
+    if (has) {
+      const float z = ld_f(rz + row);
+      rs = z > 0.0f ? z * expf(ld_f(rm + row) - M) * scale : 0.0f;
+    }
+    float inc = rs;
+    for (int off = 1; off < 32; off <<= 1) {
+      const float o = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += o;
+    }
+    int e = has ? predict_binade(pre + (inc - rs), rs) : kNoBinade;
+    pre += __shfl_sync(0xffffffffu, inc, 31);
+    int d0, d1;
+    rows_incr(v, n, row0, k1, e, tile, nullptr, &e, &d0, &d1);
+    if (has) {
+      if (d0 >= (1 << 25) || d1 >= (1 << 25)) d0 = d1 = 1 << 26;
+      const uint32_t code = e == kNoBinade ? 255u : e == kAnyBinade ? 254u : (uint32_t)(e + 128);
+      st_word(rec + (size_t)row * 2, (uint32_t)d0, tg);
+      st_word(rec + (size_t)row * 2 + 1, code | ((uint32_t)(d1 - d0 + 32768) << 8), tg);
+    }
+  }
+}
+
+// Out of line: the walk over every row's record (record words in smem at
+// `words`, decoded into the arrays after them) for the sum of e (cdf 0) or
+// the CDF search for r over slot logits lg; the values of the rows without
+// a prediction (those the walk will likely cross) are loaded up front into
+// a stash. Whole CTA.
+__device__ __noinline__ float walk_records(float* words, int V, const float* lg, float T, float M, float inv, int cdf,
+                                           float r, int* hit, float* prev, float* at) {
+  const int R = (V + kSBlk - 1) / kSBlk, NB = (R + 31) / 32;
+  int* re = reinterpret_cast<int*>(words + 2 * R);  // [R]
+  int* rd0 = re + R;                                // [R]
+  int* rd1 = rd0 + R;                               // [R]
+  int* be = rd1 + R;                                // [NB]
+  int* bd0 = be + NB;                               // [NB]
+  int* bd1 = bd0 + NB;                              // [NB]
+  float* stash = reinterpret_cast<float*>(bd1 + NB);  // [kStashRows][32]
+  __shared__ int s_nstash;
+  if (threadIdx.x == 0) s_nstash = 0;
+  DEFER_CTA_SYNC();
+  for (int row = threadIdx.x; row < R; row += kPT) {
+    const uint32_t w0 = __float_as_uint(words[2 * row]), w1 = __float_as_uint(words[2 * row + 1]);
+    const uint32_t code = w1 & 0xFFu;
+    re[row] = code == 255u ? kNoBinade : code == 254u ? kAnyBinade : (int)code - 128;
+    int slot = -1;  // a row the walk will likely cross: its values into the stash
+    if (code == 255u) {
+      slot = atomicAdd(&s_nstash, 1);
+      if (slot >= kStashRows) slot = -1;
+    }
+    rd0[row] = code == 255u ? slot : (int)w0;
+    rd1[row] = (int)w0 + (int)(w1 >> 8) - 32768;
+    if (slot >= 0) stash[slot * 32] = __int_as_float(row);  // the row, replaced by its values below
+  }
+  DEFER_CTA_SYNC();
+  const SampleVals v{lg, T, M, inv, cdf != 0};
+  {
+    // every stashed row's 32 values in one round of loads
+    const int ns = min(s_nstash, kStashRows);
+    float vals[(kStashRows * 32 + kPT - 1) / kPT];
+    int rows[(kStashRows * 32 + kPT - 1) / kPT];
+#pragma unroll
+    for (int k = 0; k < (kStashRows * 32 + kPT - 1) / kPT; k++) {
+      const int f = threadIdx.x + k * kPT, sl = f >> 5;
+      rows[k] = sl < ns ? __float_as_int(stash[sl * 32]) : -1;
+    }
+    DEFER_CTA_SYNC();
+#pragma unroll
+    for (int k = 0; k < (kStashRows * 32 + kPT - 1) / kPT; k++) {
+      const int f = threadIdx.x + k * kPT;
+      const int i = rows[k] * 32 + (f & 31);
+      vals[k] = (rows[k] >= 0 && i < V) ? v.raw(i) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < (kStashRows * 32 + kPT - 1) / kPT; k++) {
+      const int f = threadIdx.x + k * kPT;
+      if (rows[k] >= 0) stash[f] = (rows[k] * 32 + (f & 31) < V) ? v.of(vals[k]) : 0.0f;
+    }
+  }
+  DEFER_CTA_SYNC();
+  return exact_walk(v, V, cdf != 0, r, hit, prev, at, re, rd0, rd1, be, bd0, bd1, stash, nullptr);
+}
+
 // ------------------------------------------------------------------ polls
 // A wait longer than a hand-off (the token choice of SELECT, attention on a
 // few CTAs) would otherwise keep every thread of every waiting CTA
@@ -864,17 +962,121 @@ struct Flow {
     }
   }
 
+  // ------------------------------------------------- distributed sampler
+  // The exact sampler (phases.cuh) with its row passes spread over every
+  // CTA: each CTA computes the records (predicted binade and increments)
+  // of its own logits rows, which it holds in shared memory since its head
+  // stage, and publishes them as tagged words; the slot's owner CTA polls
+  // all records and walks them. Record of a row: word 0 = d0, word 1 =
+  // binade code (e + 128; 254 all-zero row, 255 no prediction) | (d1 - d0 +
+  // 32768) << 8.
+
+  // Sum over the CTA's phase threads (any order; every thread gets it).
+  __device__ float cta_sum_any(float v) {
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if ((threadIdx.x & 31) == 0) sh.ws[threadIdx.x >> 5][0] = v;
+    csync_();
+    float t = 0.0f;
+    for (int w = 0; w < kPW; w++) t += sh.ws[w][0];
+    csync_();
+    return t;
+  }
+
+  // Records of this CTA's rows of slot g's logits for the pass `cdf` (p = e
+  // * inv) or the sum of e, published with tag tg. Whole CTA.
+  __device__ void sampler_records(int g, float M, float inv, bool cdf, uint32_t tg) {
+    const float* rm = reinterpret_cast<const float*>(fb.esum) + (size_t)g * 2 * nblk;
+    const float* rz = rm + nblk;
+    const float scale = cdf ? inv : 1.0f;
+    // approximate running sum before this CTA's first row (any order)
+    float pre = 0.0f;
+    for (int r = threadIdx.x; r < k0; r += kPT) {
+      const float z = ld_f(rz + r);
+      pre += z > 0.0f ? z * expf(ld_f(rm + r) - M) * scale : 0.0f;
+    }
+    pre = cta_sum_any(pre);
+    if (threadIdx.x < 32)
+      records_rows(ol + (size_t)g * geo.ol_f, k0, k1, m.V, sh.sess[g].temperature, M, inv, cdf ? 1 : 0, rm, rz, pre,
+                   (cdf ? fb.crec : fb.zrec) + (size_t)g * nblk * 2, stage, tg);
+    csync_();
+  }
+
+  // The owner's walk over every CTA's records of slot b (tag tg): the sum of
+  // e (cdf false) or the CDF search for r. Whole CTA; false on failure.
+  __device__ bool sampler_walk(int b, float M, float inv, bool cdf, float r, uint32_t tg, float* total, int* hit,
+                               float* prev, float* at) {
+    do_poll(seg1((cdf ? fb.crec : fb.zrec) + (size_t)b * nblk * 2, stage, 2 * nblk, tg), false);
+    csync_();
+    if (fail()) return false;
+    *total = walk_records(stage, m.V, bt.logits + (size_t)b * m.V, sh.sess[b].temperature, M, inv, cdf ? 1 : 0, r, hit,
+                          prev, at);
+    return true;
+  }
+
   // ------------------------------------------------------------ select
   // Slot state update and token choice of step s for the slots this CTA
   // owns (ph_select), then the slot's step header: x = embedding row, step
   // info, RoPE rows. Returns false on failure.
-  __device__ bool select(int s) {
+  __device__ bool select(int s, unsigned first) {
     const int tid = threadIdx.x;
     const uint32_t tg = tag(s, 0);
     tr_entry(s, 0);
     // Fault drill (bt.stall): CTA 0 withholds the step header of step 0, so
     // every other CTA's first poll runs into its bounded wait.
     const bool withhold = bt.stall && s == 0 && cta == 0;
+    // Slots that sample at this step, known to every CTA: the previous
+    // step's header says so (or, at a run's first step, its programs).
+    unsigned smask = s == 0 ? first : 0u;
+    if (s > 0)
+      for (int g = 0; g < bt.B; g++)
+        if (sh.samp[g]) smask |= 1u << g;
+    if (smask) {
+      tr_mark(10);
+      const uint32_t tz = tag(s, sid_s1(m.L)), tc = tag(s, sid_s2(m.L));
+      // every CTA: M (the largest of the CTAs' maxima of s; each CTA
+      // released its logits and row statistics before its maximum) and the
+      // records of its rows in the sum of e
+      for (int g = 0; g < bt.B; g++) {
+        if (!((smask >> g) & 1u)) continue;
+        do_poll(Seg{fb.csm + (size_t)g * fb.cta_cap, stage, ncta, 1, fb.cta_cap, ncta, 1u,
+                    tag(s - 1, sid_head(m.L))},
+                true);
+        csync_();
+        if (fail()) return false;
+        float mx = -INFINITY;
+        for (int j = tid; j < ncta; j += kPT) mx = fmaxf(mx, stage[j]);
+        mx = cta_max(mx);
+        if (tid == 0) sh.M[g] = mx;
+        sampler_records(g, mx, 0.0f, false, tz);
+      }
+      tr_mark(12);
+      // owners: the exact sum, and 1 / sum for every CTA
+      for (int b = cta; b < bt.B; b += ncta) {
+        if (!((smask >> b) & 1u)) continue;
+        float Z, pv, at;
+        int hit;
+        if (!sampler_walk(b, sh.M[b], 0.0f, false, 0.0f, tz, &Z, &hit, &pv, &at)) return false;
+        const float inv = (Z > 0.0f && isfinite(Z)) ? __fdiv_rn(1.0f, Z) : 0.0f;
+        if (tid == 0) {
+          sh.Z[b] = Z;
+          sh.inv[b] = inv;
+          st_f(fb.invw + b, inv, tc);
+        }
+        csync_();
+      }
+      tr_mark(13);
+      // every CTA: the records of its rows in the CDF of p = e * (1 / sum)
+      for (int g = 0; g < bt.B; g++) {
+        if (!((smask >> g) & 1u)) continue;
+        do_poll(seg1(fb.invw + g, stage, 1, tc), false);
+        csync_();
+        if (fail()) return false;
+        const float inv = stage[0];
+        csync_();
+        sampler_records(g, sh.M[g], inv, true, tc);
+      }
+      tr_mark(14);
+    }
     for (int b = cta; b < bt.B; b += ncta) {
       DSlotState* st = sh.st + b;
       const DSession& S = sh.sess[b];
@@ -902,7 +1104,26 @@ struct Flow {
           const float T = S.temperature;
           float margin = 0.0f;
           uint32_t smp;
-          if (T != 0.0f) {
+          if (T != 0.0f && ((smask >> b) & 1u) && sh.Z[b] > 0.0f && isfinite(sh.Z[b])) {
+            // the CDF walk over every CTA's records
+            const float inv = sh.inv[b];
+            const float r = (float)(S.words[k] >> 8) * (1.0f / 16777216.0f);
+            float total, pv, at;
+            int hit;
+            if (!sampler_walk(b, sh.M[b], inv, true, r, tag(s, sid_s2(m.L)), &total, &hit, &pv, &at)) return false;
+            if (hit >= 0) {
+              smp = (uint32_t)hit;
+              margin = fminf(__fsub_rn(r, pv), __fsub_rn(at, r));
+            } else {  // r past the last CDF value: the last index with p > 0
+              const SampleVals vp{bt.logits + (size_t)b * m.V, T, sh.M[b], inv, true};
+              const int last = last_positive(vp, m.V);
+              smp = (uint32_t)(last < 0 ? 0 : last);
+              margin = __fsub_rn(r, total);
+            }
+            tr_mark(15);
+            tr_mark(11);
+          } else if (T != 0.0f && !((smask >> b) & 1u)) {
+            // (not announced by the previous header: the single-CTA sampler)
             // The previous step's logits are complete once every CTA's head
             // words are: each CTA released its logits stores before them.
             do_poll(Seg{fb.csm + (size_t)b * fb.cta_cap, stage, ncta, 1, fb.cta_cap, ncta, 1u,
@@ -922,6 +1143,8 @@ struct Flow {
                                rm + nblk, mk);
             tr_mark(11);
           } else {
+            // greedy, or a degenerate sum of e (the reference's one-hot argmax)
+            if (T != 0.0f) margin = NAN;
             float* pr = stage;
             float* lm = stage + 2 * ncta;
             int* la = reinterpret_cast<int*>(lm + ncta);
@@ -1326,7 +1549,7 @@ struct Flow {
     if (fail()) return false;
     tr_recv(s, sid_gu(l));
     const uint32_t tg = tag(s, sid_gu(l));
-    gemv<true, 4>(sl, stage, m.H, m.H, kEpiGateUp, l, tg);  // ~20 rows a CTA: one pass of 4 rows a warp
+    gemv<true>(sl, stage, m.H, m.H, kEpiGateUp, l, tg);  // the QKV loop's code: one copy stays in the i-cache
     tr_done(s, sid_gu(l));
     return true;
   }
@@ -1477,7 +1700,7 @@ struct Flow {
     }
     if (first) restat(first);  // the greedy statistics of the previous run's logits
     for (int s = 0; s < nsteps; s++) {
-      if (!select(s)) return;
+      if (!select(s, first)) return;
       bool ended = false;
       for (int l = 0; l < m.L; l++) {
         if (!qkv(s, l)) {  // failure, or (at layer 0) no active slot
@@ -1627,7 +1850,7 @@ size_t flow_tagged_words(const DModel& m, int B, int max_chunks, int sms) {
   const int nblk = (m.V + kSBlk - 1) / kSBlk;
   const size_t xw = (size_t)header_words(m);
   return (size_t)B * (xw + (size_t)m.QD + 2 * m.KVD + m.QD + m.FF) +
-         (size_t)B * m.NH * max_chunks * (m.HD + 2) + (size_t)B * sms * 3 + (size_t)B * nblk * 2;
+         (size_t)B * m.NH * max_chunks * (m.HD + 2) + (size_t)B * sms * 3 + (size_t)B * nblk * 5 + (size_t)B;
 }
 
 FlowBufs flow_bufs(const DModel& m, int B, int max_chunks, int sms, uint64_t* w) {
@@ -1651,7 +1874,11 @@ FlowBufs flow_bufs(const DModel& m, int B, int max_chunks, int sms, uint64_t* w)
   w += (size_t)B * sms;
   f.esum = w;
   w += (size_t)B * nblk;
-  f.psum = w;
+  f.zrec = w;
+  w += (size_t)B * nblk * 2;
+  f.crec = w;
+  w += (size_t)B * nblk * 2;
+  f.invw = w;
   f.epoch = 1;
   return f;
 }

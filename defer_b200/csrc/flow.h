@@ -18,8 +18,10 @@ struct FlowBufs {
   uint64_t* pt;    // [B][NH][max_chunks][HD + 2] attention chunk partials (m, l, acc)
   uint64_t* cl;    // [B][cta_cap][2] per-CTA greedy best (value, index bits)
   uint64_t* csm;   // [B][cta_cap] per-CTA max of s = l / T
-  uint64_t* esum;  // [B][nblk] block sums of e
-  uint64_t* psum;  // [B][nblk] block sums of p
+  uint64_t* esum;  // [B][2][nblk] floats, not tagged: per logits row the max of s, the sum of exp(s - max)
+  uint64_t* zrec;  // [B][nblk][2] exact sampler: per row its binade and increments in the sum of e
+  uint64_t* crec;  // [B][nblk][2] the same in the CDF of p
+  uint64_t* invw;  // [B] 1 / (sum of e) of a sampling slot
   int xw;          // words per slot of xt
   int cta_cap;     // CTA capacity of cl / csm
   uint32_t epoch;  // first tag of this run

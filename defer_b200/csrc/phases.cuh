@@ -651,6 +651,20 @@ struct SampleVals {
   __device__ __forceinline__ float operator()(int i) const { return of(raw(i)); }
 };
 
+// v_i of one exact pass from values held in shared memory: base[i - i0]
+// is logit i (a CTA's own logits rows).
+struct SharedVals {
+  const float* base;
+  int i0;
+  float T, M, inv;
+  bool p;
+  __device__ __forceinline__ float raw(int i) const { return base[i - i0]; }
+  __device__ __forceinline__ float of(float l) const {
+    const float e = e_of(l, T, M);
+    return p ? __fmul_rn(e, inv) : e;
+  }
+};
+
 // Shared memory of sample_exact (floats): per row its sum, prefix, binade
 // and two increments; per block the same but the sum; the stashed rows;
 // one [32][9] transposition tile per warp.
@@ -699,10 +713,20 @@ __device__ __forceinline__ int walk_level(float& S, int j0, int n, int e, Incr d
   const int eS = walk_binade(S);
   const bool ok = e == kAnyBinade || (eS != kNoBinade && e == eS);
   Incr t = (in && ok && e != kAnyBinade) ? d : Incr{0, 0};
+  if (__all_sync(0xffffffffu, t.d0 == t.d1)) {  // no ties: a plain prefix sum
+    int x = t.d0;
 #pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const Incr o{__shfl_up_sync(0xffffffffu, t.d0, off), __shfl_up_sync(0xffffffffu, t.d1, off)};
-    if (lane >= off) t = incr_then(o, t);
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x = min(x + y, 1 << 26);
+    }
+    t.d0 = t.d1 = x;
+  } else {
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Incr o{__shfl_up_sync(0xffffffffu, t.d0, off), __shfl_up_sync(0xffffffffu, t.d1, off)};
+      if (lane >= off) t = incr_then(o, t);
+    }
   }
   float Sj = S;
   bool stop = !ok;
@@ -746,6 +770,163 @@ __device__ __forceinline__ bool walk_values(float& S, float& P, int& hit, float 
   return false;
 }
 
+// Predicted binade of a row whose running sum goes from about lo to about
+// lo + rs, or kNoBinade (straddles a power of two, starts at 0, or leaves
+// the range where the integer steps apply).
+__device__ __forceinline__ int predict_binade(float lo, float rs) {
+  const float hi = lo + rs;
+  if (lo > 0.0f && isfinite(hi)) {
+    const int el = binade_of(lo);
+    if (el == binade_of(hi) && el >= -102 && el <= 100) return el;
+  }
+  return kNoBinade;
+}
+
+// Increments of the 32 rows row0, row0 + 1, ... (lane = row; rows >= R
+// contribute nothing) under each lane's predicted binade e. The values
+// arrive 8 columns at a time through the warp's [32][9] tile of shared
+// memory (a load instruction covers 4 rows x 8 columns: whole 32-byte
+// sectors), computed where they are loaded; then each lane adds its row's
+// values in order, keeping the running parity that ties need, for an even
+// and an odd incoming multiple. *e_out: e, or kAnyBinade for an all-zero
+// row; a kNoBinade row's values go to stash_row when it is non-null. Warp.
+template <class Src>
+__device__ __forceinline__ void rows_incr(const Src& v, int n, int row0, int R, int e, float* tile, float* stash_row,
+                                          int* e_out, int* d0, int* d1) {
+  const int lane = threadIdx.x & 31;
+  const float scale = e != kNoBinade ? pow2f(23 - e) : 0.0f;
+  int a0 = 0, a1 = 0;  // increments for an even / odd incoming multiple
+  bool nz = false;
+  for (int c = 0; c < 4; c++) {
+    float raw[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int i = (row0 + k * 4 + (lane >> 3)) * 32 + c * 8 + (lane & 7);
+      raw[k] = i < n ? v.raw(i) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int rr = k * 4 + (lane >> 3);
+      const int i = (row0 + rr) * 32 + c * 8 + (lane & 7);
+      tile[rr * 9 + (lane & 7)] = i < n ? v.of(raw[k]) : 0.0f;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float x = tile[lane * 9 + j];
+      nz |= x != 0.0f;
+      if (stash_row) stash_row[c * 8 + j] = x;
+      if (e != kNoBinade) {
+        const float y = __fmul_rn(x, scale);  // exact: a power-of-two scale
+        if (!(y < 33554432.0f)) {  // leaves the binade (or not finite)
+          a0 = a1 = 1 << 26;
+        } else {
+          const float f = floorf(y);
+          const float fr = __fsub_rn(y, f);
+          const int fl = (int)f;
+          if (fr == 0.5f) {  // a tie goes to the even total
+            a0 += fl + ((a0 + fl) & 1);
+            a1 += fl + ((1 + a1 + fl) & 1);
+          } else {
+            const int q = fl + (fr > 0.5f ? 1 : 0);
+            a0 += q;
+            a1 += q;
+          }
+          a0 = min(a0, 1 << 26);
+          a1 = min(a1, 1 << 26);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  (void)R;
+  *e_out = nz ? e : kAnyBinade;
+  *d0 = nz ? a0 : 0;
+  *d1 = nz ? a1 : 0;
+}
+
+// Block composition and the walk over the rows' records (re, rd0, rd1:
+// binade and increments, the stash slot of a kNoBinade row in rd0, -1 when
+// its values are not stashed): the sum or CDF search of exact_seq. be, bd0,
+// bd1: [NB] scratch. Whole CTA. `marks`: one stamp when the walk ends.
+template <class Src>
+static __device__ float exact_walk(const Src& v, int n, bool find, float r, int* found, float* prev, float* at,
+                                   const int* re, const int* rd0, const int* rd1, int* be, int* bd0, int* bd1,
+                                   const float* stash, unsigned long long* marks) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = (n + 31) / 32, NB = (R + 31) / 32;
+  __shared__ float s_res, s_prev, s_at;
+  __shared__ int s_found;
+  // blocks: the composed increments when every row is all zeros or runs in
+  // one binade
+  for (int b = warp; b < NB; b += kPW) {
+    const int row = b * 32 + lane;
+    const int e = row < R ? re[row] : kAnyBinade;
+    int common = kAnyBinade;
+    const unsigned some = __ballot_sync(0xffffffffu, e != kAnyBinade);
+    if (some) {
+      const int e0 = __shfl_sync(0xffffffffu, e, __ffs(some) - 1);
+      common = __all_sync(0xffffffffu, e == kAnyBinade || e == e0) ? e0 : kNoBinade;
+    }
+    Incr d = (row < R && e != kAnyBinade && e != kNoBinade) ? Incr{rd0[row], rd1[row]} : Incr{0, 0};
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Incr o{__shfl_up_sync(0xffffffffu, d.d0, off), __shfl_up_sync(0xffffffffu, d.d1, off)};
+      if (lane >= off) d = incr_then(o, d);
+    }
+    if (lane == 31) {
+      be[b] = common;
+      bd0[b] = d.d0;
+      bd1[b] = d.d1;
+    }
+  }
+  DEFER_CTA_SYNC();
+  if (warp == 0) {  // the walk; every lane keeps the exact S
+    float S = 0.0f, P = 0.0f;
+    int hit = -1;
+    bool end = false;
+    for (int c = 0; c < NB && !end; c += 32) {
+      const int nb = min(32, NB - c);
+      const int eb = lane < nb ? be[c + lane] : kAnyBinade;
+      const Incr db = lane < nb ? Incr{bd0[c + lane], bd1[c + lane]} : Incr{0, 0};
+      for (int jb = 0; jb < nb && !end;) {
+        const int fb = walk_level(S, jb, nb, eb, db, find, r);
+        if (fb >= nb) break;
+        const int b = c + fb;  // into the block's rows
+        const int nr = min(32, R - b * 32);
+        const int er = lane < nr ? re[b * 32 + lane] : kAnyBinade;
+        const Incr dr = lane < nr ? Incr{rd0[b * 32 + lane], rd1[b * 32 + lane]} : Incr{0, 0};
+        for (int jr = 0; jr < nr && !end;) {
+          const int fr = walk_level(S, jr, nr, er, dr, find, r);
+          if (fr >= nr) break;
+          const int row = b * 32 + fr;  // into the row's values
+          const int e_row = __shfl_sync(0xffffffffu, er, fr);
+          const int slot = __shfl_sync(0xffffffffu, dr.d0, fr);
+          const int i = row * 32 + lane;
+          const float x = (e_row == kNoBinade && slot >= 0) ? stash[slot * 32 + lane] : (i < n ? v(i) : 0.0f);
+          end = walk_values(S, P, hit, x, row * 32, find, r);
+          jr = fr + 1;
+        }
+        jb = fb + 1;
+      }
+    }
+    if (lane == 0) {
+      if (marks) marks[0] = gtimer_ns();
+      s_res = S;
+      s_found = hit;
+      s_prev = P;
+      s_at = S;
+    }
+  }
+  DEFER_CTA_SYNC();
+  const float res = s_res;
+  if (found) *found = s_found;
+  if (prev) *prev = s_prev;
+  if (at) *at = s_at;
+  DEFER_CTA_SYNC();
+  return res;
+}
+
 // The sequential fp32 sum of v(0..n) (find = false), or the CDF search
 // (find = true): the first i with v_i > 0 and r < S_{i+1}, reported with
 // the CDF before and at it; S is returned either way (the total when not
@@ -765,8 +946,7 @@ static __device__ float exact_seq(const SampleVals& v, int n, bool find, float r
   int* bd1 = bd0 + NB;                             // [NB]
   float* bp = reinterpret_cast<float*>(bd1 + NB);  // [NB] block prefix
   float* stash = bp + NB;                          // [kStashRows][32]
-  __shared__ float s_res, s_prev, s_at;
-  __shared__ int s_found, s_nstash;
+  __shared__ int s_nstash;
   if (tid == 0) s_nstash = 0;
   // prefixes: rows inside their block (warp per block), then the blocks
   for (int b = warp; b < NB; b += kPW) {
@@ -801,156 +981,28 @@ static __device__ float exact_seq(const SampleVals& v, int n, bool find, float r
   DEFER_CTA_SYNC();
   for (int row = tid; row < R; row += kPT) rp[row] += bp[row >> 5];
   DEFER_CTA_SYNC();
-  // rows: predicted binade and increments. A warp takes a block of 32 rows,
-  // lane = row. The values arrive 8 columns at a time through the warp's
-  // [32][9] tile of shared memory (a load instruction covers 4 rows x 8
-  // columns: whole 32-byte sectors), computed where they are loaded; then
-  // each lane adds its row's values in order, keeping the running parity
-  // that ties need, for an even and an odd incoming multiple.
+  // rows: predicted binade and increments, a warp per block of 32 rows
   float* tile = stash + 32 * kStashRows + warp * (32 * 9);
   for (int b = warp; b < NB; b += kPW) {
     const int row = b * 32 + lane;
     const bool has = row < R;
-    int e = kNoBinade;
-    if (has) {
-      const float lo = rp[row], hi = lo + rs[row];
-      if (lo > 0.0f && isfinite(hi)) {
-        const int el = binade_of(lo);
-        if (el == binade_of(hi) && el >= -102 && el <= 100) e = el;
-      }
-    }
+    int e = has ? predict_binade(rp[row], rs[row]) : kNoBinade;
     int slot = -1;  // stash slot of a row the walk will likely cross
     if (has && e == kNoBinade) {
       slot = atomicAdd(&s_nstash, 1);
       if (slot >= kStashRows) slot = -1;
     }
-    const float scale = e != kNoBinade ? pow2f(23 - e) : 0.0f;
-    int a0 = 0, a1 = 0;  // increments for an even / odd incoming multiple
-    bool nz = false;
-    for (int c = 0; c < 4; c++) {
-      float raw[8];
-#pragma unroll
-      for (int k = 0; k < 8; k++) {
-        const int i = (b * 32 + k * 4 + (lane >> 3)) * 32 + c * 8 + (lane & 7);
-        raw[k] = i < n ? v.raw(i) : 0.0f;
-      }
-#pragma unroll
-      for (int k = 0; k < 8; k++) {
-        const int rr = k * 4 + (lane >> 3);
-        const int i = (b * 32 + rr) * 32 + c * 8 + (lane & 7);
-        tile[rr * 9 + (lane & 7)] = i < n ? v.of(raw[k]) : 0.0f;
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const float x = tile[lane * 9 + j];
-        nz |= x != 0.0f;
-        if (slot >= 0) stash[slot * 32 + c * 8 + j] = x;
-        if (e != kNoBinade) {
-          const float y = __fmul_rn(x, scale);  // exact: a power-of-two scale
-          if (!(y < 33554432.0f)) {  // leaves the binade (or not finite)
-            a0 = a1 = 1 << 26;
-          } else {
-            const float f = floorf(y);
-            const float fr = __fsub_rn(y, f);
-            const int fl = (int)f;
-            if (fr == 0.5f) {  // a tie goes to the even total
-              a0 += fl + ((a0 + fl) & 1);
-              a1 += fl + ((1 + a1 + fl) & 1);
-            } else {
-              const int q = fl + (fr > 0.5f ? 1 : 0);
-              a0 += q;
-              a1 += q;
-            }
-            a0 = min(a0, 1 << 26);
-            a1 = min(a1, 1 << 26);
-          }
-        }
-      }
-      __syncwarp();
-    }
+    int d0, d1;
+    rows_incr(v, n, b * 32, R, e, tile, slot >= 0 ? stash + slot * 32 : nullptr, &e, &d0, &d1);
     if (has) {
-      if (!nz) {
-        re[row] = kAnyBinade;
-        rd0[row] = rd1[row] = 0;
-      } else {
-        re[row] = e;
-        rd0[row] = e == kNoBinade ? slot : a0;
-        rd1[row] = a1;
-      }
-    }
-  }
-  DEFER_CTA_SYNC();
-  // blocks: the composed increments when every row is all zeros or runs in
-  // one binade
-  for (int b = warp; b < NB; b += kPW) {
-    const int row = b * 32 + lane;
-    const int e = row < R ? re[row] : kAnyBinade;
-    int common = kAnyBinade;
-    for (int j = 0; j < 32; j++) {
-      const int ej = __shfl_sync(0xffffffffu, e, j);
-      if (ej == kAnyBinade) continue;
-      if (common == kAnyBinade) common = ej;
-      else if (ej != common) common = kNoBinade;
-    }
-    Incr d = (row < R && e != kAnyBinade && e != kNoBinade) ? Incr{rd0[row], rd1[row]} : Incr{0, 0};
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const Incr o{__shfl_up_sync(0xffffffffu, d.d0, off), __shfl_up_sync(0xffffffffu, d.d1, off)};
-      if (lane >= off) d = incr_then(o, d);
-    }
-    if (lane == 31) {
-      be[b] = common;
-      bd0[b] = d.d0;
-      bd1[b] = d.d1;
+      re[row] = e;
+      rd0[row] = e == kNoBinade ? slot : d0;
+      rd1[row] = d1;
     }
   }
   DEFER_CTA_SYNC();
   if (marks && tid == 0) marks[0] = gtimer_ns();
-  if (warp == 0) {  // the walk; every lane keeps the exact S
-    float S = 0.0f, P = 0.0f;
-    int hit = -1;
-    bool end = false;
-    for (int c = 0; c < NB && !end; c += 32) {
-      const int nb = min(32, NB - c);
-      const int eb = lane < nb ? be[c + lane] : kAnyBinade;
-      const Incr db = lane < nb ? Incr{bd0[c + lane], bd1[c + lane]} : Incr{0, 0};
-      for (int jb = 0; jb < nb && !end;) {
-        const int fb = walk_level(S, jb, nb, eb, db, find, r);
-        if (fb >= nb) break;
-        const int b = c + fb;  // into the block's rows
-        const int nr = min(32, R - b * 32);
-        const int er = lane < nr ? re[b * 32 + lane] : kAnyBinade;
-        const Incr dr = lane < nr ? Incr{rd0[b * 32 + lane], rd1[b * 32 + lane]} : Incr{0, 0};
-        for (int jr = 0; jr < nr && !end;) {
-          const int fr = walk_level(S, jr, nr, er, dr, find, r);
-          if (fr >= nr) break;
-          const int row = b * 32 + fr;  // into the row's values
-          const int e_row = __shfl_sync(0xffffffffu, er, fr);
-          const int slot = __shfl_sync(0xffffffffu, dr.d0, fr);
-          const int i = row * 32 + lane;
-          const float x = (e_row == kNoBinade && slot >= 0) ? stash[slot * 32 + lane] : (i < n ? v(i) : 0.0f);
-          end = walk_values(S, P, hit, x, row * 32, find, r);
-          jr = fr + 1;
-        }
-        jb = fb + 1;
-      }
-    }
-    if (lane == 0) {
-      if (marks) marks[1] = gtimer_ns();
-      s_res = S;
-      s_found = hit;
-      s_prev = P;
-      s_at = S;
-    }
-  }
-  DEFER_CTA_SYNC();
-  const float res = s_res;
-  if (found) *found = s_found;
-  if (prev) *prev = s_prev;
-  if (at) *at = s_at;
-  DEFER_CTA_SYNC();
-  return res;
+  return exact_walk(v, n, find, r, found, prev, at, re, rd0, rd1, be, bd0, bd1, stash, marks ? marks + 1 : nullptr);
 }
 
 // Row sums of v (the walk's steering; any rounding) into smem[0..R).
@@ -1049,7 +1101,8 @@ static __device__ int last_positive(const SampleVals& v, int V) {
 // exp(s - max) (block_stats), which steer the walk in place of a pass of
 // row sums. `marks` (instrumentation, or null): globaltimer stamps when
 // each pass's rows and blocks are ready and when its walk ends (4 words).
-static __device__ uint32_t sample_exact(const float* lg, int V, float T, uint32_t word, float* margin, float* smem,
+static __device__ __noinline__ uint32_t sample_exact(const float* lg, int V, float T, uint32_t word, float* margin,
+                                                    float* smem,
                                        bool m_given = false, float m_max = 0.0f, const float* row_m = nullptr,
                                        const float* row_z = nullptr, unsigned long long* marks = nullptr) {
   int amax = 0;

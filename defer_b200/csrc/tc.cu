@@ -22,27 +22,30 @@
 // (g * 8 + c) * 128 bytes, so the leading byte offset (next k chunk) is 128
 // and the stride byte offset (next row group) is 1024. Activations of one
 // K block: [hi][mid][lo] or [hi][lo], 128 rows each (16 KB per term);
-// weights are packed once into tiles of 64 rows x 64 k, [hi][lo] per tile
-// (16 KB, 8 KB when bf16), ordered row tile major, K block minor, so a
+// weights are packed once into tiles of 128 rows x 64 k, [hi][lo] per tile
+// (32 KB, 16 KB when bf16), ordered row tile major, K block minor, so a
 // CTA's K range is contiguous.
 //
-// GEMM kernel (k_tc_gemm): one CTA per (64-row tile, K split); 6 warps.
-// Warp 4 streams A and W blocks with bulk copies into a 4-stage ring
-// (mbarrier complete_tx); warp 5 issues the MMAs (M = 128, N = 64, K = 16
-// per instruction, 3 products per k step) and commits each stage back to
-// the producer. The tensor core's own fp32 accumulation loses accuracy over
+// GEMM kernel (k_tc_gemm): one CTA per (128-row tile, K split); 6 warps.
+// Warp 4 streams A and W blocks with bulk copies into a 3-stage ring of
+// 64 KB stages (mbarrier complete_tx); warp 5 issues the MMAs (M = 128,
+// N = 128, K = 16 per instruction, 3 products per k step) and commits each
+// stage back to the producer. The tensor core's own fp32 accumulation loses accuracy over
 // long chains (on the 8B widths a 32-block chain was ~10x less accurate than
 // fp32 dot products), so the K range is cut into groups of kTcGroup blocks:
 // each group accumulates from zero into one of two TMEM buffers, and warps
 // 0-3 read it (tcgen05.ld, TMEM lane = slot) and add it into registers in
 // group order while the next group runs in the other buffer; they store the
-// 64 partial sums at the end. Every wait is bounded; a wait that runs out
-// sets the status word, the CTA drains its copies and MMAs in flight and
-// frees its tensor memory.
+// 128 partial sums at the end. A 128-row tile reads the activation block
+// once per 128 weight rows: with fp32 weights the bytes a CTA brings in
+// are half weights, half activations (a 64-row tile: one third weights).
+// Every wait is bounded; a wait that runs out sets the status word, the CTA
+// drains its copies and MMAs in flight and frees its tensor memory.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <vector>
@@ -55,12 +58,12 @@
 namespace defer {
 namespace {
 
-constexpr int kTcBN = 64;                        // weight rows per tile (MMA N)
+constexpr int kTcBN = 128;                       // weight rows per tile (MMA N)
 constexpr int kTcBK = 64;                        // K per block
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 3;
 constexpr int kTcABytes = kTcM * kTcBK * 2;      // one bf16 term of an activation block
 constexpr int kTcWBytes = kTcBN * kTcBK * 2;     // one bf16 term of a weight tile
-constexpr int kTcStageMax = 3 * kTcABytes + kTcWBytes;  // the largest stage: 3 + 1 terms (2 + 2 is less)
+constexpr int kTcStageMax = 3 * kTcABytes + kTcWBytes;  // the largest stage: 3 + 1 terms (2 + 2 is the same)
 constexpr int kTcThreads = 192;  // warps 0-3 drain TMEM, 4 copies, 5 issues MMAs
 constexpr int kTcGroup = 4;      // K blocks per tensor-core accumulation chain
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
@@ -137,7 +140,8 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 struct TcGemmArgs {
   const unsigned char* A;  // [nkb][aterms][kTcM * kTcBK] bf16
   const unsigned char* W;  // [ntile][nkb][wterms][kTcBN * kTcBK] bf16
-  float* Y;                // [splits][kTcM][n_pad] partial sums
+  float* Y;                // [splits][kTcM][n_pad] partial sums; the total in split 0's rows
+  unsigned* tickets;       // [ntile] splits of the tile finished
   int nkb, splits, n_pad, wterms, aterms;  // aterms = 3 when wterms = 1, else 2
   int* status;
   const int* active;  // the step's "any slot active" flag, or null (always run)
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   extern __shared__ __align__(1024) unsigned char tsm[];
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], acc_full[2], acc_empty[2], drain;
   __shared__ uint32_t tmem_base;
-  __shared__ int failed;
+  __shared__ int failed, last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (g.active && __ldcg(g.active) == 0) return;  // no slot fed a token this step
   const int tile = blockIdx.x / g.splits, sp = blockIdx.x % g.splits;
@@ -172,7 +176,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 5) {  // two 128 x 64 fp32 accumulators: 128 columns of tensor memory
+  if (warp == 5) {  // two 128 x 128 fp32 accumulators: 256 columns of tensor memory
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base)),
                  "r"(2 * kTcBN)
                  : "memory");
@@ -186,6 +190,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   const unsigned a_bytes = (unsigned)g.aterms * kTcABytes;
   const unsigned stage_bytes = a_bytes + (unsigned)wtile;  // a multiple of 1024
 
+  float acc[kTcBN];  // the draining warps' sums (slot = TMEM lane, one row tile)
+#pragma unroll
+  for (int c = 0; c < kTcBN; c++) acc[c] = 0.0f;
   if (warp == 4) {
     if (lane == 0) {
       // producer: this CTA's K blocks of A and of its weight tile
@@ -255,12 +262,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
       if (!mb_wait(&drain, 0u)) atomicCAS(g.status, kStOk, kStTimeout);
     }
   } else {
-    // warps 0-3: lane r of TMEM = slot r; each group's 64 partial sums are
+    // warps 0-3: lane r of TMEM = slot r; each group's 128 partial sums are
     // added into registers in group order (fp32, round to nearest), which
     // keeps every tensor-core accumulation chain to kTcGroup K blocks
-    float acc[kTcBN];
-#pragma unroll
-    for (int c = 0; c < kTcBN; c++) acc[c] = 0.0f;
     bool ok = true;
     for (int gi = 0; gi < ngroups; gi++) {
       const int buf = gi & 1;
@@ -288,15 +292,48 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     if (!ok) {
       if (lane == 0) atomicCAS(g.status, kStOk, kStTimeout);
       *(volatile int*)&failed = 1;
-    } else {
+    } else if (g.splits > 1) {
       const int r = warp * 32 + lane;  // an empty K range stores zeros
       float* y = g.Y + ((size_t)sp * kTcM + r) * g.n_pad + (size_t)tile * kTcBN;
 #pragma unroll
       for (int c = 0; c < kTcBN; c += 4)
         *reinterpret_cast<float4*>(y + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+      __threadfence();  // this split's partials before its ticket
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (g.splits > 1 && tid == 0) {
+    const unsigned t = atomicAdd(g.tickets + tile, 1u);
+    last = t == (unsigned)g.splits - 1;
+    if (last) g.tickets[tile] = 0;  // every split has counted: zero for the next GEMM
+  }
+  __syncthreads();
+  if (warp < 4 && !*(volatile int*)&failed && (g.splits == 1 || last)) {
+    // the tile's total, the splits added in split order (this split's own
+    // partials from registers), into split 0's rows
+    if (g.splits > 1) __threadfence();
+    const int r = warp * 32 + lane;
+    float* y0 = g.Y + (size_t)r * g.n_pad + (size_t)tile * kTcBN;
+#pragma unroll
+    for (int c = 0; c < kTcBN; c += 4) {
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < g.splits; q++) {
+        float4 p;
+        if (q == sp) p = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+        else p = __ldcg(reinterpret_cast<const float4*>(g.Y + ((size_t)q * kTcM + r) * g.n_pad + (size_t)tile * kTcBN + c));
+        if (q == 0) {
+          t = p;
+        } else {
+          t.x = __fadd_rn(t.x, p.x);
+          t.y = __fadd_rn(t.y, p.y);
+          t.z = __fadd_rn(t.z, p.z);
+          t.w = __fadd_rn(t.w, p.w);
+        }
+      }
+      *reinterpret_cast<float4*>(y0 + c) = t;
+    }
+  }
   __syncthreads();
   if (warp == 5) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -441,41 +478,57 @@ __global__ void k_tc_qkv_epi(DModel m, DBatch bt, int l, const float* Y, int spl
   }
 }
 
-// x[b] += Y (the O or down projection, split sums in order), then slot row
-// b of the next projection's A operand from the updated row, normalised
-// with `nw` (the next RMSNorm's weights): one launch and one pass over x
-// instead of a residual kernel and a prep. One CTA per slot.
-__global__ void __launch_bounds__(256) k_tc_resid_prep(DModel m, DBatch bt, const float* Y, int splits, int n_pad,
+// x[b] += Y (the O or down projection's total), then slot row b of the next
+// projection's A operand from the updated row, normalised with `nw` (the
+// next RMSNorm's weights): one launch and one pass over x instead of a
+// residual kernel and a prep. One CTA per slot.
+__global__ void __launch_bounds__(256) k_tc_resid_prep(DModel m, DBatch bt, const float* __restrict__ Y, int n_pad,
                                                        const float* nw, int nkb, unsigned char* A,
                                                        const int* active, int aterms) {
   const int b = blockIdx.x, tid = threadIdx.x;
   if (active && __ldcg(active) == 0) return;
   const bool live = b < bt.B && live_slot(bt, b);
-  float* xr = bt.x + (size_t)b * m.H;
-  if (live)
-    for (int k = tid; k < m.H; k += 256) xr[k] = __fadd_rn(xr[k], ysum(Y, splits, n_pad, b, k));
+  float* __restrict__ xr = bt.x + (size_t)b * m.H;
+  const float* __restrict__ yr = Y + (size_t)b * n_pad;
+  if (live) {
+#pragma unroll 4
+    for (int k = tid; k < m.H; k += 256) xr[k] = __fadd_rn(__ldcg(xr + k), __ldcg(yr + k));
+  }
   __syncthreads();
   prep_row(xr, nw, m.eps, m.H, nkb, live, b, A, aterms);
 }
 
-// g = act(gate) * up of slot row b, straight into the down projection's A
-// operand (g itself is not stored). One CTA per slot.
-__global__ void __launch_bounds__(256) k_tc_gu_prep(DModel m, DBatch bt, const float* Y, int splits, int n_pad,
+// g = act(gate) * up of slot row b (gate and up interleaved in Y), straight
+// into the down projection's A operand (g itself is not stored). Grid:
+// (slot, 2048-wide slice of g).
+__global__ void __launch_bounds__(256) k_tc_gu_prep(DModel m, DBatch bt, const float* __restrict__ Y, int n_pad,
                                                     int nkb, unsigned char* A, const int* active, int aterms) {
-  const int b = blockIdx.x, tid = threadIdx.x;
+  const int b = blockIdx.x;
   if (active && __ldcg(active) == 0) return;
   const bool live = b < bt.B && live_slot(bt, b);
-  const int kpad = nkb * kTcBK;
-  for (int k0 = tid * 8; k0 < kpad; k0 += 256 * 8) {
-    float v[8];
+  const int k0 = (blockIdx.y * 256 + threadIdx.x) * 8;
+  if (k0 >= nkb * kTcBK) return;
+  float v[8];
+  if (live && k0 + 8 <= m.FF) {
+    const float4* yp = reinterpret_cast<const float4*>(Y + (size_t)b * n_pad + 2 * (size_t)k0);
+    float4 q[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) q[e] = __ldcg(yp + e);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      v[2 * e] = gate_act_mul(m, q[e].x, q[e].y);
+      v[2 * e + 1] = gate_act_mul(m, q[e].z, q[e].w);
+    }
+  } else {
 #pragma unroll
     for (int e = 0; e < 8; e++) {
       const int j = k0 + e;
-      v[e] = (live && j < m.FF) ? gate_act_mul(m, ysum(Y, splits, n_pad, b, 2 * j), ysum(Y, splits, n_pad, b, 2 * j + 1))
+      v[e] = (live && j < m.FF) ? gate_act_mul(m, __ldcg(Y + (size_t)b * n_pad + 2 * j),
+                                               __ldcg(Y + (size_t)b * n_pad + 2 * j + 1))
                                 : 0.0f;
     }
-    put_a_chunk(A, b, k0, v, aterms);
   }
+  put_a_chunk(A, b, k0, v, aterms);
 }
 
 __global__ void k_tc_head_epi(DModel m, DBatch bt, const float* Y, int splits, int n_pad) {
@@ -557,10 +610,13 @@ void tc_prep(const float* x, const float* nw, float eps, int K, int B, const DSl
 }
 
 int tc_splits(const TcMatrix& w, int sms) {
-  // enough CTAs to stream the weights from every SM, at least 4 K blocks each
-  int s = 1;
-  while (w.ntile * s < sms && w.nkb / (2 * s) >= 4) s *= 2;
-  return s;
+  // The last split of a tile reads the other splits' 64 KB partials, so s
+  // splits cost a tile about W/s + (s - 1) * 64 KB of one SM's reads (W the
+  // tile's weight bytes): s near sqrt(W / 64 KB); at most one wave of CTAs
+  // (one CTA per SM) and at least 4 K blocks a split.
+  const double wtile = (double)kTcBN * w.K * 2.0 * w.wterms;
+  const int best = (int)std::lround(std::sqrt(wtile / (64.0 * 1024.0)));
+  return std::max(1, std::min({sms / std::max(1, w.ntile), w.nkb / 4, best}));
 }
 
 // Kernel attributes are set once per device.
@@ -573,8 +629,8 @@ static bool first_on_device(unsigned long long& mask) {
   return true;
 }
 
-void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s,
-             const int* active) {
+void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, unsigned* tickets, int* status,
+             cudaStream_t s, const int* active) {
   static unsigned long long attr = 0;
   if (first_on_device(attr))
     DEFER_CUDA(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -584,6 +640,7 @@ void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, in
   g.A = A;
   g.W = w.data;
   g.Y = Y;
+  g.tickets = tickets;
   g.nkb = w.nkb;
   g.splits = splits;
   g.n_pad = w.ntile * kTcBN;
@@ -627,22 +684,23 @@ void launch_steps_tc(const DModel& m, const TcModel& tm, const DBatch& bt0, int 
       const TcLayer& T = tm.layers[l];
       // the A operand of QKV is ready (the step's first prep, or the last
       // layer's residual)
-      tc_gemm(wk.A, T.qkv, wk.Y, T.s_qkv, bt.status, st, act);
-      k_tc_qkv_epi<<<ew, 256, 0, st>>>(m, bt, l, wk.Y, T.s_qkv, T.qkv.ntile * kTcBN);
+      tc_gemm(wk.A, T.qkv, wk.Y, T.s_qkv, wk.tickets, bt.status, st, act);
+      k_tc_qkv_epi<<<ew, 256, 0, st>>>(m, bt, l, wk.Y, 1, T.qkv.ntile * kTcBN);
       k_tc_attn<<<std::min(attn_units, sms * 8), kThreads, smem, st>>>(m, bt, l);
       k_tc_combine<<<sms, kThreads, 0, st>>>(m, bt);
       tc_prep(bt.att, nullptr, 0.0f, m.QD, bt.B, bt.st, wk.A, at, st, act);
-      tc_gemm(wk.A, T.o, wk.Y, T.s_o, bt.status, st, act);
-      k_tc_resid_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.s_o, T.o.ntile * kTcBN, T.ffn_norm, nkb_h, wk.A, act, at);
-      tc_gemm(wk.A, T.gu, wk.Y, T.s_gu, bt.status, st, act);
-      k_tc_gu_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.s_gu, T.gu.ntile * kTcBN, nkb_ff, wk.A, act, at);
-      tc_gemm(wk.A, T.down, wk.Y, T.s_down, bt.status, st, act);
+      tc_gemm(wk.A, T.o, wk.Y, T.s_o, wk.tickets, bt.status, st, act);
+      k_tc_resid_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.o.ntile * kTcBN, T.ffn_norm, nkb_h, wk.A, act, at);
+      tc_gemm(wk.A, T.gu, wk.Y, T.s_gu, wk.tickets, bt.status, st, act);
+      k_tc_gu_prep<<<dim3(kTcM, div_up((long)nkb_ff * kTcBK, 2048)), 256, 0, st>>>(m, bt, wk.Y, T.gu.ntile * kTcBN,
+                                                                            nkb_ff, wk.A, act, at);
+      tc_gemm(wk.A, T.down, wk.Y, T.s_down, wk.tickets, bt.status, st, act);
       const float* next_norm = l + 1 < m.L ? tm.layers[l + 1].attn_norm : m.norm;
-      k_tc_resid_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.s_down, T.down.ntile * kTcBN, next_norm, nkb_h, wk.A, act,
+      k_tc_resid_prep<<<kTcM, 256, 0, st>>>(m, bt, wk.Y, T.down.ntile * kTcBN, next_norm, nkb_h, wk.A, act,
                                            at);
     }
-    tc_gemm(wk.A, tm.head, wk.Y, tm.s_head, bt.status, st, act);
-    k_tc_head_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, tm.s_head, tm.head.ntile * kTcBN);
+    tc_gemm(wk.A, tm.head, wk.Y, tm.s_head, wk.tickets, bt.status, st, act);
+    k_tc_head_epi<<<ew, 256, 0, st>>>(m, bt, wk.Y, 1, tm.head.ntile * kTcBN);
     k_tc_stats<<<std::min(sms * 4, std::max(1, bt.B * nb / kPW)), kThreads, 0, st>>>(m, bt);
   }
   k_tc_finalize<<<bt.B, kThreads, 0, st>>>(bt);
@@ -687,22 +745,27 @@ void tc_gemm_check(int device, const float* X, int M, const float* W, int N, int
   DEFER_CUDA(cudaMemset(status, 0, sizeof(int)));
   TcMatrix w = tc_pack(dW, N, K, w_bf16, static_cast<unsigned char*>(dP), st);
   const int splits = tc_splits(w, sms);
+  void* dT = nullptr;
   DEFER_CUDA(cudaMalloc(&dY, tc_y_floats(w, splits) * sizeof(float)));
+  DEFER_CUDA(cudaMalloc(&dT, (size_t)w.ntile * sizeof(unsigned)));
+  DEFER_CUDA(cudaMemset(dT, 0, (size_t)w.ntile * sizeof(unsigned)));
   tc_prep(static_cast<float*>(dX), nullptr, 0.0f, K, M, static_cast<DSlotState*>(dS), static_cast<unsigned char*>(dA),
           tc_aterms(w), st);
-  tc_gemm(static_cast<unsigned char*>(dA), w, static_cast<float*>(dY), splits, status, st);
-  std::vector<float> part(tc_y_floats(w, splits));
+  tc_gemm(static_cast<unsigned char*>(dA), w, static_cast<float*>(dY), splits, static_cast<unsigned*>(dT), status,
+          st);
+  const size_t n_pad = (size_t)w.ntile * kTcBN;
+  std::vector<float> tot((size_t)kTcM * n_pad);  // the total, in split 0's rows
+  std::vector<unsigned> tickets(w.ntile);
   int stat = 0;
-  DEFER_CUDA(cudaMemcpyAsync(part.data(), dY, part.size() * 4, cudaMemcpyDeviceToHost, st));
+  DEFER_CUDA(cudaMemcpyAsync(tot.data(), dY, tot.size() * 4, cudaMemcpyDeviceToHost, st));
+  DEFER_CUDA(cudaMemcpyAsync(tickets.data(), dT, tickets.size() * sizeof(unsigned), cudaMemcpyDeviceToHost, st));
   DEFER_CUDA(cudaMemcpyAsync(&stat, status, sizeof(int), cudaMemcpyDeviceToHost, st));
   DEFER_CUDA(cudaStreamSynchronize(st));
-  const size_t n_pad = (size_t)w.ntile * kTcBN;
   for (int r = 0; r < M; r++)
-    for (int n = 0; n < N; n++) {
-      float v = part[(size_t)r * n_pad + n];
-      for (int sp = 1; sp < splits; sp++) v += part[((size_t)sp * kTcM + r) * n_pad + n];
-      Y[(size_t)r * N + n] = v;
-    }
+    for (int n = 0; n < N; n++) Y[(size_t)r * N + n] = tot[(size_t)r * n_pad + n];
+  for (unsigned t : tickets)
+    if (t != 0 && stat == kStOk) fail(kCuda, "tensor-core GEMM: a tile's split tickets were left non-zero");
+  cudaFree(dT);
   cudaFree(dW);
   cudaFree(dX);
   cudaFree(dP);
@@ -716,6 +779,7 @@ void tc_gemm_check(int device, const float* X, int M, const float* W, int N, int
 TcModel::~TcModel() {
   if (arena) cudaFree(arena);
   if (y_buf) cudaFree(y_buf);
+  if (tickets) cudaFree(tickets);
 }
 
 TcModel* tc_model_build(const DModel& m, const std::vector<DLayer>& layers, int sms, cudaStream_t st) {
@@ -759,6 +823,12 @@ TcModel* tc_model_build(const DModel& m, const std::vector<DLayer>& layers, int 
   DEFER_CUDA(cudaMemsetAsync(t->work.A, 0, act, st));
   DEFER_CUDA(cudaMalloc(&t->y_buf, t->max_y * sizeof(float)));
   t->work.Y = t->y_buf;
+  int max_tiles = t->head.ntile;
+  for (const TcLayer& L : t->layers)
+    max_tiles = std::max({max_tiles, L.qkv.ntile, L.o.ntile, L.gu.ntile, L.down.ntile});
+  DEFER_CUDA(cudaMalloc(&t->tickets, (size_t)max_tiles * sizeof(unsigned)));
+  DEFER_CUDA(cudaMemsetAsync(t->tickets, 0, (size_t)max_tiles * sizeof(unsigned), st));
+  t->work.tickets = t->tickets;
   DEFER_CUDA(cudaStreamSynchronize(st));
   return t.release();
 }

@@ -30,6 +30,7 @@ struct TcLayer {
 struct TcWork {
   unsigned char* A = nullptr;
   float* Y = nullptr;
+  unsigned* tickets = nullptr;  // per row tile: K splits finished (zero between GEMMs)
 };
 
 struct TcModel {
@@ -38,6 +39,7 @@ struct TcModel {
   int s_head = 1;
   void* arena = nullptr;  // the packed weights, then the activation operand (owned)
   float* y_buf = nullptr; // partial sums (owned)
+  unsigned* tickets = nullptr;  // per row tile (owned)
   size_t bytes = 0;
   size_t max_act = 0;     // bytes of the largest activation operand
   size_t max_y = 0;       // floats of the largest partial-sum buffer
@@ -64,10 +66,12 @@ int tc_aterms(const TcMatrix& w);
 // non-null, split into `aterms` bf16 terms.
 void tc_prep(const float* x, const float* nw, float eps, int K, int B, const DSlotState* st, unsigned char* A,
              int aterms, cudaStream_t s, const int* active = nullptr);
-// Y[split][slot][n] partial sums of A . W^T.
-// With `active` (a device flag) the launch does nothing when it is 0.
-void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, int* status, cudaStream_t s,
-             const int* active = nullptr);
+// Y[slot][n] = A . W^T (the K splits' partial sums added in split order by
+// the last split of each row tile; Y holds splits x [128][n_pad] floats of
+// scratch). `tickets`: ntile zeroed counters, left zeroed. With `active` (a
+// device flag) the launch does nothing when it is 0.
+void tc_gemm(const unsigned char* A, const TcMatrix& w, float* Y, int splits, unsigned* tickets, int* status,
+             cudaStream_t s, const int* active = nullptr);
 
 // Runs nsteps token steps of a batch of at most 128 slots whose programs
 // never sample, the projections on the tensor cores.
