@@ -837,6 +837,13 @@ def trace_summary(tr, L: int):
                          "sum_walk": round(float(np.median(sel[:, 13] - sel[:, 12])) / 1e3, 3),
                          "cdf_rows": round(float(np.median(sel[:, 14] - sel[:, 13])) / 1e3, 3),
                          "cdf_walk": round(float(np.median(sel[:, 15] - sel[:, 14])) / 1e3, 3),
+                         "last_sum_records": round(float(tr[:, 0, 12].max() - np.median(sel[:, 10])) / 1e3, 3),
+                         "sum_polled": round(float(np.median(sel[:, 16] - sel[:, 12])) / 1e3, 3),
+                         "sum_decoded": round(float(np.median(sel[:, 17] - sel[:, 16])) / 1e3, 3),
+                         "sum_walked": round(float(np.median(sel[:, 18] - sel[:, 17])) / 1e3, 3),
+                         "cdf_polled": round(float(np.median(sel[:, 19] - sel[:, 14])) / 1e3, 3),
+                         "cdf_decoded": round(float(np.median(sel[:, 20] - sel[:, 19])) / 1e3, 3),
+                         "cdf_walked": round(float(np.median(sel[:, 21] - sel[:, 20])) / 1e3, 3),
                          "done": round(float(np.median(done[own, 0] - sel[:, 0])) / 1e3, 3)}
     t0 = tr[:, 0, 0][tr[:, 0, 0] > 0].min() if (tr[:, 0, 0] > 0).any() else 0
     last = int(max(i for i in range(len(names)) if ends[i] > 0))

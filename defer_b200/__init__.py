@@ -210,8 +210,8 @@ class Model:
         _check(_L().defer_debug_trace_arm(self._h, int(step)))
 
     def trace(self) -> np.ndarray:
-        """The last trace as uint64 [ctas, stages, 16] globaltimer ns: slot 0
-        stage entry, 1 inputs received, 2 + w phase warp w done, 10-13 warp
+        """The last trace as uint64 [ctas, stages, 24] globaltimer ns: slot 0
+        stage entry, 1 inputs received, 2 + w phase warp w done, 10-21 warp
         0's sub-stage marks (see defer_debug_trace_arm; 0 = not reached)."""
         n = ctypes.c_size_t(0)
         c, st = ctypes.c_int32(0), ctypes.c_int32(0)

@@ -154,7 +154,8 @@ struct DBatch {
 // done / token sampled, 12 = attention softmax done / sampler sum records
 // published, 13 = attention weighted sum done / sum walked, 14 = attention
 // units done / CDF records published, 15 = attention combines done / CDF
-// walked.
-constexpr int kTraceSlots = 16;
+// walked; SELECT's owner also marks 16 / 19 = sum / CDF records polled,
+// 17 / 20 = decoded and crossed rows loaded, 18 / 21 = walk done.
+constexpr int kTraceSlots = 24;
 
 }  // namespace defer

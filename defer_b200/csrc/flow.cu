@@ -266,13 +266,20 @@ __device__ __noinline__ void records_rows(const float* olg, int k0, int k1, int 
   }
 }
 
+// Rows the owner's walk loads up front, and the staging floats the walk
+// needs: record words, decoded rows and blocks, the stash.
+constexpr int kWalkStash = 32;
+__host__ __device__ constexpr size_t walk_records_floats(int V) {
+  return 5 * (size_t)((V + 31) / 32) + 3 * (size_t)(((V + 31) / 32 + 31) / 32) + 32 * (size_t)kWalkStash;
+}
+
 // Out of line: the walk over every row's record (record words in smem at
 // `words`, decoded into the arrays after them) for the sum of e (cdf 0) or
 // the CDF search for r over slot logits lg; the values of the rows without
 // a prediction (those the walk will likely cross) are loaded up front into
 // a stash. Whole CTA.
 __device__ __noinline__ float walk_records(float* words, int V, const float* lg, float T, float M, float inv, int cdf,
-                                           float r, int* hit, float* prev, float* at) {
+                                           float r, int* hit, float* prev, float* at, unsigned long long* marks) {
   const int R = (V + kSBlk - 1) / kSBlk, NB = (R + 31) / 32;
   int* re = reinterpret_cast<int*>(words + 2 * R);  // [R]
   int* rd0 = re + R;                                // [R]
@@ -280,7 +287,7 @@ __device__ __noinline__ float walk_records(float* words, int V, const float* lg,
   int* be = rd1 + R;                                // [NB]
   int* bd0 = be + NB;                               // [NB]
   int* bd1 = bd0 + NB;                              // [NB]
-  float* stash = reinterpret_cast<float*>(bd1 + NB);  // [kStashRows][32]
+  float* stash = reinterpret_cast<float*>(bd1 + NB);  // [kWalkStash][32]
   __shared__ int s_nstash;
   if (threadIdx.x == 0) s_nstash = 0;
   DEFER_CTA_SYNC();
@@ -291,7 +298,7 @@ __device__ __noinline__ float walk_records(float* words, int V, const float* lg,
     int slot = -1;  // a row the walk will likely cross: its values into the stash
     if (code == 255u) {
       slot = atomicAdd(&s_nstash, 1);
-      if (slot >= kStashRows) slot = -1;
+      if (slot >= kWalkStash) slot = -1;
     }
     rd0[row] = code == 255u ? slot : (int)w0;
     rd1[row] = (int)w0 + (int)(w1 >> 8) - 32768;
@@ -301,29 +308,30 @@ __device__ __noinline__ float walk_records(float* words, int V, const float* lg,
   const SampleVals v{lg, T, M, inv, cdf != 0};
   {
     // every stashed row's 32 values in one round of loads
-    const int ns = min(s_nstash, kStashRows);
-    float vals[(kStashRows * 32 + kPT - 1) / kPT];
-    int rows[(kStashRows * 32 + kPT - 1) / kPT];
+    const int ns = min(s_nstash, kWalkStash);
+    float vals[(kWalkStash * 32 + kPT - 1) / kPT];
+    int rows[(kWalkStash * 32 + kPT - 1) / kPT];
 #pragma unroll
-    for (int k = 0; k < (kStashRows * 32 + kPT - 1) / kPT; k++) {
+    for (int k = 0; k < (kWalkStash * 32 + kPT - 1) / kPT; k++) {
       const int f = threadIdx.x + k * kPT, sl = f >> 5;
       rows[k] = sl < ns ? __float_as_int(stash[sl * 32]) : -1;
     }
     DEFER_CTA_SYNC();
 #pragma unroll
-    for (int k = 0; k < (kStashRows * 32 + kPT - 1) / kPT; k++) {
+    for (int k = 0; k < (kWalkStash * 32 + kPT - 1) / kPT; k++) {
       const int f = threadIdx.x + k * kPT;
       const int i = rows[k] * 32 + (f & 31);
       vals[k] = (rows[k] >= 0 && i < V) ? v.raw(i) : 0.0f;
     }
 #pragma unroll
-    for (int k = 0; k < (kStashRows * 32 + kPT - 1) / kPT; k++) {
+    for (int k = 0; k < (kWalkStash * 32 + kPT - 1) / kPT; k++) {
       const int f = threadIdx.x + k * kPT;
       if (rows[k] >= 0) stash[f] = (rows[k] * 32 + (f & 31) < V) ? v.of(vals[k]) : 0.0f;
     }
   }
   DEFER_CTA_SYNC();
-  return exact_walk(v, V, cdf != 0, r, hit, prev, at, re, rd0, rd1, be, bd0, bd1, stash, nullptr);
+  if (marks && threadIdx.x == 0) marks[0] = now_ns();
+  return exact_walk(v, V, cdf != 0, r, hit, prev, at, re, rd0, rd1, be, bd0, bd1, stash, marks ? marks + 1 : nullptr);
 }
 
 // ------------------------------------------------------------------ polls
@@ -1008,8 +1016,12 @@ struct Flow {
     do_poll(seg1((cdf ? fb.crec : fb.zrec) + (size_t)b * nblk * 2, stage, 2 * nblk, tg), false);
     csync_();
     if (fail()) return false;
+    unsigned long long* mk = (bt.trace && cur_s == bt.trace_step && cur_sid == 0)
+                                 ? bt.trace + (size_t)cta * KS * kTraceSlots + (cdf ? 19 : 16)
+                                 : nullptr;
+    if (mk && threadIdx.x == 0) mk[0] = now_ns();
     *total = walk_records(stage, m.V, bt.logits + (size_t)b * m.V, sh.sess[b].temperature, M, inv, cdf ? 1 : 0, r, hit,
-                          prev, at);
+                          prev, at, mk ? mk + 1 : nullptr);
     return true;
   }
 
@@ -1825,6 +1837,7 @@ FlowPlan flow_plan(const DModel& m, int B, int max_chunks, int sms) {
   st = std::max(st, (size_t)nblk + ng2 + ng3 + 8);
   st = std::max(st, (size_t)4 * grid);
   st = std::max(st, sample_exact_floats(m.V));  // the exact sampler of SELECT
+  st = std::max(st, walk_records_floats(m.V));  // the owner's walk over every CTA's records
   st = (st + 31) & ~(size_t)31;
   const size_t rest = 4 * (st + (size_t)G * (ol_f + ox_f + rope_f) + nw_f) + (((size_t)m.L * sizeof(DLayer) + 15) & ~(size_t)15);
   const size_t budget = (size_t)optin > kStaticSmemReserve ? (size_t)optin - kStaticSmemReserve : 0;

@@ -707,12 +707,18 @@ __device__ __forceinline__ Incr value_incr(float v, int e, bool* tie) {
 // all zeros or runs in S's binade, S stays below the next power of two and
 // (searching) r >= S. Returns the first item that stops it (n if none),
 // with S the exact sum before that item.
-__device__ __forceinline__ int walk_level(float& S, int j0, int n, int e, Incr d, bool find, float r) {
+struct WalkPos {
+  float S;
+  int f;
+};
+// Out of line (one warm copy for the three levels of the walk).
+static __device__ __noinline__ WalkPos walk_level_call(float S, int j0, int n, int e, int d0, int d1, int find,
+                                                       float r) {
   const int lane = threadIdx.x & 31;
   const bool in = lane >= j0 && lane < n;
   const int eS = walk_binade(S);
   const bool ok = e == kAnyBinade || (eS != kNoBinade && e == eS);
-  Incr t = (in && ok && e != kAnyBinade) ? d : Incr{0, 0};
+  Incr t = (in && ok && e != kAnyBinade) ? Incr{d0, d1} : Incr{0, 0};
   if (__all_sync(0xffffffffu, t.d0 == t.d1)) {  // no ties: a plain prefix sum
     int x = t.d0;
 #pragma unroll
@@ -740,39 +746,52 @@ __device__ __forceinline__ int walk_level(float& S, int j0, int n, int e, Incr d
   const unsigned sm = __ballot_sync(0xffffffffu, in && stop);
   const int f = sm ? __ffs(sm) - 1 : n;
   const float Sb = __shfl_sync(0xffffffffu, Sj, f > 0 ? min(f, 32) - 1 : 0);
-  if (f > j0) S = Sb;
-  return f;
+  return WalkPos{f > j0 ? Sb : S, f};
+}
+__device__ __forceinline__ int walk_level(float& S, int j0, int n, int e, Incr d, bool find, float r) {
+  const WalkPos p = walk_level_call(S, j0, n, e, d.d0, d.d1, find ? 1 : 0, r);
+  S = p.S;
+  return p.f;
 }
 
 // One row value by value (v = this lane's value, base = index of lane 0):
 // integer runs in S's binade, fp32 additions where they stop. True when the
 // walk ends here (the CDF hit, or a sum that is no longer finite).
-__device__ __forceinline__ bool walk_values(float& S, float& P, int& hit, float v, int base, bool find, float r) {
+struct WalkVals {
+  float S, P;
+  int hit, end;
+};
+static __device__ __noinline__ WalkVals walk_values_call(float S, float P, int hit, float v, int base, int find,
+                                                         float r) {
   int j0 = 0;
   for (int round = 0; round <= 32; round++) {  // every round consumes a value
     const int eS = walk_binade(S);
     bool tie;
     const Incr d = eS != kNoBinade ? value_incr(v, eS, &tie) : Incr{0, 0};
     const int e = v == 0.0f ? kAnyBinade : (eS != kNoBinade ? eS : kNoBinade);
-    const int f = walk_level(S, j0, 32, e, d, find, r);
-    if (f >= 32) return false;
+    const int f = walk_level(S, j0, 32, e, d, find != 0, r);
+    if (f >= 32) return WalkVals{S, P, hit, 0};
     const float vf = __shfl_sync(0xffffffffu, v, f);
     const float Sp = S;
     S = __fadd_rn(S, vf);
-    if (find && vf > 0.0f && r < S) {
-      hit = base + f;
-      P = Sp;
-      return true;
-    }
-    if (!isfinite(S)) return true;
+    if (find && vf > 0.0f && r < S) return WalkVals{S, Sp, base + f, 1};
+    if (!isfinite(S)) return WalkVals{S, P, hit, 1};
     j0 = f + 1;
   }
-  return false;
+  return WalkVals{S, P, hit, 0};
+}
+__device__ __forceinline__ bool walk_values(float& S, float& P, int& hit, float v, int base, bool find, float r) {
+  const WalkVals w = walk_values_call(S, P, hit, v, base, find ? 1 : 0, r);
+  S = w.S;
+  P = w.P;
+  hit = w.hit;
+  return w.end != 0;
 }
 
 // Predicted binade of a row whose running sum goes from about lo to about
 // lo + rs, or kNoBinade (straddles a power of two, starts at 0, or leaves
-// the range where the integer steps apply).
+// the range where the integer steps apply): a kNoBinade row is one the
+// walk expects to enter value by value.
 __device__ __forceinline__ int predict_binade(float lo, float rs) {
   const float hi = lo + rs;
   if (lo > 0.0f && isfinite(hi)) {

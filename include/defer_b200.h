@@ -236,15 +236,16 @@ DEFER_API int defer_model_timing(defer_model* m, double* device_ms, uint64_t* ru
 /* Instrumentation (no counterpart in the reference): arms a per-stage time
  * trace of step `step` (< 0 disarms) of the next dataflow token-loop run on
  * this model. For every CTA and stage of that step the kernel records
- * globaltimer nanoseconds in 16 slots: 0 stage entry, 1 inputs received
+ * globaltimer nanoseconds in 24 slots: 0 stage entry, 1 inputs received
  * (after the poll), 2 + w phase warp w finished its share; warp 0 also
- * marks 10 RMS statistic ready / attention rows staged, 11 first weight
- * piece in shared memory / attention scores done, 12 attention softmax
- * done, 13 attention weighted sum done. Stages: 0 select, then
+ * marks sub-stages in slots 10-21 (RMS statistic ready, first weight piece
+ * in shared memory; attention rows staged, scores, softmax, weighted sum,
+ * units, combines; in select the sampler's records published, polled,
+ * decoded and walked for the sum and for the CDF). Stages: 0 select, then
  * per layer l: 1 + 5l QKV, 2 + 5l attention, 3 + 5l O, 4 + 5l gate/up,
- * 5 + 5l down; then head, sampler sums 1 and 2. */
+ * 5 + 5l down; then head and two unused slots. */
 DEFER_API int defer_debug_trace_arm(defer_model* m, int32_t step);
-/* The last trace: n = ctas * stages * 16 stamps (0 = not reached). */
+/* The last trace: n = ctas * stages * 24 stamps (0 = not reached). */
 DEFER_API int defer_debug_trace_read(const defer_model* m, uint64_t* out, size_t cap, size_t* n, int32_t* ctas,
                                      int32_t* stages);
 /* Fault drill (no counterpart in the reference; the test of the device
