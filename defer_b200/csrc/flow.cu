@@ -331,7 +331,8 @@ __device__ __noinline__ float walk_records(float* words, int V, const float* lg,
   }
   DEFER_CTA_SYNC();
   if (marks && threadIdx.x == 0) marks[0] = now_ns();
-  return exact_walk(v, V, cdf != 0, r, hit, prev, at, re, rd0, rd1, be, bd0, bd1, stash, marks ? marks + 1 : nullptr);
+  return exact_walk(v, V, cdf != 0, r, hit, prev, at, re, rd0, rd1, be, bd0, bd1, stash, marks ? marks + 1 : nullptr,
+                    reinterpret_cast<int*>(words));  // the record words are decoded: [2R] segments
 }
 
 // ------------------------------------------------------------------ polls

@@ -871,11 +871,45 @@ __device__ __forceinline__ void rows_incr(const Src& v, int n, int row0, int R, 
 template <class Src>
 static __device__ float exact_walk(const Src& v, int n, bool find, float r, int* found, float* prev, float* at,
                                    const int* re, const int* rd0, const int* rd1, int* be, int* bd0, int* bd1,
-                                   const float* stash, unsigned long long* marks) {
+                                   const float* stash, unsigned long long* marks, int* seg) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int R = (n + 31) / 32, NB = (R + 31) / 32;
   __shared__ float s_res, s_prev, s_at;
   __shared__ int s_found;
+  // segments: within a block, the rows between rows without a prediction.
+  // seg[2 row] = the increments d0 from the segment's first row through
+  // this one, seg[2 row + 1] = their binade code (e + 128, 254 all zero,
+  // 255 mixed) << 16 | (d1 - d0 + 32768). A walk entering a segment at its
+  // first row crosses it with one uniform step instead of a warp scan.
+  for (int b = warp; b < NB; b += kPW) {
+    const int row = b * 32 + lane;
+    const int e = row < R ? re[row] : kAnyBinade;
+    const bool flag = e == kNoBinade;
+    const unsigned fm = __ballot_sync(0xffffffffu, flag);
+    const unsigned below = fm & ((1u << lane) - 1u);
+    const int start = below ? 32 - __clz(below) : 0;
+    const bool real = !flag && e != kAnyBinade;
+    // binade of the segment's first row with a prediction, if any
+    const unsigned rm = __ballot_sync(0xffffffffu, real) & ~((1u << start) - 1u);
+    const int first = rm ? __ffs(rm) - 1 : 32;
+    const int ef = __shfl_sync(0xffffffffu, e, first < 32 ? first : 0);
+    const unsigned mm = __ballot_sync(0xffffffffu, real && e != ef);  // (a real row has first <= lane)
+    const unsigned span = (lane == 31 ? 0xffffffffu : ((1u << (lane + 1)) - 1u)) & ~((1u << start) - 1u);
+    const bool uniform = (mm & span) == 0u;
+    Incr t = real ? Incr{rd0[row], rd1[row]} : Incr{0, 0};
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const Incr o{__shfl_up_sync(0xffffffffu, t.d0, off), __shfl_up_sync(0xffffffffu, t.d1, off)};
+      if (lane >= off && lane - off >= start) t = incr_then(o, t);
+    }
+    if (row < R && !flag) {
+      const int es = !uniform ? kNoBinade : (first < 32 && first <= lane) ? ef : kAnyBinade;
+      const uint32_t code = es == kNoBinade ? 255u : es == kAnyBinade ? 254u : (uint32_t)(es + 128);
+      const bool sat = t.d0 >= (1 << 25) || t.d1 >= (1 << 25);
+      seg[2 * row] = sat ? (1 << 26) : t.d0;
+      seg[2 * row + 1] = (int)((code << 16) | (uint32_t)((sat ? 0 : t.d1 - t.d0) + 32768));
+    }
+  }
   // blocks: the composed increments when every row is all zeros or runs in
   // one binade
   for (int b = warp; b < NB; b += kPW) {
@@ -915,7 +949,44 @@ static __device__ float exact_walk(const Src& v, int n, bool find, float r, int*
         const int nr = min(32, R - b * 32);
         const int er = lane < nr ? re[b * 32 + lane] : kAnyBinade;
         const Incr dr = lane < nr ? Incr{rd0[b * 32 + lane], rd1[b * 32 + lane]} : Incr{0, 0};
+        const unsigned fmask = __ballot_sync(0xffffffffu, lane < nr && er == kNoBinade);
         for (int jr = 0; jr < nr && !end;) {
+          if (jr == 0 || ((fmask >> (jr - 1)) & 1u)) {
+            // at a segment's first row: its rows up to the next row without
+            // a prediction in one step, when they run in S's binade
+            const unsigned ahead = fmask & ~((1u << jr) - 1u);
+            const int endr = ahead ? __ffs(ahead) - 1 : nr;
+            bool stepped = endr == jr;  // an empty segment
+            if (endr > jr) {
+              const int k = b * 32 + endr - 1;
+              const int w0 = seg[2 * k], w1 = seg[2 * k + 1];
+              const uint32_t code = (uint32_t)w1 >> 16;
+              const int eS = walk_binade(S);
+              if (code == 254u) {
+                stepped = true;  // all zeros
+              } else if (code != 255u && eS != kNoBinade && (int)code - 128 == eS) {
+                const int M = (int)__fmul_rn(S, pow2f(23 - eS));
+                const int dd = (M & 1) ? w0 + (w1 & 0xFFFF) - 32768 : w0;
+                if (M + dd < (1 << 24)) {
+                  const float Sn = __fmul_rn((float)(M + dd), pow2f(eS - 23));
+                  if (!(find && r < Sn)) {
+                    S = Sn;
+                    stepped = true;
+                  }
+                }
+              }
+            }
+            if (stepped) {
+              if (endr >= nr) break;
+              const int row = b * 32 + endr;  // the row without a prediction, value by value
+              const int slot = __shfl_sync(0xffffffffu, dr.d0, endr);
+              const int i = row * 32 + lane;
+              const float x = slot >= 0 ? stash[slot * 32 + lane] : (i < n ? v(i) : 0.0f);
+              end = walk_values(S, P, hit, x, row * 32, find, r);
+              jr = endr + 1;
+              continue;
+            }
+          }
           const int fr = walk_level(S, jr, nr, er, dr, find, r);
           if (fr >= nr) break;
           const int row = b * 32 + fr;  // into the row's values
@@ -1021,7 +1092,8 @@ static __device__ float exact_seq(const SampleVals& v, int n, bool find, float r
   }
   DEFER_CTA_SYNC();
   if (marks && tid == 0) marks[0] = gtimer_ns();
-  return exact_walk(v, n, find, r, found, prev, at, re, rd0, rd1, be, bd0, bd1, stash, marks ? marks + 1 : nullptr);
+  return exact_walk(v, n, find, r, found, prev, at, re, rd0, rd1, be, bd0, bd1, stash, marks ? marks + 1 : nullptr,
+                    reinterpret_cast<int*>(rs));  // the row sums and prefixes are done with: [2R] segments
 }
 
 // Row sums of v (the walk's steering; any rounding) into smem[0..R).
