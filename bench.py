@@ -702,6 +702,7 @@ def main(argv=None):
                          "the 1.7B shape's gate/up matrix (16384 x 2048, fp32 weights)")
     ap.add_argument("--profile-slots", type=int, default=512)
     ap.add_argument("--profile-prompt", type=int, default=128)
+    ap.add_argument("--profile-gen", type=int, default=2, help="sampled tokens per session of --profile-case batched")
     ap.add_argument("--trace", action="store_true",
                     help="no measurement: per-stage critical-path breakdown of the dataflow kernel from "
                          "globaltimer stamps of one traced step (--profile-prompt tokens of context)")
@@ -712,7 +713,7 @@ def main(argv=None):
     if a.trace:
         return profile_trace(a.profile_prompt, a.trace_out)
     if a.profile_case == "batched":
-        return profile_case_batched(a.profile_slots, a.profile_prompt)
+        return profile_case_batched(a.profile_slots, a.profile_prompt, a.profile_gen)
     if a.profile_case == "ablation":
         return profile_case_ablation()
     if a.profile_case == "tc-gemm":
@@ -875,10 +876,10 @@ def profile_trace(context: int, out: str = None):
     return 0
 
 
-def profile_case_batched(n: int, plen: int):
-    """n sessions (plen-token uniform prompts, T=0.8, 2 sampled tokens) as one
-    batch on the per-stage launch path, so that ncu sees every stage of the
-    batched step as its own kernel."""
+def profile_case_batched(n: int, plen: int, gen: int = 2):
+    """n sessions (plen-token uniform prompts, T=0.8, `gen` sampled tokens) as
+    one batch on the per-stage launch path, so that ncu sees every stage of
+    the batched step as its own kernel."""
     os.environ["DEFER_B200_PHASED"] = "1"
     import numpy as np
     import defer_b200 as D
@@ -887,8 +888,8 @@ def profile_case_batched(n: int, plen: int):
     rng = np.random.default_rng(3)
     prompts = [[int(t) for t in rng.integers(0, m.config.vocab_size, plen)] for _ in range(n)]
     seeds = [D.seed_from_u64(i) for i in range(n)]
-    _, ms = D.generate_batch(m, prompts, seeds, [0.8] * n, [2] * n, batch=n)
-    print(json.dumps({"profile_case": "batched", "slots": n, "steps": plen + 2, "device_ms": ms}))
+    _, ms = D.generate_batch(m, prompts, seeds, [0.8] * n, [gen] * n, batch=n)
+    print(json.dumps({"profile_case": "batched", "slots": n, "steps": plen + gen, "device_ms": ms}))
     return 0
 
 

@@ -711,8 +711,7 @@ struct WalkPos {
   float S;
   int f;
 };
-// Out of line (one warm copy for the three levels of the walk).
-static __device__ __noinline__ WalkPos walk_level_call(float S, int j0, int n, int e, int d0, int d1, int find,
+static __device__ __forceinline__ WalkPos walk_level_call(float S, int j0, int n, int e, int d0, int d1, int find,
                                                        float r) {
   const int lane = threadIdx.x & 31;
   const bool in = lane >= j0 && lane < n;
@@ -761,7 +760,7 @@ struct WalkVals {
   float S, P;
   int hit, end;
 };
-static __device__ __noinline__ WalkVals walk_values_call(float S, float P, int hit, float v, int base, int find,
+static __device__ __forceinline__ WalkVals walk_values_call(float S, float P, int hit, float v, int base, int find,
                                                          float r) {
   int j0 = 0;
   for (int round = 0; round <= 32; round++) {  // every round consumes a value
@@ -1192,7 +1191,7 @@ static __device__ int last_positive(const SampleVals& v, int V) {
 // exp(s - max) (block_stats), which steer the walk in place of a pass of
 // row sums. `marks` (instrumentation, or null): globaltimer stamps when
 // each pass's rows and blocks are ready and when its walk ends (4 words).
-static __device__ __noinline__ uint32_t sample_exact(const float* lg, int V, float T, uint32_t word, float* margin,
+static __device__ uint32_t sample_exact(const float* lg, int V, float T, uint32_t word, float* margin,
                                                     float* smem,
                                        bool m_given = false, float m_max = 0.0f, const float* row_m = nullptr,
                                        const float* row_z = nullptr, unsigned long long* marks = nullptr) {
