@@ -1220,9 +1220,17 @@ static __device__ uint32_t sample_exact(const float* lg, int V, float T, uint32_
     return (uint32_t)amax;
   }
   const float inv = __fdiv_rn(1.0f, Z);
-  for (int row = threadIdx.x; row < (V + 31) / 32; row += kPT) smem[row] *= inv;  // rows of p, roughly
-  DEFER_CTA_SYNC();
   const SampleVals vp{lg, T, M, inv, true};
+  // rows of p, roughly (the sum's walk reused the row sums' space)
+  if (row_m) {
+    for (int row = threadIdx.x; row < (V + 31) / 32; row += kPT) {
+      const float z = ld_f(row_z + row);
+      smem[row] = z > 0.0f ? z * expf(ld_f(row_m + row) - M) * inv : 0.0f;
+    }
+    DEFER_CTA_SYNC();
+  } else {
+    row_sums(vp, V, smem);
+  }
   const float r = (float)(word >> 8) * (1.0f / 16777216.0f);
   int hit;
   float prev, at;
