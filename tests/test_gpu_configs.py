@@ -28,6 +28,7 @@ them in spawned worker processes as soon as their inputs exist.
 import json
 import multiprocessing as mp
 import os
+import tempfile
 from concurrent.futures import ProcessPoolExecutor
 
 import numpy as np
@@ -39,8 +40,9 @@ from tests.gpu_util import KV_TOL, LOGIT_TOL, kv_close, logits_close, model_file
 
 pytestmark = pytest.mark.gpu
 
-OUT = os.path.join(os.environ.get("GRAFT_REPO_ROOT", os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
-                   "gpurun_out")
+# where the per-configuration parity records (disagreement rates, worst
+# errors) are written: DEFER_PARITY_OUT, else a folder in the temp dir
+OUT = os.environ.get("DEFER_PARITY_OUT", os.path.join(tempfile.gettempdir(), "defer_parity"))
 
 
 def _tokens(vocab, n, seed):
